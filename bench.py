@@ -1,0 +1,353 @@
+"""Benchmark of the MoCE layer forward on B200.
+
+Workload (one step = one forward of the layer over one batch): the ResNet-50
+stage-4 MoCE layer, N=256 images per GPU, C_in=512, 7x7, E=2048 experts
+(2047 routed + residual), k=32, half-normal X, N(0,1) routing logits, the
+shared Linear(k,1) temperature gate with temp_min=0.1, temp_max=10.  Inputs
+are synthetic and seeded.  Each GPU processes its own batch (weak scaling,
+no collective on the data path).
+
+Metric: algorithmic HBM bytes (X read once + Y written once + parameters)
+per second, whole job; also reported as % of 8 TB/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--dtype bf16|fp32]
+    python bench.py --impl reference ...   # the CPU oracle port, host cores
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B, C, H, W, E, K = 256, 512, 7, 7, 2048, 32
+TMIN, TMAX, TAU = 0.1, 10.0, 1.0
+NOMINAL_HBM_GBS = 8000.0
+L2_BYTES = 126 * 1024 * 1024
+WORKLOAD = "ResNet-50 stage-4 MoCE layer forward: N=256/GPU C=512 7x7 E=2048 k=32"
+
+
+def algo_bytes(b, esize):
+    """X read once + Y written once + parameters (idx int32 + ln fp32 + mask + gate)."""
+    x = b * C * H * W * esize
+    y = b * E * H * W * esize
+    params = (E - 1) * K * 8 + C * 4 + K * 4 + 4
+    return x + y + params, x, y
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def mix_traffic():
+    """DRAM bytes per mix launch from the committed ncu summary, if any."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "mix_kernel_traffic.json")) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+class Clocks:
+    """nvidia-smi sampler running during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            for line in open(self.path):
+                f = [s.strip() for s in line.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    sm.append(float(f[1]))
+                    mx = max(mx, float(f[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, f[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+            os.unlink(self.path)
+        except Exception:
+            pass
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def make_inputs(dev, dtype, seed):
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    X = torch.randn(B, C, H, W, generator=g).abs()
+    L = torch.randn(E - 1, C, generator=torch.Generator().manual_seed(1))
+    gw = (torch.rand(1, K, generator=torch.Generator().manual_seed(2)) * 2 - 1) * (6.0 / (K + 1)) ** 0.5
+    gb = torch.zeros(1)
+    return X.to(dev, dtype), L.to(dev), gw.to(dev), gb.to(dev), X
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    from moce_thesis_b200 import MoCE, native
+    mc = native()
+    dtype = torch.bfloat16 if args.dtype == "bf16" else torch.float32
+    esize = 2 if dtype == torch.bfloat16 else 4
+    bytes_step, xb, yb = algo_bytes(B, esize)
+
+    # the layer with the workload's parameters; supports frozen (eval cache)
+    x0, L, gw, gb, Xcpu = make_inputs(dev, dtype, seed=1000 + rank)
+    layer = MoCE(in_channels=C, sampling_factor=1, k=K, temp_min=TMIN, temp_max=TMAX).to(dev)
+    layer.num_experts = E
+    layer.routing_logits = torch.nn.Parameter(L.clone())
+    with torch.no_grad():
+        layer.gate.weight.copy_(gw)
+        layer.gate.bias.copy_(gb)
+    layer.eval()
+    layer.build_eval_cache()
+    r = layer._route
+    gwf = layer.cached_gate_weight.detach().reshape(-1).float().contiguous()
+    gbf = layer.cached_gate_bias.detach().reshape(-1).float().contiguous()
+    ln = r.ln
+
+    # rotating input/output sets whose total exceeds L2 several times over
+    nsets = max(2, int(3 * L2_BYTES // (xb + yb)) + 1)
+    xs = [x0] + [(x0 * (1.0 + 0.001 * i)).contiguous() for i in range(1, nsets)]
+    ys = [torch.empty(B, E, H, W, device=dev, dtype=dtype) for _ in range(nsets)]
+    Ts = [torch.empty(B, E - 1, device=dev) for _ in range(nsets)]
+
+    def step(i):
+        x = xs[i % nsets]
+        _, T = mc.gate_temperature(x, r.idx, gwf, gbf, layer.cached_temp_min_tau, layer.cached_temp_range_tau)
+        mc.mix(x, r.idx, ln, T, r.mask, ys[i % nsets])
+        return T
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+
+    st = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ev0.record(st)
+        for i in range(args.steps):
+            step(i)
+        ev1.record(st)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    value = world * bytes_step * args.steps / (ms * 1e-3) / 1e9
+
+    # dominant kernel (pass 2, the mix) timed alone on the same stream
+    Tfix = [step(i) for i in range(nsets)]
+    torch.cuda.synchronize()
+    reps = max(args.steps, 20)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(reps):
+        mc.mix(xs[i % nsets], r.idx, ln, Tfix[i % nsets], r.mask, ys[i % nsets])
+    e1.record(st)
+    torch.cuda.synchronize()
+    mix_ms = e0.elapsed_time(e1) / reps
+    mix_bytes = xb + yb + (E - 1) * K * 8 + C * 4 + B * (E - 1) * 4
+    e0.record(st)
+    for i in range(reps):
+        mc.gate_temperature(xs[i % nsets], r.idx, gwf, gbf, layer.cached_temp_min_tau, layer.cached_temp_range_tau)
+    e1.record(st)
+    torch.cuda.synchronize()
+    gate_ms = e0.elapsed_time(e1) / reps
+
+    # end to end through the public API: pinned host X -> layer -> host Y
+    xh = x0.cpu().pin_memory()
+    yh = torch.empty(B, E, H, W, dtype=dtype).pin_memory()
+    with torch.no_grad():
+        for _ in range(2):
+            yh.copy_(layer(xh.to(dev, non_blocking=True)), non_blocking=True)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0.record(st)
+        for _ in range(args.steps):
+            yh.copy_(layer(xh.to(dev, non_blocking=True)), non_blocking=True)
+        e1.record(st)
+        torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = world * bytes_step * args.steps / (e2e_ms * 1e-3) / 1e9
+
+    peak, peak_kind = peaks()
+    tr = mix_traffic()
+    traffic = None
+    if tr and tr.get("dtype") == args.dtype:
+        traffic = tr.get("dram_bytes_per_launch")
+    achieved = mix_bytes / (mix_ms * 1e-3) / 1e9
+    out = {
+        "metric": "MoCE fwd HBM GB/s (% of 8 TB/s)",
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "pct_of_8tbs": round(100.0 * value / world / NOMINAL_HBM_GBS, 2),
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": args.dtype,
+        "data": "synthetic (seeded half-normal X, N(0,1) logits)",
+        "config": {"workload": WORKLOAD, "global_batch": B * world, "C": C, "HW": H * W, "E": E, "k": K,
+                   "parallelism": f"batch-sharded x{world}, no data-path collective",
+                   "l2": f"{nsets} rotating X/Y sets ({nsets * (xb + yb) / 2**20:.0f} MiB > 126 MiB L2)"},
+        "kernels_ms": {"pass1_gate": round(gate_ms, 5), "pass2_mix": round(mix_ms, 5)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "kernel": "mix_kernel (pass 2)", "peak_kind": f"{peak_kind} copy bandwidth"},
+        "e2e": {"value": round(e2e, 3), "unit": "GB/s", "h2d_bytes_per_step": xb, "d2h_bytes_per_step": yb,
+                "api": "moce_thesis_b200.MoCE.forward_eval, pinned host X in, host Y out"},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(args.dtype, Xcpu, L.cpu(), gw.cpu(), gb.cpu())
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def cpu_baseline(dtype, X, L, gw, gb, sample=8):
+    """The numpy oracle on a bounded sample of the workload (host cores)."""
+    import numpy as np
+    from oracle import moce_oracle as O
+    esize = 2 if dtype == "bf16" else 4
+    Xs = X[:sample].numpy()
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        O.forward(Xs, L.numpy(), gw.numpy(), gb.numpy(), K, TMIN, TMAX, TAU, mode="eval", dtype=np.float32)
+        reps += 1
+        if time.perf_counter() - t0 > 5.0:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    nb, _, _ = algo_bytes(sample, esize)
+    return {"value": round(nb / dt / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{sample} of {B} images, {reps} forward(s), float32 numpy oracle, bytes counted at {dtype}",
+            "ms_per_sample_batch": round(dt * 1e3, 2)}
+
+
+def run_reference(args):
+    """Reference arm: the CPU oracle port of the reference layer on host cores."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+    torch.set_num_threads(os.cpu_count() or 1)
+    from oracle import moce_oracle as O
+    _, L, gw, gb, X = make_inputs("cpu", torch.float32, seed=1000)
+    esize = 2 if args.dtype == "bf16" else 4
+    sample = 4
+    Xs, Ln, gwn, gbn = X[:sample].numpy(), L.numpy(), gw.numpy(), gb.numpy()
+    for _ in range(args.warmup):
+        O.forward(Xs, Ln, gwn, gbn, K, TMIN, TMAX, TAU, mode="eval", dtype=np.float32)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.forward(Xs, Ln, gwn, gbn, K, TMIN, TMAX, TAU, mode="eval", dtype=np.float32)
+    dt = (time.perf_counter() - t0) / args.steps
+    nb, xb, yb = algo_bytes(sample, esize)
+    value = nb / dt / 1e9
+    out = {
+        "impl": "reference",
+        "metric": "MoCE fwd HBM GB/s (% of 8 TB/s)",
+        "value": round(value, 4), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": args.dtype, "data": "synthetic (seeded half-normal X, N(0,1) logits)",
+        "config": {"workload": WORKLOAD, "global_batch": B * world, "C": C, "HW": H * W, "E": E, "k": K},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+                         "sample": f"{sample} of {B} images per step, float32 numpy oracle"},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--dtype", choices=["bf16", "fp32"], default="bf16")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

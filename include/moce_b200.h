@@ -1,0 +1,161 @@
+/*
+ * moce_b200.h -- C ABI of the B200 (sm_100a) MoCE layer kernels.
+ *
+ * Plain pointers and sizes only: every tensor argument is a device pointer to
+ * a dense, contiguous array laid out as documented; no allocation happens
+ * inside any entry point (callers pass outputs and, where noted, a workspace
+ * sized by the matching *_workspace_bytes query).  Every call is asynchronous
+ * on `stream` (a cudaStream_t; NULL = legacy default stream) and returns a
+ * moce_status; moce_last_error() gives a message for the calling thread.
+ *
+ * Shapes: B batch, C input channels, HW = H*W spatial positions, E_r routed
+ * experts (the layer has E = E_r + 1 output channels, the last one is the
+ * residual expert), k supports per expert.  X is [B, C, HW]; Y is [B, E, HW].
+ *
+ * Reference interfaces replaced (Elianiluk/MoCE_thesis):
+ *   moce_fixed/moce_layer_cuda.cpp  -- pybind wrappers of the 7 entry points
+ *   moce_fixed/moce_kernel.cu       -- their CUDA implementations
+ *   MoCE.py                         -- the ATen parts of the layer (cache
+ *                                      build, pooling, gate, softmax)
+ */
+#ifndef MOCE_B200_H
+#define MOCE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  MOCE_OK = 0,
+  MOCE_ERR_INVALID = 1,      /* bad pointer, shape or dtype */
+  MOCE_ERR_UNSUPPORTED = 2,  /* shape outside the supported range */
+  MOCE_ERR_CUDA = 3,         /* a CUDA runtime call or launch failed */
+  MOCE_ERR_WORKSPACE = 4     /* workspace missing or too small */
+} moce_status;
+
+typedef enum { MOCE_F32 = 0, MOCE_BF16 = 1, MOCE_F16 = 2 } moce_dtype;
+
+/* Message for the last non-OK status returned on the calling thread. */
+const char* moce_last_error(void);
+
+/* Library version string. */
+const char* moce_version(void);
+
+/*
+ * Support selection, logit normalisation and coverage (the eval cache).
+ * Replaces MoCE.build_eval_cache (MoCE.py:85-109) and the per-step topk of
+ * MoCE.forward_train (MoCE.py:160-187).
+ *   logits  fp32 [E_r, C]      routing logits L
+ *   idx     int32 [E_r, k]     out: TopK(L_e, k), descending logit, ties by
+ *                              ascending channel (torch.topk order when the
+ *                              row has no ties)
+ *   ln      fp32 [E_r, k]      out: (sel - mean) / max(std_unbiased, 1)
+ *   mask    int32 [C]          out: 1 where no expert selects the channel
+ *   meta    int32 [2]          out: {number of uncovered channels, 0}
+ *   toff    int32 [C+1]        out (optional, NULL to skip): CSR offsets of
+ *   tslot   int32 [E_r*k]      the per-channel list of flat slots e*k+i with
+ *                              idx[e,i] == c, ascending (used by backward)
+ */
+int moce_route_build(const float* logits, int64_t E_r, int64_t C, int64_t k,
+                     int32_t* idx, float* ln, int32_t* mask, int32_t* meta,
+                     int32_t* toff, int32_t* tslot, void* stream);
+
+/*
+ * Global average pool: pooled[b,c] = mean_p X[b,c,p] (fp32 out).
+ * Replaces moce_pool (moce_layer_cuda.cpp:8-10, moce_kernel.cu:849-861).
+ * pooled has the dtype of X in the reference; here it is always fp32.
+ */
+int moce_pool(const void* x, int dtype, int64_t B, int64_t C, int64_t HW,
+              float* pooled, void* stream);
+
+/*
+ * Pass 1: global average pool fused with the shared Linear(k,1) temperature
+ * gate.  Replaces the ATen code of MoCE.forward_eval (MoCE.py:212-218) and
+ * MoCE.forward_train (MoCE.py:174-178):
+ *   z[b,c]  = mean_p X[b,c,p]                         (fp32 [B, C], out)
+ *   g       = gate_w . z[b, idx[e,:]] + gate_b[0]
+ *   T[b,e]  = max(tmin_tau + trange_tau * sigmoid(g), 1e-3)  (fp32 [B, E_r], out)
+ * with tmin_tau = temp_min * tau and trange_tau = (temp_max - temp_min) * tau.
+ * gate_w fp32 [k], gate_b fp32 [1] are device pointers.  If `pooled_in` is
+ * not NULL it is used as z (fp32 [B, C]) and X is not read (x may be NULL).
+ */
+int moce_gate_temperature(const void* x, int dtype, const float* pooled_in,
+                          int64_t B, int64_t C, int64_t HW, const int32_t* idx,
+                          int64_t E_r, int64_t k, const float* gate_w,
+                          const float* gate_b, float tmin_tau, float trange_tau,
+                          float* z, float* T, void* stream);
+
+/*
+ * Pass 2: per-expert softmax of ln[e,:] / T[b,e], the convex gather-mix of
+ * the k selected channels, and the residual expert (mean over channels with
+ * mask[c] == 1, or 0 when there are none).  Y has the dtype of X.
+ * Replaces MoCE.py:219-229 and fused_moce_forward_dynamic_temp's kernels
+ * (moce_kernel.cu:57-231).
+ */
+int moce_mix(const void* x, int dtype, int64_t B, int64_t C, int64_t HW,
+             const int32_t* idx, const float* ln, const float* T,
+             int64_t E_r, int64_t k, const int32_t* mask, void* y,
+             void* stream);
+
+/*
+ * Drop-in for fused_moce_forward_dynamic_temp(input, indices, weights,
+ * mask_int) (moce_layer_cuda.cpp:19-26, moce_kernel.cu:1079-1153): the mix
+ * with caller-computed per-sample weights fp32 [B, E_r, K].  `indices` is
+ * [E_r, K] int64 (index_bits = 64, as MoCE.py passes) or int32 (32).
+ */
+int moce_forward_dynamic_temp(const void* x, int dtype, const void* indices,
+                              int index_bits, const float* weights,
+                              const int32_t* mask, void* y, int64_t B,
+                              int64_t C, int64_t HW, int64_t E_r, int64_t K,
+                              void* stream);
+
+/*
+ * Drop-in for fused_moce_gate_route (moce_layer_cuda.cpp:36-45,
+ * moce_kernel.cu:396-485; pooled given) and fused_moce_gate_route_all
+ * (moce_layer_cuda.cpp:89-98, moce_kernel.cu:867-942; pooled == NULL, pool
+ * computed here).  logits_norm fp32 [E_r, K] is used as given; T is
+ * max((temp_min + (temp_max - temp_min) * sigmoid(g)) * tau, 1e-3).
+ * workspace: moce_gate_route_workspace_bytes(B, C, E_r) bytes, 256-aligned.
+ */
+size_t moce_gate_route_workspace_bytes(int64_t B, int64_t C, int64_t E_r);
+int moce_gate_route(const void* x, int dtype, const float* pooled,
+                    const void* indices, int index_bits,
+                    const float* logits_norm, const float* gate_w,
+                    const float* gate_b, const int32_t* mask, float temp_min,
+                    float temp_max, float tau, void* y, int64_t B, int64_t C,
+                    int64_t HW, int64_t E_r, int64_t K, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/*
+ * Backward of the layer (no reference kernel: the reference trains through
+ * autograd over MoCE.forward_train, MoCE.py:153-201).  Given dY [B, E, HW]
+ * (dtype of X), the forward's z and T, and the route cache (including the
+ * transposed lists), writes
+ *   dX      [B, C, HW]   dtype of X
+ *   dL      fp32 [E_r, C]  gradient of the routing logits through the
+ *                           selected-logit normalisation (zero off-support;
+ *                           the auxiliary-loss gradient is not included)
+ *   dgate_w fp32 [k], dgate_b fp32 [1]
+ * Reductions over the batch are deterministic (fixed order, no atomics).
+ * workspace: moce_backward_workspace_bytes(...) bytes.
+ */
+size_t moce_backward_workspace_bytes(int64_t B, int64_t C, int64_t HW,
+                                     int64_t E_r, int64_t k);
+int moce_backward(const void* x, const void* dy, int dtype, int64_t B,
+                  int64_t C, int64_t HW, const float* logits,
+                  const int32_t* idx, const float* ln, const int32_t* mask,
+                  const int32_t* meta, const int32_t* toff,
+                  const int32_t* tslot, int64_t E_r, int64_t k,
+                  const float* gate_w, const float* gate_b, float tmin_tau,
+                  float trange_tau, const float* z, const float* T, void* dx,
+                  float* dL, float* dgate_w, float* dgate_b, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOCE_B200_H */

@@ -1,0 +1,341 @@
+// Backward kernels of the MoCE layer on sm_100a.
+//
+// The reference has no backward kernel: it trains through autograd over
+// MoCE.forward_train (MoCE.py:153-201).  The gradients below are that graph's,
+// derived by hand (u = ln/T, a = softmax(u)):
+//   da[b,e,i] = sum_p dY[b,e,p] X[b,S_ei,p]
+//   du = a (da - sum_j a_j da_j);  dln_b = du / T;  dT = -sum_i du_i u_i / T
+//   dT passes the 1e-3 clamp only where the unclamped value >= 1e-3
+//   dg = dT * (tmax - tmin) * tau * sigmoid(g) (1 - sigmoid(g))
+//   dgate_w[i] = sum_{b,e} dg z[b,S_ei];  dgate_b = sum dg;  dz[b,S_ei] += dg w_i
+//   dX[b,c,p] = sum_{(e,i): S_ei = c} a dY[b,e,p] + mask[c]/n_u dY[b,E_r,p] + dz[b,c]/HW
+//   dL[e,S_e] = backward of ln = (sel - mean) / max(std, 1) applied to sum_b dln_b
+// Batch reductions run in a fixed order (no atomics), so results are
+// deterministic.
+#include "common.cuh"
+
+namespace moce {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+
+int bwd_chunks(int64_t B, int64_t E_r) {
+  // depends on shapes only, so the workspace size is device independent
+  const int64_t target = 1184;  // 8 CTAs x 148 SMs
+  int64_t nch = B >= target ? 1 : (target + B - 1) / B;
+  const int64_t max_ch = (E_r + kWarps - 1) / kWarps;
+  if (nch > max_ch) nch = max_ch;
+  return nch < 1 ? 1 : (int)nch;
+}
+
+struct BwdWs {
+  float* a;       // [B, E_r, k] softmax weights
+  float* dlnb;    // [B, E_r, k] per-sample d ln
+  float* dg;      // [B, E_r]
+  float* part_w;  // [B * nch, k]
+  float* part_b;  // [B * nch]
+  float* dln;     // [E_r, k]
+};
+
+size_t ws_layout(int64_t B, int64_t E_r, int64_t k, unsigned char* base, BwdWs* w) {
+  const int nch = bwd_chunks(B, E_r);
+  const size_t sz[6] = {(size_t)B * E_r * k * 4, (size_t)B * E_r * k * 4, (size_t)B * E_r * 4,
+                        (size_t)B * nch * k * 4, (size_t)B * nch * 4, (size_t)E_r * k * 4};
+  size_t off = 0;
+  float* ptr[6];
+  for (int i = 0; i < 6; ++i) {
+    ptr[i] = base ? reinterpret_cast<float*>(base + off) : nullptr;
+    off += align256(sz[i] ? sz[i] : 1);
+  }
+  if (w) *w = BwdWs{ptr[0], ptr[1], ptr[2], ptr[3], ptr[4], ptr[5]};
+  return off;
+}
+
+// grid (nch, B): warp per expert.  da by warp-reduced dot products over the
+// pixels, then the softmax / temperature / gate chain per (b, e).
+template <typename T>
+__global__ void __launch_bounds__(kThreads) bwd_route_kernel(
+    const T* __restrict__ x, const T* __restrict__ dy, int C, int HW, const int32_t* __restrict__ idx,
+    const float* __restrict__ ln, int E_r, int k, const float* __restrict__ gate_w,
+    const float* __restrict__ gate_b, float tmin_tau, float trange_tau, const float* __restrict__ z,
+    const float* __restrict__ Tb, BwdWs ws) {
+  extern __shared__ float s_mem[];
+  float* s_z = s_mem;                     // C
+  float* s_w = s_z + C;                   // k
+  float* s_pw = s_w + k;                  // kWarps * k
+  float* s_pb = s_pw + kWarps * k;        // kWarps
+  const int b = blockIdx.y, ch = blockIdx.x, nch = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int c = threadIdx.x; c < C; c += kThreads) s_z[c] = z[(size_t)b * C + c];
+  for (int i = threadIdx.x; i < k; i += kThreads) s_w[i] = gate_w[i];
+  for (int i = threadIdx.x; i < kWarps * k; i += kThreads) s_pw[i] = 0.0f;
+  if (threadIdx.x < kWarps) s_pb[threadIdx.x] = 0.0f;
+  __syncthreads();
+  const float bias = gate_b[0];
+  const int per = (E_r + nch - 1) / nch;
+  const int e0 = ch * per, e1 = min(E_r, e0 + per);
+  const int E = E_r + 1;
+  const T* xb = x + (size_t)b * C * HW;
+  for (int e = e0 + warp; e < e1; e += kWarps) {
+    const int32_t* ie = idx + (size_t)e * k;
+    const float* lne = ln + (size_t)e * k;
+    const size_t be = (size_t)b * E_r + e;
+    const float t = Tb[be];
+    float g = 0.0f;
+    for (int i = lane; i < k; i += 32) g += s_w[i] * s_z[ie[i]];
+    g = warp_sum(g) + bias;
+    float m = -INFINITY;
+    for (int i = lane; i < k; i += 32) m = nan_max(m, lne[i] / t);
+    m = warp_max(m);
+    float ssum = 0.0f;
+    for (int i = lane; i < k; i += 32) ssum += expf(lne[i] / t - m);
+    ssum = warp_sum(ssum);
+    const T* dye = dy + ((size_t)b * E + e) * HW;
+    float S = 0.0f;
+    for (int i0 = 0; i0 < k; i0 += 32) {
+      const int i = i0 + lane;
+      const int c_l = (i < k) ? ie[i] : 0;
+      const float a_l = (i < k) ? expf(lne[i] / t - m) / ssum : 0.0f;
+      float da_l = 0.0f;
+      const int n = min(32, k - i0);
+      for (int j = 0; j < n; ++j) {
+        const int c = __shfl_sync(kFull, c_l, j);
+        const T* xr = xb + (size_t)c * HW;
+        float part = 0.0f;
+        for (int p = lane; p < HW; p += 32) part += to_f(dye[p]) * to_f(xr[p]);
+        part = warp_sum(part);
+        if (lane == j) da_l = part;
+      }
+      if (i < k) {
+        ws.a[be * k + i] = a_l;
+        ws.dlnb[be * k + i] = da_l;   // holds da until the second sweep
+      }
+      S += a_l * da_l;
+    }
+    S = warp_sum(S);
+    float dTp = 0.0f;
+    for (int i0 = 0; i0 < k; i0 += 32) {
+      const int i = i0 + lane;
+      if (i < k) {
+        const float a_l = ws.a[be * k + i];
+        const float du = a_l * (ws.dlnb[be * k + i] - S);
+        ws.dlnb[be * k + i] = du / t;
+        dTp += du * (lne[i] / t);
+      }
+    }
+    float dT = -warp_sum(dTp) / t;
+    const float sig = 1.0f / (1.0f + expf(-g));
+    const float t_raw = tmin_tau + trange_tau * sig;
+    if (!(t_raw >= 1e-3f)) dT = 0.0f;
+    const float dg = dT * trange_tau * sig * (1.0f - sig);
+    if (lane == 0) {
+      ws.dg[be] = dg;
+      s_pb[warp] += dg;
+    }
+    for (int i = lane; i < k; i += 32) s_pw[warp * k + i] += dg * s_z[ie[i]];
+  }
+  __syncthreads();
+  const size_t q = (size_t)b * nch + ch;
+  for (int i = threadIdx.x; i < k; i += kThreads) {
+    float s = 0.0f;
+    for (int w = 0; w < kWarps; ++w) s += s_pw[w * k + i];
+    ws.part_w[q * k + i] = s;
+  }
+  if (threadIdx.x == 0) {
+    float s = 0.0f;
+    for (int w = 0; w < kWarps; ++w) s += s_pb[w];
+    ws.part_b[q] = s;
+  }
+}
+
+// grid (ceil(C / 8), B): warp per input channel c.  Gathers the transposed
+// list of c (every (e, i) with S_ei = c) against dY rows.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) bwd_dx_kernel(
+    const T* __restrict__ dy, int C, int HW, int E_r, int k, const int32_t* __restrict__ mask,
+    const int32_t* __restrict__ meta, const int32_t* __restrict__ toff, const int32_t* __restrict__ tslot,
+    const float* __restrict__ gate_w, BwdWs ws, T* __restrict__ dx) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x * kWarps + warp;
+  const int b = blockIdx.y;
+  if (c >= C) return;
+  const int s0 = toff[c], s1 = toff[c + 1];
+  const size_t bek = (size_t)b * E_r * k;
+  float dz = 0.0f;
+  for (int s = s0 + lane; s < s1; s += 32) {
+    const int slot = tslot[s];
+    dz += ws.dg[(size_t)b * E_r + slot / k] * gate_w[slot % k];
+  }
+  dz = warp_sum(dz);
+  const int n_u = meta[0];
+  const float rw = (mask[c] == 1 && n_u > 0) ? 1.0f / (float)n_u : 0.0f;
+  const float dz_hw = dz / (float)HW;
+  const int E = E_r + 1;
+  const T* dyb = dy + (size_t)b * E * HW;
+  T* dxr = dx + ((size_t)b * C + c) * HW;
+  for (int p0 = 0; p0 < HW; p0 += 32) {
+    const int p = p0 + lane;
+    float acc = 0.0f;
+    for (int sc = s0; sc < s1; sc += 32) {
+      const int s = sc + lane;
+      int e_l = 0;
+      float a_l = 0.0f;
+      if (s < s1) {
+        const int slot = tslot[s];
+        e_l = slot / k;
+        a_l = ws.a[bek + slot];
+      }
+      const int n = min(32, s1 - sc);
+      for (int j = 0; j < n; ++j) {
+        const int e = __shfl_sync(kFull, e_l, j);
+        const float a = __shfl_sync(kFull, a_l, j);
+        if (p < HW) acc += a * to_f(dyb[(size_t)e * HW + p]);
+      }
+    }
+    if (p < HW) {
+      if (rw != 0.0f) acc += rw * to_f(dyb[(size_t)E_r * HW + p]);
+      dxr[p] = from_f<T>(acc + dz_hw);
+    }
+  }
+}
+
+// grid ceil(E_r / 8): warp per expert.  Sums d ln over the batch in order,
+// then back-propagates the centring / std normalisation into dL[e, S_e].
+__global__ void __launch_bounds__(kThreads) bwd_logits_kernel(
+    const float* __restrict__ L, int C, int B, const int32_t* __restrict__ idx, int E_r, int k, BwdWs ws,
+    float* __restrict__ dL) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x * kWarps + warp;
+  if (e >= E_r) return;
+  const float* Le = L + (size_t)e * C;
+  const int32_t* ie = idx + (size_t)e * k;
+  float* dLe = dL + (size_t)e * C;
+  for (int c = lane; c < C; c += 32) dLe[c] = 0.0f;
+  double ssel = 0.0;
+  for (int i = lane; i < k; i += 32) {
+    float s = 0.0f;
+    for (int b = 0; b < B; ++b) s += ws.dlnb[((size_t)b * E_r + e) * k + i];
+    ws.dln[(size_t)e * k + i] = s;
+    ssel += (double)Le[ie[i]];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ssel += __shfl_xor_sync(kFull, ssel, o);
+  const double mean = ssel / (double)k;
+  double ss = 0.0, sdc = 0.0;
+  for (int i = lane; i < k; i += 32) {
+    const double cen = (double)Le[ie[i]] - mean;
+    ss += cen * cen;
+    sdc += (double)ws.dln[(size_t)e * k + i] * cen;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ss += __shfl_xor_sync(kFull, ss, o);
+    sdc += __shfl_xor_sync(kFull, sdc, o);
+  }
+  const double sd = (k > 1) ? sqrt(ss / (double)(k - 1)) : (double)NAN;
+  const double scale = (sd != sd) ? sd : (sd < 1.0 ? 1.0 : sd);
+  // d scale = -sum(dln * cen) / scale^2 ; flows into sel only where sd >= 1
+  const double g_sd = (sd >= 1.0) ? (-sdc / (scale * scale)) / ((double)(k - 1) * sd) : 0.0;
+  double sdcen = 0.0;
+  for (int i = lane; i < k; i += 32) {
+    const double cen = (double)Le[ie[i]] - mean;
+    sdcen += (double)ws.dln[(size_t)e * k + i] / scale + g_sd * cen;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sdcen += __shfl_xor_sync(kFull, sdcen, o);
+  const double mdc = sdcen / (double)k;
+  __syncwarp();
+  for (int i = lane; i < k; i += 32) {
+    const double cen = (double)Le[ie[i]] - mean;
+    const double dcen = (double)ws.dln[(size_t)e * k + i] / scale + g_sd * cen;
+    dLe[ie[i]] = (float)(dcen - mdc);
+  }
+}
+
+// Single CTA: fixed-order sum of the per-CTA gate partials.
+__global__ void bwd_gate_reduce_kernel(BwdWs ws, int nq, int k, float* __restrict__ dgw, float* __restrict__ dgb) {
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    float s = 0.0f;
+    for (int q = 0; q < nq; ++q) s += ws.part_w[(size_t)q * k + i];
+    dgw[i] = s;
+  }
+  if (threadIdx.x == 0) {
+    float s = 0.0f;
+    for (int q = 0; q < nq; ++q) s += ws.part_b[q];
+    dgb[0] = s;
+  }
+}
+
+int check_bwd_shapes(int64_t B, int64_t C, int64_t HW, int64_t E_r, int64_t k) {
+  MOCE_REQUIRE(B >= 0 && C >= 1 && HW >= 1 && E_r >= 1 && k >= 1 && k <= C, MOCE_ERR_INVALID,
+               "moce_backward: invalid shape");
+  MOCE_REQUIRE(B < 65536 && C * HW < (int64_t)1 << 31 && (E_r + 1) * HW < (int64_t)1 << 31 &&
+                   B * E_r * k < (int64_t)1 << 40 && E_r * k < (int64_t)1 << 31 && k <= 4096 && C <= 32768,
+               MOCE_ERR_UNSUPPORTED, "moce_backward: shape too large");
+  return MOCE_OK;
+}
+
+}  // namespace
+}  // namespace moce
+
+using namespace moce;
+
+extern "C" size_t moce_backward_workspace_bytes(int64_t B, int64_t C, int64_t HW, int64_t E_r, int64_t k) {
+  (void)C;
+  (void)HW;
+  return ws_layout(B, E_r, k, nullptr, nullptr);
+}
+
+extern "C" int moce_backward(const void* x, const void* dy, int dtype, int64_t B, int64_t C, int64_t HW,
+                             const float* logits, const int32_t* idx, const float* ln, const int32_t* mask,
+                             const int32_t* meta, const int32_t* toff, const int32_t* tslot, int64_t E_r,
+                             int64_t k, const float* gate_w, const float* gate_b, float tmin_tau,
+                             float trange_tau, const float* z, const float* T, void* dx, float* dL,
+                             float* dgate_w, float* dgate_b, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  MOCE_REQUIRE(x && dy && logits && idx && ln && mask && meta && toff && tslot && gate_w && gate_b && z && T &&
+                   dx && dL && dgate_w && dgate_b,
+               MOCE_ERR_INVALID, "moce_backward: null pointer argument");
+  MOCE_REQUIRE(dtype_ok(dtype), MOCE_ERR_INVALID, "moce_backward: unknown dtype %d", dtype);
+  int rc = check_bwd_shapes(B, C, HW, E_r, k);
+  if (rc) return rc;
+  const size_t need = moce_backward_workspace_bytes(B, C, HW, E_r, k);
+  MOCE_REQUIRE(workspace && workspace_bytes >= need && ((uintptr_t)workspace & 255) == 0, MOCE_ERR_WORKSPACE,
+               "moce_backward: workspace of %zu bytes (256-aligned) required", need);
+  cudaStream_t st = (cudaStream_t)stream;
+  BwdWs ws;
+  ws_layout(B, E_r, k, static_cast<unsigned char*>(workspace), &ws);
+  const int nch = bwd_chunks(B, E_r);
+  if (B == 0) {
+    if (cudaMemsetAsync(dL, 0, (size_t)E_r * C * 4, st) != cudaSuccess ||
+        cudaMemsetAsync(dgate_w, 0, (size_t)k * 4, st) != cudaSuccess ||
+        cudaMemsetAsync(dgate_b, 0, 4, st) != cudaSuccess)
+      return set_error(MOCE_ERR_CUDA, "moce_backward: memset failed");
+    return MOCE_OK;
+  }
+  rc = dispatch_dtype(dtype, [&](auto tag) {
+    using Tt = decltype(tag);
+    const size_t smem = (size_t)(C + k + kWarps * k + kWarps) * 4;
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(bwd_route_kernel<Tt>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+      return set_error(MOCE_ERR_UNSUPPORTED, "moce_backward: route smem %zu", smem);
+    bwd_route_kernel<Tt><<<dim3(nch, (unsigned)B), kThreads, smem, st>>>(
+        static_cast<const Tt*>(x), static_cast<const Tt*>(dy), (int)C, (int)HW, idx, ln, (int)E_r, (int)k,
+        gate_w, gate_b, tmin_tau, trange_tau, z, T, ws);
+    int r = check_launch("moce_backward/route");
+    if (r) return r;
+    bwd_dx_kernel<Tt><<<dim3((unsigned)((C + kWarps - 1) / kWarps), (unsigned)B), kThreads, 0, st>>>(
+        static_cast<const Tt*>(dy), (int)C, (int)HW, (int)E_r, (int)k, mask, meta, toff, tslot, gate_w, ws,
+        static_cast<Tt*>(dx));
+    return check_launch("moce_backward/dx");
+  });
+  if (rc) return rc;
+  bwd_logits_kernel<<<(unsigned)((E_r + kWarps - 1) / kWarps), kThreads, 0, st>>>(logits, (int)C, (int)B, idx,
+                                                                                  (int)E_r, (int)k, ws, dL);
+  rc = check_launch("moce_backward/logits");
+  if (rc) return rc;
+  bwd_gate_reduce_kernel<<<1, 256, 0, st>>>(ws, (int)(B * nch), (int)k, dgate_w, dgate_b);
+  return check_launch("moce_backward/gate");
+}

@@ -1,0 +1,384 @@
+// PyTorch binding of the MoCE C ABI, importable as `moce_fixed.moce_cuda`.
+//
+// Mirrors the reference binding (moce_fixed/moce_layer_cuda.cpp:117-138):
+// the same seven functions with the same arguments and return lists, so the
+// reference MoCE.py (`import moce_fixed.moce_cuda`, MoCE.py:7, call at
+// MoCE.py:224) runs on these kernels unchanged.  Differences, all supersets:
+//   * kernels launch on the current CUDA stream (the reference uses the
+//     legacy default stream, moce_kernel.cu:1116);
+//   * input may be float32, bfloat16 or float16 (the reference accepts
+//     float32 only); indices may be int64 (as MoCE.py passes) or int32;
+//   * K is not limited to 64 (moce_kernel.cu:424 and others).
+// Additional functions expose the native pipeline (route build, pass 1,
+// pass 2, backward) used by moce_thesis_b200.MoCE.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <vector>
+
+#include "../../include/moce_b200.h"
+
+namespace {
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be CUDA")
+#define CHECK_CONTIGUOUS(x) TORCH_CHECK((x).is_contiguous(), #x " must be contiguous")
+#define CHECK_INPUT(x) \
+  CHECK_CUDA(x);       \
+  CHECK_CONTIGUOUS(x)
+
+void ok(int rc) { TORCH_CHECK(rc == MOCE_OK, "moce_b200: ", moce_last_error()); }
+
+int dtype_of(const torch::Tensor& t) {
+  switch (t.scalar_type()) {
+    case torch::kFloat32: return MOCE_F32;
+    case torch::kBFloat16: return MOCE_BF16;
+    case torch::kFloat16: return MOCE_F16;
+    default: TORCH_CHECK(false, "input must be float32, bfloat16 or float16");
+  }
+  return -1;
+}
+
+int index_bits(const torch::Tensor& t) {
+  TORCH_CHECK(t.scalar_type() == torch::kInt64 || t.scalar_type() == torch::kInt32,
+              "indices must be int64 or int32");
+  return t.scalar_type() == torch::kInt64 ? 64 : 32;
+}
+
+void* cur_stream() { return (void*)at::cuda::getCurrentCUDAStream().stream(); }
+
+struct Dims {
+  int64_t B, C, H, W, HW, E_r, K;
+};
+
+Dims dims(const torch::Tensor& input, const torch::Tensor& indices) {
+  TORCH_CHECK(input.dim() == 4, "input must be (B, C, H, W)");
+  TORCH_CHECK(indices.dim() == 2, "indices must be (E_routed, K)");
+  Dims d;
+  d.B = input.size(0);
+  d.C = input.size(1);
+  d.H = input.size(2);
+  d.W = input.size(3);
+  d.HW = d.H * d.W;
+  d.E_r = indices.size(0);
+  d.K = indices.size(1);
+  return d;
+}
+
+torch::Tensor f32_opts_like(const torch::Tensor& t, at::IntArrayRef shape) {
+  return torch::empty(shape, t.options().dtype(torch::kFloat32));
+}
+
+// Events on the current stream around a callable; returns elapsed ms.
+template <typename F>
+float timed(F&& f) {
+  cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
+  cudaEvent_t a, b;
+  cudaEventCreate(&a);
+  cudaEventCreate(&b);
+  cudaEventRecord(a, st);
+  f();
+  cudaEventRecord(b, st);
+  cudaEventSynchronize(b);
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, a, b);
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  return ms;
+}
+
+// ------------------------------------------------------- reference surface
+
+std::vector<torch::Tensor> py_moce_pool(torch::Tensor input) {
+  CHECK_INPUT(input);
+  TORCH_CHECK(input.dim() == 4, "input must be (B, C, H, W)");
+  const c10::cuda::CUDAGuard guard(input.device());
+  const int64_t B = input.size(0), C = input.size(1), HW = input.size(2) * input.size(3);
+  auto pooled = f32_opts_like(input, {B, C});
+  ok(::moce_pool(input.data_ptr(), dtype_of(input), B, C, HW, pooled.data_ptr<float>(), cur_stream()));
+  // the reference returns pooled in the input dtype (moce_kernel.cu:853)
+  return {input.scalar_type() == torch::kFloat32 ? pooled : pooled.to(input.scalar_type())};
+}
+
+std::vector<torch::Tensor> fused_moce_forward_dynamic_temp(torch::Tensor input, torch::Tensor indices,
+                                                           torch::Tensor weights, torch::Tensor mask_int) {
+  CHECK_INPUT(input);
+  CHECK_INPUT(indices);
+  CHECK_INPUT(weights);
+  CHECK_INPUT(mask_int);
+  TORCH_CHECK(weights.scalar_type() == torch::kFloat32, "weights must be float32");
+  TORCH_CHECK(mask_int.scalar_type() == torch::kInt32, "mask_int must be int32");
+  const c10::cuda::CUDAGuard guard(input.device());
+  Dims d = dims(input, indices);
+  TORCH_CHECK(weights.dim() == 3 && weights.size(0) == d.B && weights.size(1) == d.E_r && weights.size(2) == d.K,
+              "weights must be (B, E_routed, K)");
+  TORCH_CHECK(mask_int.numel() == d.C, "mask_int must have C entries");
+  auto out = torch::empty({d.B, d.E_r + 1, d.H, d.W}, input.options());
+  ok(moce_forward_dynamic_temp(input.data_ptr(), dtype_of(input), indices.data_ptr(), index_bits(indices),
+                               weights.data_ptr<float>(), mask_int.data_ptr<int32_t>(), out.data_ptr(), d.B, d.C,
+                               d.HW, d.E_r, d.K, cur_stream()));
+  return {out};
+}
+
+void check_gate_route_args(const torch::Tensor& input, const torch::Tensor& indices, const torch::Tensor& logits_norm,
+                           const torch::Tensor& gate_weight, const torch::Tensor& gate_bias,
+                           const torch::Tensor& mask_int, const Dims& d) {
+  CHECK_INPUT(input);
+  CHECK_INPUT(indices);
+  CHECK_INPUT(logits_norm);
+  CHECK_INPUT(gate_weight);
+  CHECK_INPUT(gate_bias);
+  CHECK_INPUT(mask_int);
+  TORCH_CHECK(logits_norm.scalar_type() == torch::kFloat32, "logits_norm must be float32");
+  TORCH_CHECK(gate_weight.scalar_type() == torch::kFloat32, "gate_weight must be float32");
+  TORCH_CHECK(gate_bias.scalar_type() == torch::kFloat32, "gate_bias must be float32");
+  TORCH_CHECK(mask_int.scalar_type() == torch::kInt32, "mask_int must be int32");
+  TORCH_CHECK(logits_norm.numel() == d.E_r * d.K, "logits_norm must be (E_routed, K)");
+  TORCH_CHECK(gate_weight.numel() == d.K, "gate_weight must have K entries");
+  TORCH_CHECK(gate_bias.numel() >= 1, "gate_bias must have one entry");
+  TORCH_CHECK(mask_int.numel() == d.C, "mask_int must have C entries");
+}
+
+torch::Tensor gate_route_impl(torch::Tensor input, const torch::Tensor* pooled, torch::Tensor indices,
+                              torch::Tensor logits_norm, torch::Tensor gate_weight, torch::Tensor gate_bias,
+                              torch::Tensor mask_int, double temp_min, double temp_max, double tau) {
+  Dims d = dims(input, indices);
+  check_gate_route_args(input, indices, logits_norm, gate_weight, gate_bias, mask_int, d);
+  const float* pooled_ptr = nullptr;
+  torch::Tensor pooled_f32;
+  if (pooled) {
+    CHECK_INPUT(*pooled);
+    TORCH_CHECK(pooled->numel() == d.B * d.C, "pooled must be (B, C)");
+    pooled_f32 = pooled->scalar_type() == torch::kFloat32 ? *pooled : pooled->to(torch::kFloat32);
+    pooled_ptr = pooled_f32.data_ptr<float>();
+  }
+  auto out = torch::empty({d.B, d.E_r + 1, d.H, d.W}, input.options());
+  const size_t wsb = moce_gate_route_workspace_bytes(d.B, d.C, d.E_r);
+  auto ws = torch::empty({(int64_t)wsb + 256}, input.options().dtype(torch::kUInt8));
+  void* wsp = (void*)(((uintptr_t)ws.data_ptr() + 255) & ~(uintptr_t)255);
+  ok(moce_gate_route(input.data_ptr(), dtype_of(input), pooled_ptr, indices.data_ptr(), index_bits(indices),
+                     logits_norm.data_ptr<float>(), gate_weight.data_ptr<float>(), gate_bias.data_ptr<float>(),
+                     mask_int.data_ptr<int32_t>(), (float)temp_min, (float)temp_max, (float)tau, out.data_ptr(),
+                     d.B, d.C, d.HW, d.E_r, d.K, wsp, wsb, cur_stream()));
+  return out;
+}
+
+std::vector<torch::Tensor> fused_moce_gate_route(torch::Tensor input, torch::Tensor pooled, torch::Tensor indices,
+                                                 torch::Tensor logits_norm, torch::Tensor gate_weight,
+                                                 torch::Tensor gate_bias, torch::Tensor mask_int, double temp_min,
+                                                 double temp_max, double tau) {
+  const c10::cuda::CUDAGuard guard(input.device());
+  return {gate_route_impl(input, &pooled, indices, logits_norm, gate_weight, gate_bias, mask_int, temp_min,
+                          temp_max, tau)};
+}
+
+std::vector<torch::Tensor> fused_moce_gate_route_all(torch::Tensor input, torch::Tensor indices,
+                                                     torch::Tensor logits_norm, torch::Tensor gate_weight,
+                                                     torch::Tensor gate_bias, torch::Tensor mask_int, double temp_min,
+                                                     double temp_max, double tau) {
+  const c10::cuda::CUDAGuard guard(input.device());
+  return {gate_route_impl(input, nullptr, indices, logits_norm, gate_weight, gate_bias, mask_int, temp_min, temp_max,
+                          tau)};
+}
+
+// Timed variants.  The reference reports separate routed / residual kernel
+// times and clock64 sections inside its routed kernel (moce_kernel.cu:493-579,
+// 759-843, 951-1063).  Here the pipeline is two fused passes, timed with CUDA
+// events on the current stream:
+//   kernel_times (2): [pass 1 (pool + gate + temperature) ms, pass 2 (softmax + mix + residual) ms]
+//   kernel_times (3): [pass 1 ms, pass 2 ms, 0 (residual is fused into pass 2)]
+//   section_us  (4): [pass 1 us, 0 (temperature fused into pass 1), 0 (softmax fused into pass 2), pass 2 us]
+struct TwoPass {
+  torch::Tensor out;
+  float ms1, ms2;
+};
+
+TwoPass gate_route_two_pass(torch::Tensor input, const torch::Tensor* pooled, torch::Tensor indices,
+                            torch::Tensor logits_norm, torch::Tensor gate_weight, torch::Tensor gate_bias,
+                            torch::Tensor mask_int, double temp_min, double temp_max, double tau) {
+  Dims d = dims(input, indices);
+  check_gate_route_args(input, indices, logits_norm, gate_weight, gate_bias, mask_int, d);
+  torch::Tensor idx32 = indices.scalar_type() == torch::kInt32 ? indices : indices.to(torch::kInt32);
+  torch::Tensor pooled_f32;
+  const float* pooled_ptr = nullptr;
+  if (pooled) {
+    CHECK_INPUT(*pooled);
+    TORCH_CHECK(pooled->numel() == d.B * d.C, "pooled must be (B, C)");
+    pooled_f32 = pooled->scalar_type() == torch::kFloat32 ? *pooled : pooled->to(torch::kFloat32);
+    pooled_ptr = pooled_f32.data_ptr<float>();
+  }
+  auto out = torch::empty({d.B, d.E_r + 1, d.H, d.W}, input.options());
+  auto T = f32_opts_like(input, {d.B, d.E_r});
+  auto z = f32_opts_like(input, {d.B, d.C});
+  TwoPass r;
+  r.ms1 = timed([&] {
+    ok(moce_gate_temperature(input.data_ptr(), dtype_of(input), pooled_ptr, d.B, d.C, d.HW,
+                             idx32.data_ptr<int32_t>(), d.E_r, d.K, gate_weight.data_ptr<float>(),
+                             gate_bias.data_ptr<float>(), (float)(temp_min * tau), (float)((temp_max - temp_min) * tau),
+                             pooled ? nullptr : z.data_ptr<float>(), T.data_ptr<float>(), cur_stream()));
+  });
+  r.ms2 = timed([&] {
+    ok(moce_mix(input.data_ptr(), dtype_of(input), d.B, d.C, d.HW, idx32.data_ptr<int32_t>(),
+                logits_norm.data_ptr<float>(), T.data_ptr<float>(), d.E_r, d.K, mask_int.data_ptr<int32_t>(),
+                out.data_ptr(), cur_stream()));
+  });
+  r.out = out;
+  return r;
+}
+
+std::vector<torch::Tensor> fused_moce_gate_route_timed(torch::Tensor input, torch::Tensor pooled,
+                                                       torch::Tensor indices, torch::Tensor logits_norm,
+                                                       torch::Tensor gate_weight, torch::Tensor gate_bias,
+                                                       torch::Tensor mask_int, double temp_min, double temp_max,
+                                                       double tau) {
+  const c10::cuda::CUDAGuard guard(input.device());
+  auto r = gate_route_two_pass(input, &pooled, indices, logits_norm, gate_weight, gate_bias, mask_int, temp_min,
+                               temp_max, tau);
+  return {r.out, torch::tensor({r.ms1, r.ms2})};
+}
+
+std::vector<torch::Tensor> fused_moce_gate_route_section_timed(torch::Tensor input, torch::Tensor pooled,
+                                                               torch::Tensor indices, torch::Tensor logits_norm,
+                                                               torch::Tensor gate_weight, torch::Tensor gate_bias,
+                                                               torch::Tensor mask_int, double temp_min,
+                                                               double temp_max, double tau) {
+  const c10::cuda::CUDAGuard guard(input.device());
+  auto r = gate_route_two_pass(input, &pooled, indices, logits_norm, gate_weight, gate_bias, mask_int, temp_min,
+                               temp_max, tau);
+  return {r.out, torch::tensor({r.ms1 * 1000.f, 0.f, 0.f, r.ms2 * 1000.f})};
+}
+
+std::vector<torch::Tensor> fused_moce_gate_route_all_timed(torch::Tensor input, torch::Tensor indices,
+                                                           torch::Tensor logits_norm, torch::Tensor gate_weight,
+                                                           torch::Tensor gate_bias, torch::Tensor mask_int,
+                                                           double temp_min, double temp_max, double tau) {
+  const c10::cuda::CUDAGuard guard(input.device());
+  auto r = gate_route_two_pass(input, nullptr, indices, logits_norm, gate_weight, gate_bias, mask_int, temp_min,
+                               temp_max, tau);
+  return {r.out, torch::tensor({r.ms1, r.ms2, 0.f}), torch::tensor({r.ms1 * 1000.f, 0.f, 0.f, r.ms2 * 1000.f})};
+}
+
+// ------------------------------------------------------- native pipeline
+
+std::vector<torch::Tensor> route_build(torch::Tensor logits, int64_t k, bool transposed) {
+  CHECK_INPUT(logits);
+  TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.dim() == 2, "logits must be float32 (E_r, C)");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  const int64_t E_r = logits.size(0), C = logits.size(1);
+  auto i32 = logits.options().dtype(torch::kInt32);
+  auto idx = torch::empty({E_r, k}, i32);
+  auto ln = torch::empty({E_r, k}, logits.options());
+  auto mask = torch::empty({C}, i32);
+  auto meta = torch::empty({2}, i32);
+  torch::Tensor toff, tslot;
+  if (transposed) {
+    toff = torch::empty({C + 1}, i32);
+    tslot = torch::empty({E_r * k}, i32);
+  } else {
+    toff = torch::empty({0}, i32);
+    tslot = torch::empty({0}, i32);
+  }
+  ok(moce_route_build(logits.data_ptr<float>(), E_r, C, k, idx.data_ptr<int32_t>(), ln.data_ptr<float>(),
+                      mask.data_ptr<int32_t>(), meta.data_ptr<int32_t>(),
+                      transposed ? toff.data_ptr<int32_t>() : nullptr, transposed ? tslot.data_ptr<int32_t>() : nullptr,
+                      cur_stream()));
+  return {idx, ln, mask, meta, toff, tslot};
+}
+
+std::vector<torch::Tensor> gate_temperature(torch::Tensor x, torch::Tensor idx, torch::Tensor gate_w,
+                                            torch::Tensor gate_b, double tmin_tau, double trange_tau) {
+  CHECK_INPUT(x);
+  CHECK_INPUT(idx);
+  CHECK_INPUT(gate_w);
+  CHECK_INPUT(gate_b);
+  TORCH_CHECK(idx.scalar_type() == torch::kInt32, "idx must be int32");
+  TORCH_CHECK(gate_w.scalar_type() == torch::kFloat32 && gate_b.scalar_type() == torch::kFloat32,
+              "gate parameters must be float32");
+  const c10::cuda::CUDAGuard guard(x.device());
+  Dims d = dims(x, idx);
+  TORCH_CHECK(gate_w.numel() == d.K && gate_b.numel() >= 1, "gate shape mismatch");
+  auto z = f32_opts_like(x, {d.B, d.C});
+  auto T = f32_opts_like(x, {d.B, d.E_r});
+  ok(moce_gate_temperature(x.data_ptr(), dtype_of(x), nullptr, d.B, d.C, d.HW, idx.data_ptr<int32_t>(), d.E_r, d.K,
+                           gate_w.data_ptr<float>(), gate_b.data_ptr<float>(), (float)tmin_tau, (float)trange_tau,
+                           z.data_ptr<float>(), T.data_ptr<float>(), cur_stream()));
+  return {z, T};
+}
+
+torch::Tensor mix(torch::Tensor x, torch::Tensor idx, torch::Tensor ln, torch::Tensor T, torch::Tensor mask,
+                  c10::optional<torch::Tensor> out_opt) {
+  CHECK_INPUT(x);
+  CHECK_INPUT(idx);
+  CHECK_INPUT(ln);
+  CHECK_INPUT(T);
+  CHECK_INPUT(mask);
+  TORCH_CHECK(idx.scalar_type() == torch::kInt32 && mask.scalar_type() == torch::kInt32, "idx/mask must be int32");
+  TORCH_CHECK(ln.scalar_type() == torch::kFloat32 && T.scalar_type() == torch::kFloat32, "ln/T must be float32");
+  const c10::cuda::CUDAGuard guard(x.device());
+  Dims d = dims(x, idx);
+  TORCH_CHECK(ln.numel() == d.E_r * d.K && T.numel() == d.B * d.E_r && mask.numel() == d.C, "shape mismatch");
+  torch::Tensor out;
+  if (out_opt.has_value()) {
+    out = *out_opt;
+    CHECK_INPUT(out);
+    TORCH_CHECK(out.scalar_type() == x.scalar_type() && out.numel() == d.B * (d.E_r + 1) * d.HW, "out mismatch");
+  } else {
+    out = torch::empty({d.B, d.E_r + 1, d.H, d.W}, x.options());
+  }
+  ok(moce_mix(x.data_ptr(), dtype_of(x), d.B, d.C, d.HW, idx.data_ptr<int32_t>(), ln.data_ptr<float>(),
+              T.data_ptr<float>(), d.E_r, d.K, mask.data_ptr<int32_t>(), out.data_ptr(), cur_stream()));
+  return out;
+}
+
+std::vector<torch::Tensor> backward(torch::Tensor x, torch::Tensor dy, torch::Tensor logits, torch::Tensor idx,
+                                    torch::Tensor ln, torch::Tensor mask, torch::Tensor meta, torch::Tensor toff,
+                                    torch::Tensor tslot, torch::Tensor gate_w, torch::Tensor gate_b, double tmin_tau,
+                                    double trange_tau, torch::Tensor z, torch::Tensor T) {
+  for (auto* t : {&x, &dy, &logits, &idx, &ln, &mask, &meta, &toff, &tslot, &gate_w, &gate_b, &z, &T}) {
+    CHECK_INPUT(*t);
+  }
+  TORCH_CHECK(dy.scalar_type() == x.scalar_type(), "dy must have the dtype of x");
+  const c10::cuda::CUDAGuard guard(x.device());
+  Dims d = dims(x, idx);
+  TORCH_CHECK(dy.numel() == d.B * (d.E_r + 1) * d.HW, "dy must be (B, E, H, W)");
+  TORCH_CHECK(toff.numel() == d.C + 1 && tslot.numel() == d.E_r * d.K, "transposed lists missing");
+  auto dx = torch::empty_like(x);
+  auto dL = f32_opts_like(x, {d.E_r, d.C});
+  auto dgw = f32_opts_like(x, {1, d.K});
+  auto dgb = f32_opts_like(x, {1});
+  const size_t wsb = moce_backward_workspace_bytes(d.B, d.C, d.HW, d.E_r, d.K);
+  auto ws = torch::empty({(int64_t)wsb + 256}, x.options().dtype(torch::kUInt8));
+  void* wsp = (void*)(((uintptr_t)ws.data_ptr() + 255) & ~(uintptr_t)255);
+  ok(moce_backward(x.data_ptr(), dy.data_ptr(), dtype_of(x), d.B, d.C, d.HW, logits.data_ptr<float>(),
+                   idx.data_ptr<int32_t>(), ln.data_ptr<float>(), mask.data_ptr<int32_t>(), meta.data_ptr<int32_t>(),
+                   toff.data_ptr<int32_t>(), tslot.data_ptr<int32_t>(), d.E_r, d.K, gate_w.data_ptr<float>(),
+                   gate_b.data_ptr<float>(), (float)tmin_tau, (float)trange_tau, z.data_ptr<float>(),
+                   T.data_ptr<float>(), dx.data_ptr(), dL.data_ptr<float>(), dgw.data_ptr<float>(),
+                   dgb.data_ptr<float>(), wsp, wsb, cur_stream()));
+  return {dx, dL, dgw, dgb};
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  // reference surface (moce_layer_cuda.cpp:117-138)
+  m.def("moce_pool", &py_moce_pool, "Channel average pool (B,C,H,W) -> [(B,C)]");
+  m.def("fused_moce_forward_dynamic_temp", &fused_moce_forward_dynamic_temp,
+        "Weighted sum + residual with caller weights (B,E_routed,K); returns [out]");
+  m.def("fused_moce_gate_route", &fused_moce_gate_route, "Pooled given: gate+temperature+softmax+mix; returns [out]");
+  m.def("fused_moce_gate_route_timed", &fused_moce_gate_route_timed,
+        "Timed fused_moce_gate_route; returns [out, kernel_ms[pass1, pass2]]");
+  m.def("fused_moce_gate_route_section_timed", &fused_moce_gate_route_section_timed,
+        "Section-timed fused_moce_gate_route; returns [out, section_us[pass1, 0, 0, pass2]]");
+  m.def("fused_moce_gate_route_all", &fused_moce_gate_route_all, "Pool+gate+temperature+softmax+mix; returns [out]");
+  m.def("fused_moce_gate_route_all_timed", &fused_moce_gate_route_all_timed,
+        "Timed fused_moce_gate_route_all; returns [out, kernel_ms[pass1, pass2, 0], section_us]");
+  // native pipeline
+  m.def("route_build", &route_build, "Top-k supports, normalised logits, mask, meta, transposed lists",
+        py::arg("logits"), py::arg("k"), py::arg("transposed") = true);
+  m.def("gate_temperature", &gate_temperature, "Pass 1: (z, T)");
+  m.def("mix", &mix, "Pass 2: softmax + gather-mix + residual", py::arg("x"), py::arg("idx"), py::arg("ln"),
+        py::arg("T"), py::arg("mask"), py::arg("out") = py::none());
+  m.def("backward", &backward, "Layer backward: (dx, dL, dgate_w, dgate_b)");
+  m.def("version", []() { return std::string(moce_version()); });
+}

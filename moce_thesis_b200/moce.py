@@ -1,0 +1,194 @@
+"""The MoCE layer on the sm_100a kernels.
+
+``MoCE`` keeps the public surface of the reference module
+(Elianiluk/MoCE_thesis ``MoCE.py:11-230``): constructor arguments,
+``routing_logits`` and ``gate`` parameters, the ``aux_loss`` attribute,
+``build_eval_cache`` / ``clear_eval_cache``, ``forward_train`` /
+``forward_eval``, the ``cached_*`` attributes and the state_dict keys.  What
+changes is where the work runs:
+
+* eval (``MoCE.py:204-230``): pass 1 (pool + gate + temperature) and pass 2
+  (softmax + gather-mix + residual) are two native kernels; bf16/fp16 inputs
+  are read and written natively (the reference upcasts to fp32, then casts
+  back).
+* train (``MoCE.py:153-201``): the same two passes under
+  ``MoCEFunction``, whose backward is a native kernel chain (the reference
+  trains through autograd over multi-GB gathered tensors).  Supports are
+  re-selected every step, as the reference does (``MoCE.py:160``).
+
+The auxiliary/coverage loss (``MoCE.py:118-151``) depends on the routing
+logits only and stays a PyTorch expression.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+
+def native():
+    """The compiled binding ``moce_fixed.moce_cuda`` (raises if unbuilt)."""
+    import moce_fixed.moce_cuda as m
+    return m
+
+
+class _Route:
+    """Native route cache of one logits tensor: int32 supports and friends."""
+
+    __slots__ = ("idx", "ln", "mask", "meta", "toff", "tslot")
+
+    def __init__(self, logits: torch.Tensor, k: int, transposed: bool):
+        self.idx, self.ln, self.mask, self.meta, self.toff, self.tslot = native().route_build(
+            logits.detach().float().contiguous(), int(k), bool(transposed))
+
+
+class MoCEFunction(torch.autograd.Function):
+    """Y = MoCE(X; L, gate) with the native forward and backward.
+
+    Inputs: x [B, C, H, W]; logits [E_r, C]; gate_w [1, k]; gate_b [1]; the
+    temperature constants tmin_tau = temp_min * tau and
+    trange_tau = (temp_max - temp_min) * tau; and a route cache built from
+    the same logits (with transposed lists when gradients are needed).
+    """
+
+    @staticmethod
+    def forward(ctx, x, logits, gate_w, gate_b, tmin_tau, trange_tau, route):
+        m = native()
+        x = x.contiguous()
+        gw = gate_w.detach().reshape(-1).float().contiguous()
+        gb = gate_b.detach().reshape(-1).float().contiguous()
+        z, T = m.gate_temperature(x, route.idx, gw, gb, float(tmin_tau), float(trange_tau))
+        y = m.mix(x, route.idx, route.ln, T, route.mask)
+        ctx.save_for_backward(x, logits.detach(), gw, gb, z, T)
+        ctx.route = route
+        ctx.consts = (float(tmin_tau), float(trange_tau))
+        ctx.gate_shapes = (gate_w.shape, gate_b.shape)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, logits, gw, gb, z, T = ctx.saved_tensors
+        r = ctx.route
+        if r.toff.numel() == 0:
+            raise RuntimeError("MoCEFunction: route cache was built without transposed lists")
+        dx, dL, dgw, dgb = native().backward(
+            x, dy.to(x.dtype).contiguous(), logits.float().contiguous(), r.idx, r.ln, r.mask, r.meta, r.toff,
+            r.tslot, gw, gb, ctx.consts[0], ctx.consts[1], z, T)
+        wshape, bshape = ctx.gate_shapes
+        return (dx, dL.to(logits.dtype), dgw.reshape(wshape), dgb.reshape(bshape), None, None, None)
+
+
+class MoCE(nn.Module):
+    """Mixture of Channel Experts: E-1 routed experts + 1 residual expert.
+
+    Same constructor and attributes as the reference (``MoCE.py:26-79``).
+    """
+
+    def __init__(self, in_channels=256, sampling_factor=4, k=8, tau=1.0, balance_weight=0.05,
+                 specialization_weight=0.1, diversity_weight=0.01, temp_min=0.2, temp_max=5.0):
+        super().__init__()
+        self.in_channels = in_channels
+        self.num_experts = in_channels // sampling_factor
+        self.k = k
+        self.tau = tau
+        self.balance_weight = balance_weight
+        self.specialization_weight = specialization_weight
+        self.diversity_weight = diversity_weight
+        self.temp_min = temp_min
+        self.temp_max = temp_max
+        self._last_temperature = None
+        self.aux_loss = 0.0
+        routed = max(self.num_experts - 1, 1)
+        self.target_experts_per_channel = routed * self.k / max(float(self.in_channels), 1.0)
+        self.routing_logits = nn.Parameter(torch.randn(self.num_experts - 1, in_channels))
+        self.gate = nn.Linear(k, 1)
+        nn.init.xavier_uniform_(self.gate.weight)
+        nn.init.zeros_(self.gate.bias)
+        self.register_buffer("cached_indices", None)
+        self.register_buffer("cached_selected_logits_norm", None)
+        self.register_buffer("cached_mask_int", None, persistent=False)
+        self.cached_temp_min_tau = None
+        self.cached_temp_range_tau = None
+        self.cached_gate_weight = None
+        self.cached_gate_bias = None
+        self._route = None        # native eval cache (int32 supports etc.)
+
+    # ------------------------------------------------------------------
+    def forward(self, x):
+        return self.forward_train(x) if self.training else self.forward_eval(x)
+
+    # ------------------------------------------------------------------
+    def build_eval_cache(self):
+        """Select supports, normalise their logits and mark uncovered channels.
+
+        Runs the native route-build kernel; fills the reference's cached_*
+        attributes (``MoCE.py:85-109``) plus the int32 native cache.
+        """
+        with torch.no_grad():
+            route = _Route(self.routing_logits, self.k, transposed=False)
+            self._route = route
+            self.cached_indices = route.idx.long()
+            self.cached_selected_logits_norm = route.ln.to(self.routing_logits.dtype)
+            self.cached_mask_int = route.mask
+        self.cached_temp_min_tau = float(self.temp_min) * float(self.tau)
+        self.cached_temp_range_tau = float(self.temp_max - self.temp_min) * float(self.tau)
+        self.cached_gate_weight = self.gate.weight.squeeze(0).contiguous()
+        # as in the reference, .contiguous() of the (contiguous) bias returns
+        # the Parameter itself, which nn.Module registers under this name
+        self.cached_gate_bias = self.gate.bias.contiguous()
+
+    def clear_eval_cache(self):
+        self.cached_indices = None
+        self.cached_selected_logits_norm = None
+        self.cached_mask_int = None
+        self._route = None
+
+    # ------------------------------------------------------------------
+    def _compute_aux_losses(self, x, E_routed, tau):
+        """Balance + specialisation + diversity losses (``MoCE.py:118-151``)."""
+        P = F.softmax(self.routing_logits / tau, dim=1)               # [E_r, C]
+        usage = P.mean(dim=0)
+        balance = (usage - usage.mean()).pow(2).mean()
+        per_channel = P / P.sum(dim=0, keepdim=True).clamp(min=1e-8)
+        entropy = -(per_channel * per_channel.clamp(min=1e-8).log()).sum(dim=0)
+        target = math.log(max(float(self.target_experts_per_channel), 1.0))
+        specialization = F.relu(entropy - target).mean()
+        if E_routed > 1:
+            overlap = P @ P.t()
+            off = ~torch.eye(E_routed, dtype=torch.bool, device=P.device)
+            diversity = overlap[off].mean()
+        else:
+            diversity = P.new_zeros(())
+        self.aux_loss = (self.balance_weight * balance + self.specialization_weight * specialization
+                         + self.diversity_weight * diversity)
+
+    def forward_train(self, x):
+        B, C, H, W = x.shape
+        E_routed = self.num_experts - 1
+        tau = max(float(self.tau), 1e-4)
+        with torch.no_grad():
+            route = _Route(self.routing_logits, self.k, transposed=True)
+        self._compute_aux_losses(x, E_routed, tau)
+        y = MoCEFunction.apply(x, self.routing_logits, self.gate.weight, self.gate.bias,
+                               self.temp_min * tau, (self.temp_max - self.temp_min) * tau, route)
+        return y
+
+    # ------------------------------------------------------------------
+    def forward_eval(self, x):
+        if self.cached_indices is None:
+            raise RuntimeError("MoCE eval cache not built. Call build_moce_cache(model) before eval.")
+        route = self._route
+        if route is None or route.idx.device != x.device:
+            # cache restored from a state_dict, or moved: rebuild the native part
+            route = _Route(self.routing_logits, self.k, transposed=False)
+            self._route = route
+        m = native()
+        xc = x.contiguous()
+        gw = self.cached_gate_weight.detach().reshape(-1).float().contiguous()
+        gb = self.cached_gate_bias.detach().reshape(-1).float().contiguous()
+        ln = self.cached_selected_logits_norm.detach().float().contiguous()
+        _, T = m.gate_temperature(xc, route.idx, gw, gb, float(self.cached_temp_min_tau),
+                                  float(self.cached_temp_range_tau))
+        return m.mix(xc, route.idx, ln, T, route.mask)

@@ -1,0 +1,94 @@
+"""Torch-tensor conveniences over the C ABI (ctypes), used by the GPU tests.
+
+Every helper calls exactly one or two entry points of ``include/moce_b200.h``
+with device pointers of torch tensors and the current stream; outputs are
+allocated here (the entry points never allocate).
+"""
+from __future__ import annotations
+
+import torch
+
+from moce_thesis_b200 import capi
+from moce_thesis_b200.capi import call, dtype_code, ptr, stream_handle
+
+
+def route_build(L: torch.Tensor, k: int, transposed: bool = True):
+    E_r, C = L.shape
+    dev = L.device
+    i32 = dict(dtype=torch.int32, device=dev)
+    idx = torch.empty(E_r, k, **i32)
+    ln = torch.empty(E_r, k, dtype=torch.float32, device=dev)
+    mask = torch.empty(C, **i32)
+    meta = torch.empty(2, **i32)
+    toff = torch.empty(C + 1, **i32) if transposed else None
+    tslot = torch.empty(E_r * k, **i32) if transposed else None
+    call("moce_route_build", ptr(L), E_r, C, k, ptr(idx), ptr(ln), ptr(mask), ptr(meta), ptr(toff), ptr(tslot),
+         stream_handle())
+    return dict(idx=idx, ln=ln, mask=mask, meta=meta, toff=toff, tslot=tslot)
+
+
+def gate_temperature(x, idx, gate_w, gate_b, tmin_tau, trange_tau, pooled=None):
+    B, C = x.shape[:2]
+    HW = x.shape[2] * x.shape[3]
+    E_r, k = idx.shape
+    z = torch.empty(B, C, dtype=torch.float32, device=x.device)
+    T = torch.empty(B, E_r, dtype=torch.float32, device=x.device)
+    call("moce_gate_temperature", ptr(x), dtype_code(x), ptr(pooled), B, C, HW, ptr(idx), E_r, k, ptr(gate_w),
+         ptr(gate_b), tmin_tau, trange_tau, ptr(z), ptr(T), stream_handle())
+    return z, T
+
+
+def mix(x, idx, ln, T, mask):
+    B, C, H, W = x.shape
+    E_r, k = idx.shape
+    y = torch.empty(B, E_r + 1, H, W, dtype=x.dtype, device=x.device)
+    call("moce_mix", ptr(x), dtype_code(x), B, C, H * W, ptr(idx), ptr(ln), ptr(T), E_r, k, ptr(mask), ptr(y),
+         stream_handle())
+    return y
+
+
+def forward(x, L, gate_w, gate_b, k, tmin, tmax, tau, route=None):
+    """Eval-form forward through the C ABI: route build, pass 1, pass 2."""
+    r = route or route_build(L, k, transposed=False)
+    z, T = gate_temperature(x, r["idx"], gate_w, gate_b, tmin * tau, (tmax - tmin) * tau)
+    return mix(x, r["idx"], r["ln"], T, r["mask"]), dict(r, z=z, T=T)
+
+
+def forward_dynamic_temp(x, indices, weights, mask):
+    B, C, H, W = x.shape
+    E_r, K = indices.shape
+    y = torch.empty(B, E_r + 1, H, W, dtype=x.dtype, device=x.device)
+    bits = 64 if indices.dtype == torch.int64 else 32
+    call("moce_forward_dynamic_temp", ptr(x), dtype_code(x), ptr(indices), bits, ptr(weights), ptr(mask), ptr(y),
+         B, C, H * W, E_r, K, stream_handle())
+    return y
+
+
+def gate_route(x, pooled, indices, ln, gate_w, gate_b, mask, tmin, tmax, tau):
+    B, C, H, W = x.shape
+    E_r, K = indices.shape
+    y = torch.empty(B, E_r + 1, H, W, dtype=x.dtype, device=x.device)
+    nb = capi.lib().moce_gate_route_workspace_bytes(B, C, E_r)
+    ws = torch.empty(nb + 256, dtype=torch.uint8, device=x.device)
+    wp = (ws.data_ptr() + 255) & ~255
+    bits = 64 if indices.dtype == torch.int64 else 32
+    call("moce_gate_route", ptr(x), dtype_code(x), ptr(pooled), ptr(indices), bits, ptr(ln), ptr(gate_w),
+         ptr(gate_b), ptr(mask), tmin, tmax, tau, ptr(y), B, C, H * W, E_r, K, wp, nb, stream_handle())
+    return y
+
+
+def backward(x, dy, L, r, gate_w, gate_b, tmin_tau, trange_tau):
+    B, C, H, W = x.shape
+    E_r, k = r["idx"].shape
+    dx = torch.empty_like(x)
+    dL = torch.empty(E_r, C, dtype=torch.float32, device=x.device)
+    dgw = torch.empty(k, dtype=torch.float32, device=x.device)
+    dgb = torch.empty(1, dtype=torch.float32, device=x.device)
+    nb = capi.lib().moce_backward_workspace_bytes(B, C, H * W, E_r, k)
+    ws = torch.empty(nb + 256, dtype=torch.uint8, device=x.device)
+    wp = (ws.data_ptr() + 255) & ~255
+    call("moce_backward", ptr(x), ptr(dy), dtype_code(x), B, C, H * W, ptr(L), ptr(r["idx"]), ptr(r["ln"]),
+         ptr(r["mask"]), ptr(r["meta"]), ptr(r["toff"]), ptr(r["tslot"]), E_r, k, ptr(gate_w), ptr(gate_b),
+         tmin_tau, trange_tau, ptr(r["z"]), ptr(r["T"]), ptr(dx), ptr(dL), ptr(dgw), ptr(dgb), wp, nb,
+         stream_handle())
+    return dict(dX=dx, dL=dL, dgate_w=dgw, dgate_b=dgb)

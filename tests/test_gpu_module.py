@@ -1,0 +1,139 @@
+"""GPU tests of the nn.Module surface and of the ``moce_fixed.moce_cuda``
+binding (the reference module path), against the reference golden vectors.
+
+The layer is built the way ``tests/golden/make_golden.py`` builds the
+reference one (sampling_factor=1, then E, the logits and the gate forced to
+the case's values).  Tolerances as in ``test_gpu_parity.py``.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from inputs import CASES, make_inputs
+from moce_thesis_b200 import MoCE, native
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+FULL = [n for n, c in CASES.items() if not c.get("summary")]
+DEV = "cuda:0"
+
+
+def load(name):
+    return dict(np.load(os.path.join(GOLD, f"{name}.npz")))
+
+
+def close(a, b, rtol=1e-5, floor=1e-6):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return bool(np.all(np.abs(a - b) <= rtol * np.abs(b) + floor * max(np.abs(b).max(), 1e-30)))
+
+
+def maxrel(a, b, floor=1e-3):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), floor))
+
+
+def build_layer(case, t):
+    C, E, k = case["C"], case["E"], case["k"]
+    m = MoCE(in_channels=C, sampling_factor=1, k=k, tau=case["tau"], temp_min=case["tmin"], temp_max=case["tmax"])
+    m.num_experts = E
+    m.routing_logits = torch.nn.Parameter(t["L"].clone())
+    m.target_experts_per_channel = (max(E - 1, 1) * k) / max(float(C), 1.0)
+    with torch.no_grad():
+        m.gate.weight.copy_(t["gate_w"])
+        m.gate.bias.copy_(t["gate_b"])
+    return m.to(DEV)
+
+
+@pytest.mark.parametrize("name", FULL)
+def test_module_train_forward_backward(name):
+    g, c = load(name), CASES[name]
+    t = make_inputs(c)
+    m = build_layer(c, t)
+    m.train()
+    x = t["X"].to(DEV).requires_grad_(True)
+    y = m(x)
+    assert close(y.detach().cpu().numpy(), g["Y_train"])
+    assert abs(float(m.aux_loss) - float(g["aux"])) <= 1e-5 * max(abs(float(g["aux"])), 1e-6)
+    (y * t["dY"].to(DEV)).sum().backward()
+    assert maxrel(x.grad.cpu().numpy(), g["dX"]) < 1e-5
+    assert maxrel(m.gate.weight.grad.cpu().numpy(), g["dgate_w"]) < 1e-5
+    assert maxrel(m.gate.bias.grad.cpu().numpy(), g["dgate_b"]) < 1e-5
+    # routing-logit gradient = main path + auxiliary loss (reference autograd of both)
+    m.zero_grad()
+    y = m(t["X"].to(DEV))
+    ((y * t["dY"].to(DEV)).sum() + m.aux_loss).backward()
+    assert maxrel(m.routing_logits.grad.cpu().numpy(), g["dL"] + g["dL_aux"]) < 1e-5
+
+
+@pytest.mark.parametrize("name", FULL)
+def test_module_eval(name):
+    g, c = load(name), CASES[name]
+    t = make_inputs(c)
+    m = build_layer(c, t).eval()
+    with pytest.raises(RuntimeError, match="eval cache not built"):
+        m(t["X"].to(DEV))
+    m.build_eval_cache()
+    np.testing.assert_array_equal(m.cached_indices.cpu().numpy(), g["idx"])
+    assert m.cached_indices.dtype == torch.int64
+    np.testing.assert_array_equal(m.cached_mask_int.cpu().numpy(), g["mask"])
+    with torch.no_grad():
+        y = m(t["X"].to(DEV))
+        yb = m(t["X"].to(DEV, torch.bfloat16))
+    assert close(y.cpu().numpy(), g["Y_eval"])
+    assert yb.dtype == torch.bfloat16
+    assert close(yb.float().cpu().numpy(), g["Y_eval"], rtol=2e-2, floor=1e-2)
+
+
+def test_state_dict_keys_match_reference_layout():
+    m = MoCE(in_channels=32, sampling_factor=2, k=4).to(DEV)
+    assert set(m.state_dict()) == {"routing_logits", "gate.weight", "gate.bias"}
+    m.eval()
+    m.build_eval_cache()
+    # after the cache build the reference state_dict also carries these
+    assert {"cached_indices", "cached_selected_logits_norm", "cached_gate_bias"} <= set(m.state_dict())
+
+
+@pytest.mark.parametrize("name", ["small_resid", "covered_odd", "k40"])
+def test_binding_reference_functions(name):
+    """The seven reference entry points, called the way MoCE.py would."""
+    g, c = load(name), CASES[name]
+    mc = native()
+    X = torch.from_numpy(g["X"]).to(DEV)
+    idx64 = torch.from_numpy(g["idx"]).to(DEV)
+    w = torch.from_numpy(g["weights"]).to(DEV)
+    mask = torch.from_numpy(g["mask"]).to(DEV)
+    ln = torch.from_numpy(g["ln"]).to(DEV)
+    gw = torch.from_numpy(g["gate_w"].reshape(-1)).to(DEV)
+    gb = torch.from_numpy(g["gate_b"]).to(DEV)
+    out, = mc.fused_moce_forward_dynamic_temp(X, idx64, w, mask)
+    assert close(out.cpu().numpy(), g["Y_eval"])
+    pooled, = mc.moce_pool(X)
+    assert close(pooled.cpu().numpy(), X.mean((2, 3)).cpu().numpy())
+    args = (idx64, ln, gw, gb, mask, c["tmin"], c["tmax"], c["tau"])
+    for fn in (mc.fused_moce_gate_route, mc.fused_moce_gate_route_timed, mc.fused_moce_gate_route_section_timed):
+        res = fn(X, pooled, *args)
+        assert close(res[0].cpu().numpy(), g["Y_eval"]), fn.__name__
+    for fn in (mc.fused_moce_gate_route_all, mc.fused_moce_gate_route_all_timed):
+        res = fn(X, *args)
+        assert close(res[0].cpu().numpy(), g["Y_eval"]), fn.__name__
+    _, kt = mc.fused_moce_gate_route_timed(X, pooled, *args)
+    assert kt.shape == (2,) and float(kt.min()) >= 0.0
+    _, kt3, sec = mc.fused_moce_gate_route_all_timed(X, *args)
+    assert kt3.shape == (3,) and sec.shape == (4,)
+
+
+def test_binding_errors_match_reference_checks():
+    mc = native()
+    X = torch.rand(2, 8, 3, 3, device=DEV)
+    idx = torch.zeros(3, 2, dtype=torch.int64, device=DEV)
+    mask = torch.zeros(8, dtype=torch.int32, device=DEV)
+    with pytest.raises(RuntimeError, match="must be CUDA"):
+        mc.fused_moce_forward_dynamic_temp(X.cpu(), idx, torch.rand(2, 3, 2, device=DEV), mask)
+    with pytest.raises(RuntimeError, match="weights must be"):
+        mc.fused_moce_forward_dynamic_temp(X, idx, torch.rand(2, 3, 3, device=DEV), mask)
+    with pytest.raises(RuntimeError, match="mask_int must be int32"):
+        mc.fused_moce_forward_dynamic_temp(X, idx, torch.rand(2, 3, 2, device=DEV), mask.long())
