@@ -64,6 +64,49 @@ int moce_route_build(const float* logits, int64_t E_r, int64_t C, int64_t k,
                      int32_t* toff, int32_t* tslot, void* stream);
 
 /*
+ * Support schedule for the scheduled mix (no reference counterpart: it is a
+ * layout of the supports chosen at cache-build time).  Experts are grouped
+ * 32 per warp (balance != 0: greedily, so each group's supports spread over
+ * the 32 shared-memory banks; balance == 0: experts 32g .. 32g+31), and each
+ * group's supports are ordered into moce_schedule_steps(k) steps in which the
+ * 32 lanes read 32 different banks.
+ *   group_expert int32 [G*32], G = ceil(E_r/32)    out: expert of each lane, -1 if none
+ *   sched        int32 [G*S*32], S = moce_schedule_steps(k)
+ *                out: entry (slot << 16) | channel, slot 0xFFFF = idle step
+ * Requires k <= 256, C <= 65535, E_r <= 32768.
+ */
+int moce_schedule_steps(int64_t k);
+int moce_schedule_build(const int32_t* idx, int64_t E_r, int64_t C, int64_t k,
+                        int balance, int32_t* group_expert, int32_t* sched,
+                        void* stream);
+
+/*
+ * Pass 1 of the fast path: one read of X gives the pooled means z (fp32
+ * [B, C], MoCE.py:174 / 212) and, if y is not NULL, the residual expert
+ * channel y[:, E_r, :] (mean over channels with mask[c] == 1, 0 if none;
+ * MoCE.py:191-196, moce_kernel.cu:148-231).  y is [B, E_r+1, HW] in the dtype
+ * of X; meta is the route cache's {n_uncovered, 0}.
+ */
+int moce_pool_residual(const void* x, int dtype, int64_t B, int64_t C,
+                       int64_t HW, const int32_t* mask, const int32_t* meta,
+                       float* z, void* y, int64_t E_r, void* stream);
+
+/*
+ * Pass 2 of the fast path: routed experts 0 .. E_r-1 of y from X, the pooled
+ * z of pass 1, the normalised logits ln [E_r, k] and the schedule.  Fuses
+ * the gate and temperature (MoCE.py:216-218 / 175-178), the softmax of ln/T
+ * (MoCE.py:219-221 / 188) and the gather-mix (moce_kernel.cu:57-141).  If
+ * T_out is not NULL the temperatures fp32 [B, E_r] are written there (the
+ * backward needs them).  Requires moce_schedule_steps(k) <= 52 (k <= 44).
+ */
+int moce_mix_scheduled(const void* x, int dtype, int64_t B, int64_t C,
+                       int64_t HW, const float* z, const float* ln,
+                       int64_t E_r, int64_t k, const int32_t* group_expert,
+                       const int32_t* sched, const float* gate_w,
+                       const float* gate_b, float tmin_tau, float trange_tau,
+                       void* y, float* T_out, void* stream);
+
+/*
  * Global average pool: pooled[b,c] = mean_p X[b,c,p] (fp32 out).
  * Replaces moce_pool (moce_layer_cuda.cpp:8-10, moce_kernel.cu:849-861).
  * pooled has the dtype of X in the reference; here it is always fp32.

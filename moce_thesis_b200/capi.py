@@ -28,6 +28,11 @@ SIGNATURES = {
     "moce_version": (ctypes.c_char_p, []),
     "moce_route_build": (_i32, [_p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p]),
     "moce_pool": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p]),
+    "moce_schedule_steps": (_i32, [_i64]),
+    "moce_schedule_build": (_i32, [_p, _i64, _i64, _i64, _i32, _p, _p, _p]),
+    "moce_pool_residual": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _p]),
+    "moce_mix_scheduled": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _i64, _i64, _p, _p, _p, _p, _f32, _f32,
+                                  _p, _p, _p]),
     "moce_gate_temperature": (_i32, [_p, _i32, _p, _i64, _i64, _i64, _p, _i64, _i64, _p, _p, _f32, _f32,
                                      _p, _p, _p]),
     "moce_mix": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p, _p]),

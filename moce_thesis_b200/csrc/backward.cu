@@ -294,9 +294,9 @@ extern "C" int moce_backward(const void* x, const void* dy, int dtype, int64_t B
                              float trange_tau, const float* z, const float* T, void* dx, float* dL,
                              float* dgate_w, float* dgate_b, void* workspace, size_t workspace_bytes,
                              void* stream) {
-  MOCE_REQUIRE(x && dy && logits && idx && ln && mask && meta && toff && tslot && gate_w && gate_b && z && T &&
-                   dx && dL && dgate_w && dgate_b,
+  MOCE_REQUIRE(logits && idx && ln && mask && meta && toff && tslot && gate_w && gate_b && dL && dgate_w && dgate_b,
                MOCE_ERR_INVALID, "moce_backward: null pointer argument");
+  MOCE_REQUIRE(B == 0 || (x && dy && z && T && dx), MOCE_ERR_INVALID, "moce_backward: null pointer argument");
   MOCE_REQUIRE(dtype_ok(dtype), MOCE_ERR_INVALID, "moce_backward: unknown dtype %d", dtype);
   int rc = check_bwd_shapes(B, C, HW, E_r, k);
   if (rc) return rc;

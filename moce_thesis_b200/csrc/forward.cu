@@ -276,6 +276,7 @@ using namespace moce;
 
 extern "C" int moce_pool(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, float* pooled,
                          void* stream) {
+  if (B == 0) return MOCE_OK;  // an empty batch is a no-op
   MOCE_REQUIRE(x && pooled, MOCE_ERR_INVALID, "moce_pool: null pointer argument");
   MOCE_REQUIRE(dtype_ok(dtype), MOCE_ERR_INVALID, "moce_pool: unknown dtype %d", dtype);
   int rc = check_shapes("moce_pool", B, C, HW, 1, 1);
@@ -301,6 +302,7 @@ extern "C" int moce_gate_temperature(const void* x, int dtype, const float* pool
                                      int64_t k, const float* gate_w, const float* gate_b,
                                      float tmin_tau, float trange_tau, float* z, float* T,
                                      void* stream) {
+  if (B == 0) return MOCE_OK;  // an empty batch is a no-op
   MOCE_REQUIRE((x || pooled_in) && idx && gate_w && gate_b && T, MOCE_ERR_INVALID,
                "moce_gate_temperature: null pointer argument");
   MOCE_REQUIRE(dtype_ok(dtype), MOCE_ERR_INVALID, "moce_gate_temperature: unknown dtype %d", dtype);
@@ -317,6 +319,7 @@ extern "C" int moce_gate_temperature(const void* x, int dtype, const float* pool
 extern "C" int moce_mix(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* idx,
                         const float* ln, const float* T, int64_t E_r, int64_t k, const int32_t* mask, void* y,
                         void* stream) {
+  if (B == 0) return MOCE_OK;  // an empty batch is a no-op
   MOCE_REQUIRE(x && idx && ln && T && mask && y, MOCE_ERR_INVALID, "moce_mix: null pointer argument");
   MOCE_REQUIRE(dtype_ok(dtype), MOCE_ERR_INVALID, "moce_mix: unknown dtype %d", dtype);
   int rc = check_shapes("moce_mix", B, C, HW, E_r, k);
@@ -335,6 +338,7 @@ extern "C" int moce_mix(const void* x, int dtype, int64_t B, int64_t C, int64_t 
 extern "C" int moce_forward_dynamic_temp(const void* x, int dtype, const void* indices, int index_bits,
                                          const float* weights, const int32_t* mask, void* y, int64_t B,
                                          int64_t C, int64_t HW, int64_t E_r, int64_t K, void* stream) {
+  if (B == 0) return MOCE_OK;  // an empty batch is a no-op
   MOCE_REQUIRE(x && indices && weights && mask && y, MOCE_ERR_INVALID,
                "moce_forward_dynamic_temp: null pointer argument");
   MOCE_REQUIRE(dtype_ok(dtype), MOCE_ERR_INVALID, "moce_forward_dynamic_temp: unknown dtype %d", dtype);
@@ -366,6 +370,7 @@ extern "C" int moce_gate_route(const void* x, int dtype, const float* pooled, co
                                const int32_t* mask, float temp_min, float temp_max, float tau, void* y, int64_t B,
                                int64_t C, int64_t HW, int64_t E_r, int64_t K, void* workspace,
                                size_t workspace_bytes, void* stream) {
+  if (B == 0) return MOCE_OK;  // an empty batch is a no-op
   MOCE_REQUIRE(x && indices && logits_norm && gate_w && gate_b && mask && y, MOCE_ERR_INVALID,
                "moce_gate_route: null pointer argument");
   MOCE_REQUIRE(dtype_ok(dtype), MOCE_ERR_INVALID, "moce_gate_route: unknown dtype %d", dtype);

@@ -358,6 +358,61 @@ std::vector<torch::Tensor> backward(torch::Tensor x, torch::Tensor dy, torch::Te
   return {dx, dL, dgw, dgb};
 }
 
+
+// ------------------------------------------------------- fast path
+
+std::vector<torch::Tensor> schedule_build(torch::Tensor idx, int64_t C, bool balance) {
+  CHECK_INPUT(idx);
+  TORCH_CHECK(idx.scalar_type() == torch::kInt32 && idx.dim() == 2, "idx must be int32 (E_r, k)");
+  const c10::cuda::CUDAGuard guard(idx.device());
+  const int64_t E_r = idx.size(0), k = idx.size(1);
+  const int64_t G = (E_r + 31) / 32;
+  const int64_t S = moce_schedule_steps(k);
+  auto i32 = idx.options();
+  auto group_expert = torch::empty({G * 32}, i32);
+  auto sched = torch::empty({G * S * 32}, i32);
+  ok(moce_schedule_build(idx.data_ptr<int32_t>(), E_r, C, k, balance ? 1 : 0, group_expert.data_ptr<int32_t>(),
+                         sched.data_ptr<int32_t>(), cur_stream()));
+  return {group_expert, sched};
+}
+
+bool schedule_supported(int64_t k) { return k >= 1 && moce_schedule_steps(k) <= 52; }
+
+// pass 1 (pool + residual) and pass 2 (gate, temperature, softmax, mix)
+std::vector<torch::Tensor> forward_scheduled(torch::Tensor x, torch::Tensor ln, torch::Tensor mask, torch::Tensor meta,
+                                             torch::Tensor group_expert, torch::Tensor sched, torch::Tensor gate_w,
+                                             torch::Tensor gate_b, double tmin_tau, double trange_tau, bool want_T,
+                                             c10::optional<torch::Tensor> out_opt) {
+  for (auto* t : {&x, &ln, &mask, &meta, &group_expert, &sched, &gate_w, &gate_b}) {
+    CHECK_INPUT(*t);
+  }
+  TORCH_CHECK(x.dim() == 4 && ln.dim() == 2, "x must be (B, C, H, W), ln (E_r, k)");
+  TORCH_CHECK(gate_w.scalar_type() == torch::kFloat32 && gate_b.scalar_type() == torch::kFloat32 &&
+                  ln.scalar_type() == torch::kFloat32,
+              "gate and ln must be float32");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t B = x.size(0), C = x.size(1), H = x.size(2), W = x.size(3), HW = H * W;
+  const int64_t E_r = ln.size(0), k = ln.size(1);
+  TORCH_CHECK(mask.numel() == C && gate_w.numel() == k, "shape mismatch");
+  torch::Tensor y;
+  if (out_opt.has_value()) {
+    y = *out_opt;
+    CHECK_INPUT(y);
+    TORCH_CHECK(y.scalar_type() == x.scalar_type() && y.numel() == B * (E_r + 1) * HW, "out mismatch");
+  } else {
+    y = torch::empty({B, E_r + 1, H, W}, x.options());
+  }
+  auto z = f32_opts_like(x, {B, C});
+  auto T = want_T ? f32_opts_like(x, {B, E_r}) : f32_opts_like(x, {0});
+  ok(moce_pool_residual(x.data_ptr(), dtype_of(x), B, C, HW, mask.data_ptr<int32_t>(), meta.data_ptr<int32_t>(),
+                        z.data_ptr<float>(), y.data_ptr(), E_r, cur_stream()));
+  ok(moce_mix_scheduled(x.data_ptr(), dtype_of(x), B, C, HW, z.data_ptr<float>(), ln.data_ptr<float>(), E_r, k,
+                        group_expert.data_ptr<int32_t>(), sched.data_ptr<int32_t>(), gate_w.data_ptr<float>(),
+                        gate_b.data_ptr<float>(), (float)tmin_tau, (float)trange_tau, y.data_ptr(),
+                        want_T ? T.data_ptr<float>() : nullptr, cur_stream()));
+  return {y, z, T};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -380,5 +435,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mix", &mix, "Pass 2: softmax + gather-mix + residual", py::arg("x"), py::arg("idx"), py::arg("ln"),
         py::arg("T"), py::arg("mask"), py::arg("out") = py::none());
   m.def("backward", &backward, "Layer backward: (dx, dL, dgate_w, dgate_b)");
+  m.def("schedule_build", &schedule_build, "Warp groups and bank-conflict-free support schedule",
+        py::arg("idx"), py::arg("C"), py::arg("balance") = true);
+  m.def("schedule_supported", &schedule_supported, "Whether k fits the scheduled mix kernel");
+  m.def("forward_scheduled", &forward_scheduled, "Fast path: (y, z, T)", py::arg("x"), py::arg("ln"), py::arg("mask"),
+        py::arg("meta"), py::arg("group_expert"), py::arg("sched"), py::arg("gate_w"), py::arg("gate_b"),
+        py::arg("tmin_tau"), py::arg("trange_tau"), py::arg("want_T") = false, py::arg("out") = py::none());
   m.def("version", []() { return std::string(moce_version()); });
 }

@@ -35,13 +35,29 @@ def native():
 
 
 class _Route:
-    """Native route cache of one logits tensor: int32 supports and friends."""
+    """Native route cache of one logits tensor: int32 supports, normalised
+    logits, coverage, optional transposed lists (backward) and, when k fits
+    the scheduled mix kernel, the warp groups and support schedule."""
 
-    __slots__ = ("idx", "ln", "mask", "meta", "toff", "tslot")
+    __slots__ = ("idx", "ln", "mask", "meta", "toff", "tslot", "group_expert", "sched")
 
-    def __init__(self, logits: torch.Tensor, k: int, transposed: bool):
-        self.idx, self.ln, self.mask, self.meta, self.toff, self.tslot = native().route_build(
-            logits.detach().float().contiguous(), int(k), bool(transposed))
+    def __init__(self, logits: torch.Tensor, k: int, transposed: bool, balance: bool = True):
+        m = native()
+        L = logits.detach().float().contiguous()
+        self.idx, self.ln, self.mask, self.meta, self.toff, self.tslot = m.route_build(L, int(k), bool(transposed))
+        self.group_expert = self.sched = None
+        if m.schedule_supported(int(k)):
+            self.group_expert, self.sched = m.schedule_build(self.idx, L.shape[1], bool(balance))
+
+    def forward(self, x, gate_w, gate_b, tmin_tau, trange_tau, want_T=False):
+        """Both forward passes; returns (y, z, T).  T is None unless wanted."""
+        m = native()
+        if self.sched is not None:
+            y, z, T = m.forward_scheduled(x, self.ln, self.mask, self.meta, self.group_expert, self.sched, gate_w,
+                                          gate_b, float(tmin_tau), float(trange_tau), bool(want_T))
+            return y, z, (T if want_T else None)
+        z, T = m.gate_temperature(x, self.idx, gate_w, gate_b, float(tmin_tau), float(trange_tau))
+        return m.mix(x, self.idx, self.ln, T, self.mask), z, T
 
 
 class MoCEFunction(torch.autograd.Function):
@@ -59,8 +75,7 @@ class MoCEFunction(torch.autograd.Function):
         x = x.contiguous()
         gw = gate_w.detach().reshape(-1).float().contiguous()
         gb = gate_b.detach().reshape(-1).float().contiguous()
-        z, T = m.gate_temperature(x, route.idx, gw, gb, float(tmin_tau), float(trange_tau))
-        y = m.mix(x, route.idx, route.ln, T, route.mask)
+        y, z, T = route.forward(x, gw, gb, tmin_tau, trange_tau, want_T=True)
         ctx.save_for_backward(x, logits.detach(), gw, gb, z, T)
         ctx.route = route
         ctx.consts = (float(tmin_tau), float(trange_tau))
@@ -169,7 +184,9 @@ class MoCE(nn.Module):
         E_routed = self.num_experts - 1
         tau = max(float(self.tau), 1e-4)
         with torch.no_grad():
-            route = _Route(self.routing_logits, self.k, transposed=True)
+            # supports are re-selected every step; the warp grouping is the
+            # identity here (balancing is a sequential pass worth doing once)
+            route = _Route(self.routing_logits, self.k, transposed=True, balance=False)
         self._compute_aux_losses(x, E_routed, tau)
         y = MoCEFunction.apply(x, self.routing_logits, self.gate.weight, self.gate.bias,
                                self.temp_min * tau, (self.temp_max - self.temp_min) * tau, route)
@@ -184,11 +201,7 @@ class MoCE(nn.Module):
             # cache restored from a state_dict, or moved: rebuild the native part
             route = _Route(self.routing_logits, self.k, transposed=False)
             self._route = route
-        m = native()
-        xc = x.contiguous()
         gw = self.cached_gate_weight.detach().reshape(-1).float().contiguous()
         gb = self.cached_gate_bias.detach().reshape(-1).float().contiguous()
-        ln = self.cached_selected_logits_norm.detach().float().contiguous()
-        _, T = m.gate_temperature(xc, route.idx, gw, gb, float(self.cached_temp_min_tau),
-                                  float(self.cached_temp_range_tau))
-        return m.mix(xc, route.idx, ln, T, route.mask)
+        y, _, _ = route.forward(x.contiguous(), gw, gb, self.cached_temp_min_tau, self.cached_temp_range_tau)
+        return y

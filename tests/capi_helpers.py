@@ -47,9 +47,43 @@ def mix(x, idx, ln, T, mask):
     return y
 
 
-def forward(x, L, gate_w, gate_b, k, tmin, tmax, tau, route=None):
-    """Eval-form forward through the C ABI: route build, pass 1, pass 2."""
+def schedule_build(idx, C, balance=True):
+    E_r, k = idx.shape
+    G = (E_r + 31) // 32
+    S = capi.lib().moce_schedule_steps(k)
+    ge = torch.empty(G * 32, dtype=torch.int32, device=idx.device)
+    sched = torch.empty(G * S * 32, dtype=torch.int32, device=idx.device)
+    call("moce_schedule_build", ptr(idx), E_r, C, k, 1 if balance else 0, ptr(ge), ptr(sched), stream_handle())
+    return ge, sched
+
+
+def schedule_supported(k):
+    return capi.lib().moce_schedule_steps(k) <= 52
+
+
+def forward_fast(x, r, gate_w, gate_b, tmin_tau, trange_tau, want_T=True):
+    """Fast path through the C ABI: pass 1 (pool + residual), pass 2 (scheduled mix)."""
+    B, C, H, W = x.shape
+    E_r, k = r["idx"].shape
+    y = torch.empty(B, E_r + 1, H, W, dtype=x.dtype, device=x.device)
+    z = torch.empty(B, C, dtype=torch.float32, device=x.device)
+    T = torch.empty(B, E_r, dtype=torch.float32, device=x.device) if want_T else None
+    call("moce_pool_residual", ptr(x), dtype_code(x), B, C, H * W, ptr(r["mask"]), ptr(r["meta"]), ptr(z), ptr(y),
+         E_r, stream_handle())
+    call("moce_mix_scheduled", ptr(x), dtype_code(x), B, C, H * W, ptr(z), ptr(r["ln"]), E_r, k,
+         ptr(r["group_expert"]), ptr(r["sched"]), ptr(gate_w), ptr(gate_b), tmin_tau, trange_tau, ptr(y), ptr(T),
+         stream_handle())
+    return y, z, T
+
+
+def forward(x, L, gate_w, gate_b, k, tmin, tmax, tau, route=None, path="general", balance=True):
+    """Eval-form forward through the C ABI: route build, then either the
+    general two passes (pool + gate -> T, softmax + mix) or the fast path."""
     r = route or route_build(L, k, transposed=False)
+    if path == "fast":
+        r["group_expert"], r["sched"] = schedule_build(r["idx"], L.shape[1], balance)
+        y, z, T = forward_fast(x, r, gate_w, gate_b, tmin * tau, (tmax - tmin) * tau)
+        return y, dict(r, z=z, T=T)
     z, T = gate_temperature(x, r["idx"], gate_w, gate_b, tmin * tau, (tmax - tmin) * tau)
     return mix(x, r["idx"], r["ln"], T, r["mask"]), dict(r, z=z, T=T)
 

@@ -87,17 +87,31 @@ def test_route_build_large_rows(E_r, C, k):
     r = H.route_build(L.to(DEV), k)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(r["idx"].cpu().numpy(), O.select_supports(L.numpy(), k))
-    _, ti = torch.topk(L, k, dim=1)
-    np.testing.assert_array_equal(r["idx"].cpu().numpy(), ti.numpy())
+    tv, ti = torch.topk(L, k, dim=1)
+    got = r["idx"].cpu().numpy()
+    # same selected values everywhere; same order on rows without ties
+    np.testing.assert_array_equal(np.take_along_axis(L.numpy(), got, 1), tv.numpy())
+    ties = np.array([len(np.unique(row)) < C for row in L.numpy()])
+    np.testing.assert_array_equal(got[~ties], ti.numpy()[~ties])
 
 
 # ---------------------------------------------------------------- forward
 
+PATHS = ["general", "fast"]
+
+
+def path_ok(path, k):
+    return path == "general" or H.schedule_supported(k)
+
+
 @pytest.mark.parametrize("name", FULL)
-def test_forward_fp32_matches_golden(name):
+@pytest.mark.parametrize("path", PATHS)
+def test_forward_fp32_matches_golden(name, path):
     g, c = load(name), CASES[name]
+    if not path_ok(path, c["k"]):
+        pytest.skip("k beyond the scheduled kernel")
     y, st = H.forward(cu(g["X"]), cu(g["L"]), cu(g["gate_w"]), cu(g["gate_b"]), c["k"], c["tmin"], c["tmax"],
-                      c["tau"])
+                      c["tau"], path=path)
     Y = host(y)
     assert close(Y, g["Y_eval"]), relerr(Y, g["Y_eval"])
     ref = O.forward(g["X"], g["L"], g["gate_w"], g["gate_b"], c["k"], c["tmin"], c["tmax"], c["tau"], mode="eval")
@@ -111,10 +125,14 @@ def test_forward_fp32_matches_golden(name):
 
 @pytest.mark.parametrize("name", FULL)
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_forward_half_matches_oracle(name, dtype):
+@pytest.mark.parametrize("path", PATHS)
+def test_forward_half_matches_oracle(name, dtype, path):
     g, c = load(name), CASES[name]
+    if not path_ok(path, c["k"]):
+        pytest.skip("k beyond the scheduled kernel")
     x = cu(g["X"], dtype)
-    y, _ = H.forward(x, cu(g["L"]), cu(g["gate_w"]), cu(g["gate_b"]), c["k"], c["tmin"], c["tmax"], c["tau"])
+    y, _ = H.forward(x, cu(g["L"]), cu(g["gate_w"]), cu(g["gate_b"]), c["k"], c["tmin"], c["tmax"], c["tau"],
+                     path=path)
     assert y.dtype == dtype
     xr = x.float().cpu().numpy()
     ref = O.forward(xr, g["L"], g["gate_w"], g["gate_b"], c["k"], c["tmin"], c["tmax"], c["tau"], mode="eval")
@@ -172,11 +190,12 @@ def test_backward_deterministic():
 
 # ---------------------------------------------------------------- the single-layer workload
 
-def test_cfg1_against_pins():
+@pytest.mark.parametrize("path", PATHS)
+def test_cfg1_against_pins(path):
     c, g = CASES["cfg1"], load("cfg1")
     t = make_inputs(c)
     x, L, gw, gb, dy = (t[n].to(DEV) for n in ("X", "L", "gate_w", "gate_b", "dY"))
-    y, st = H.forward(x, L, gw, gb, c["k"], c["tmin"], c["tmax"], c["tau"])
+    y, st = H.forward(x, L, gw, gb, c["k"], c["tmin"], c["tmax"], c["tau"], path=path)
     Y = host(y)
     np.testing.assert_array_equal(st["idx"].cpu().numpy(), g["idx"].astype(np.int32))
     assert close(Y.reshape(-1)[g["Y_eval_pos"]], g["Y_eval_val"])
@@ -199,7 +218,10 @@ def test_cfg1_against_pins():
     (5, 130, 3, 7, 40, 33, torch.float32),     # ragged everything
     (1, 16, 1, 1, 2, 16, torch.float32),       # k == C, HW == 1, one routed expert
 ])
-def test_forward_backward_odd_shapes(B, C, H_, W_, E, k, dtype):
+@pytest.mark.parametrize("path", PATHS)
+def test_forward_backward_odd_shapes(B, C, H_, W_, E, k, dtype, path):
+    if not path_ok(path, k):
+        pytest.skip("k beyond the scheduled kernel")
     gen = torch.Generator().manual_seed(B * 1000 + C)
     X = torch.randn(B, C, H_, W_, generator=gen).abs()
     L = torch.randn(E - 1, C, generator=gen)
@@ -208,7 +230,7 @@ def test_forward_backward_odd_shapes(B, C, H_, W_, E, k, dtype):
     dY = torch.randn(B, E, H_, W_, generator=gen)
     x = X.to(DEV, dtype)
     Xr = x.float().cpu().numpy()
-    y, st = H.forward(x, L.to(DEV), gw.to(DEV), gb.to(DEV), k, 0.1, 10.0, 1.0)
+    y, st = H.forward(x, L.to(DEV), gw.to(DEV), gb.to(DEV), k, 0.1, 10.0, 1.0, path=path)
     ref = O.forward(Xr, L.numpy(), gw.numpy(), gb.numpy(), k, 0.1, 10.0, 1.0, mode="eval")
     rt = 1e-5 if dtype == torch.float32 else 1e-2
     assert close(host(y), ref, rtol=rt, floor=rt / 10), relerr(host(y), ref)
@@ -223,11 +245,12 @@ def test_forward_backward_odd_shapes(B, C, H_, W_, E, k, dtype):
         assert maxrel(got, want[key]) < 1e-5, (key, maxrel(got, want[key]))
 
 
-def test_empty_batch_is_a_noop():
+@pytest.mark.parametrize("path", PATHS)
+def test_empty_batch_is_a_noop(path):
     c = CASES["small_resid"]
     t = make_inputs(c)
     x = t["X"][:0].to(DEV)
-    y, _ = H.forward(x, t["L"].to(DEV), t["gate_w"].to(DEV), t["gate_b"].to(DEV), c["k"], 0.1, 10.0, 1.0)
+    y, _ = H.forward(x, t["L"].to(DEV), t["gate_w"].to(DEV), t["gate_b"].to(DEV), c["k"], 0.1, 10.0, 1.0, path=path)
     assert y.shape[0] == 0
 
 
@@ -242,3 +265,39 @@ def test_invalid_arguments_raise():
     z, T = H.gate_temperature(x, r["idx"], t["gate_w"].to(DEV), t["gate_b"].to(DEV), 0.1, 9.9)
     with pytest.raises(RuntimeError, match="null pointer"):
         H.mix(x, r["idx"], r["ln"], T, None)
+
+
+# ---------------------------------------------------------------- schedule
+
+@pytest.mark.parametrize("E_r,C,k,balance", [(2047, 512, 32, True), (1023, 256, 16, False), (63, 40, 7, True),
+                                              (5, 3, 3, True)])
+def test_schedule_is_a_permutation_of_the_supports(E_r, C, k, balance):
+    gen = torch.Generator().manual_seed(k)
+    L = torch.randn(E_r, C, generator=gen).to(DEV)
+    r = H.route_build(L, k, transposed=False)
+    ge, sched = H.schedule_build(r["idx"], C, balance)
+    torch.cuda.synchronize()
+    ge, sched, idx = ge.cpu().numpy(), sched.cpu().numpy(), r["idx"].cpu().numpy()
+    S = H.capi.lib().moce_schedule_steps(k)
+    G = (E_r + 31) // 32
+    assert sorted(ge[ge >= 0].tolist()) == list(range(E_r))
+    sched = sched.reshape(G, S, 32).view(np.uint32)
+    conflicts = 0
+    for g in range(G):
+        for lane in range(32):
+            e = ge[g * 32 + lane]
+            ent = sched[g, :, lane]
+            slots = ent >> 16
+            chans = ent & 0xFFFF
+            valid = slots != 0xFFFF
+            if e < 0:
+                assert not valid.any()
+                continue
+            assert sorted(slots[valid].tolist()) == list(range(k))
+            assert np.all(idx[e, slots[valid]] == chans[valid])
+        for s in range(S):
+            banks = (sched[g, s, :] & 0xFFFF) % 32
+            conflicts += 32 - len(set(banks.tolist()))
+    # balanced groups of wide layers schedule with (almost) no bank conflicts
+    if balance and E_r >= 32 and C >= 256:
+        assert conflicts <= G * S * 32 // 50, conflicts
