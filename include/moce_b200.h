@@ -107,6 +107,23 @@ int moce_mix_scheduled(const void* x, int dtype, int64_t B, int64_t C,
                        void* y, float* T_out, void* stream);
 
 /*
+ * Pass 2 on the tensor cores, for bf16 / fp16 inputs with H*W <= 64,
+ * C <= 512 and k <= 64 (the 7x7 stage-4 maps): same inputs and outputs as
+ * moce_mix_scheduled but the routed experts are computed per sample as a
+ * dense product of the 128-expert weight tile (zero off the supports) with
+ * the staged X (tcgen05.mma, accumulator in tensor memory).  Weights are
+ * rounded to the input's 16-bit type before the product (fp32 accumulation).
+ * Waits inside the kernel are bounded; moce_tc_fault reads (and optionally
+ * clears) the flag a wait that ran out sets.
+ */
+int moce_mix_tc(const void* x, int dtype, int64_t B, int64_t C, int64_t HW,
+                const float* z, const int32_t* idx, const float* ln,
+                int64_t E_r, int64_t k, const float* gate_w,
+                const float* gate_b, float tmin_tau, float trange_tau,
+                void* y, float* T_out, void* stream);
+int moce_tc_fault(int* flag, int clear);
+
+/*
  * Global average pool: pooled[b,c] = mean_p X[b,c,p] (fp32 out).
  * Replaces moce_pool (moce_layer_cuda.cpp:8-10, moce_kernel.cu:849-861).
  * pooled has the dtype of X in the reference; here it is always fp32.

@@ -76,10 +76,40 @@ def forward_fast(x, r, gate_w, gate_b, tmin_tau, trange_tau, want_T=True):
     return y, z, T
 
 
+def tc_supported(x, k):
+    C, HW = x.shape[1], x.shape[2] * x.shape[3]
+    return x.dtype in (torch.bfloat16, torch.float16) and C <= 512 and HW <= 64 and 1 <= k <= 64 \
+        and (C * HW) % 8 == 0
+
+
+def forward_tc(x, r, gate_w, gate_b, tmin_tau, trange_tau, want_T=True):
+    """Tensor-core path through the C ABI: pass 1 (pool + residual), tcgen05 mix."""
+    B, C, H, W = x.shape
+    E_r, k = r["idx"].shape
+    y = torch.empty(B, E_r + 1, H, W, dtype=x.dtype, device=x.device)
+    z = torch.empty(B, C, dtype=torch.float32, device=x.device)
+    T = torch.empty(B, E_r, dtype=torch.float32, device=x.device) if want_T else None
+    call("moce_pool_residual", ptr(x), dtype_code(x), B, C, H * W, ptr(r["mask"]), ptr(r["meta"]), ptr(z), ptr(y),
+         E_r, stream_handle())
+    call("moce_mix_tc", ptr(x), dtype_code(x), B, C, H * W, ptr(z), ptr(r["idx"]), ptr(r["ln"]), E_r, k,
+         ptr(gate_w), ptr(gate_b), tmin_tau, trange_tau, ptr(y), ptr(T), stream_handle())
+    return y, z, T
+
+
+def tc_fault(clear=True):
+    import ctypes
+    flag = ctypes.c_int(0)
+    call("moce_tc_fault", ctypes.addressof(flag), 1 if clear else 0)
+    return flag.value
+
+
 def forward(x, L, gate_w, gate_b, k, tmin, tmax, tau, route=None, path="general", balance=True):
     """Eval-form forward through the C ABI: route build, then either the
     general two passes (pool + gate -> T, softmax + mix) or the fast path."""
     r = route or route_build(L, k, transposed=False)
+    if path == "tc":
+        y, z, T = forward_tc(x, r, gate_w, gate_b, tmin * tau, (tmax - tmin) * tau)
+        return y, dict(r, z=z, T=T)
     if path == "fast":
         r["group_expert"], r["sched"] = schedule_build(r["idx"], L.shape[1], balance)
         y, z, T = forward_fast(x, r, gate_w, gate_b, tmin * tau, (tmax - tmin) * tau)

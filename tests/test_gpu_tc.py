@@ -1,0 +1,77 @@
+"""GPU parity of the tensor-core mix (tcgen05) against the oracle.
+
+The tensor-core path rounds the softmax weights to the input's 16-bit type
+before the product; the bf16/fp16 tolerance (1e-2 relative against the fp32
+oracle on the rounded input) covers it.  Every case also checks that no
+bounded wait inside the kernel ran out.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import moce_oracle as O
+import capi_helpers as H
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def close(a, b, rtol, floor):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return bool(np.all(np.abs(a - b) <= rtol * np.abs(b) + floor * max(np.abs(b).max(), 1e-30)))
+
+
+def relerr(a, b):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float((np.abs(a - b) / np.maximum(np.abs(b), 1e-3 * max(np.abs(b).max(), 1e-30))).max())
+
+
+@pytest.mark.parametrize("B,C,H_,W_,E,k,dtype", [
+    (2, 64, 5, 5, 16, 4, torch.bfloat16),       # smallest: one K block, uncovered channels
+    (3, 32, 3, 5, 33, 8, torch.float16),        # C < 64 (K padding), odd pixels
+    (4, 512, 7, 7, 300, 32, torch.bfloat16),    # stage-4 widths, partial last expert tile
+    (2, 136, 3, 7, 140, 33, torch.bfloat16),    # C not a multiple of 64, k > 32
+    (2, 16, 1, 1, 2, 16, torch.float16),        # k == C, HW == 1
+    (2, 96, 8, 8, 129, 40, torch.bfloat16),     # HW == 64 exactly
+])
+def test_tc_mix_matches_oracle(B, C, H_, W_, E, k, dtype):
+    gen = torch.Generator().manual_seed(B * 100 + C + k)
+    X = torch.randn(B, C, H_, W_, generator=gen).abs()
+    L = torch.randn(E - 1, C, generator=gen)
+    gw = torch.rand(1, k, generator=gen) - 0.5
+    gb = torch.randn(1, generator=gen) * 0.1
+    x = X.to(DEV, dtype)
+    assert H.tc_supported(x, k)
+    H.tc_fault(clear=True)
+    y, st = H.forward(x, L.to(DEV), gw.to(DEV), gb.to(DEV), k, 0.1, 10.0, 1.0, path="tc")
+    torch.cuda.synchronize()
+    assert H.tc_fault() == 0
+    ref = O.forward(x.float().cpu().numpy(), L.numpy(), gw.numpy(), gb.numpy(), k, 0.1, 10.0, 1.0, mode="eval")
+    got = y.float().cpu().numpy()
+    assert close(got, ref, 1e-2, 1e-3), relerr(got, ref)
+    _, aux = O.forward(x.float().cpu().numpy(), L.numpy(), gw.numpy(), gb.numpy(), k, 0.1, 10.0, 1.0, mode="eval",
+                       return_aux=True)
+    assert close(st["T"].cpu().numpy(), aux["T"], 1e-5, 1e-6)
+
+
+def test_tc_mix_stage4_workload_against_scheduled_path():
+    """N=256, C=512, 7x7, E=2048, k=32 (bf16): the tensor-core and the
+    scheduled CUDA-core paths agree, and a subset matches the oracle."""
+    gen = torch.Generator().manual_seed(7)
+    B, C, E, k = 256, 512, 2048, 32
+    X = torch.randn(B, C, 7, 7, generator=gen).abs()
+    L = torch.randn(E - 1, C, generator=gen)
+    gw = torch.rand(1, k, generator=gen) - 0.5
+    gb = torch.zeros(1)
+    x = X.to(DEV, torch.bfloat16)
+    H.tc_fault(clear=True)
+    y_tc, _ = H.forward(x, L.to(DEV), gw.to(DEV), gb.to(DEV), k, 0.1, 10.0, 1.0, path="tc")
+    y_f, _ = H.forward(x, L.to(DEV), gw.to(DEV), gb.to(DEV), k, 0.1, 10.0, 1.0, path="fast")
+    torch.cuda.synchronize()
+    assert H.tc_fault() == 0
+    a, b = y_tc.float().cpu().numpy(), y_f.float().cpu().numpy()
+    assert close(a, b, 1e-2, 1e-3), relerr(a, b)
+    ref = O.forward(x[:4].float().cpu().numpy(), L.numpy(), gw.numpy(), gb.numpy(), k, 0.1, 10.0, 1.0, mode="eval")
+    assert close(a[:4], ref, 1e-2, 1e-3), relerr(a[:4], ref)
