@@ -107,18 +107,30 @@ int moce_mix_scheduled(const void* x, int dtype, int64_t B, int64_t C,
                        void* y, float* T_out, void* stream);
 
 /*
- * Pass 2 on the tensor cores, for bf16 / fp16 inputs with H*W <= 64,
- * C <= 512 and k <= 64 (the 7x7 stage-4 maps): same inputs and outputs as
- * moce_mix_scheduled but the routed experts are computed per sample as a
- * dense product of the 128-expert weight tile (zero off the supports) with
- * the staged X (tcgen05.mma, accumulator in tensor memory).  Weights are
+ * Tensor-core fast path, for bf16 / fp16 inputs with H*W <= 64, C <= 512 and
+ * k <= 64 (the 7x7 stage-4 maps).
+ *
+ * moce_pool_stage: pass 1 as moce_pool_residual, plus a copy of X in the
+ * tensor-core operand layout: xstage [B, Kp, 64] 16-bit, Kp = C rounded up to
+ * 64, each 128-byte channel row holding 64 zero-padded pixels in 16-byte
+ * units swizzled by (channel mod 8).  moce_tc_stage_bytes gives its size.
+ *
+ * moce_mix_tc: pass 2.  Same outputs as moce_mix_scheduled; the routed
+ * experts are computed per sample as a dense product of the 128-expert weight
+ * tile (zero off the supports) with the staged X (bulk copies into shared
+ * memory, tcgen05.mma with the accumulator in tensor memory).  Weights are
  * rounded to the input's 16-bit type before the product (fp32 accumulation).
  * Waits inside the kernel are bounded; moce_tc_fault reads (and optionally
  * clears) the flag a wait that ran out sets.
  */
-int moce_mix_tc(const void* x, int dtype, int64_t B, int64_t C, int64_t HW,
-                const float* z, const int32_t* idx, const float* ln,
-                int64_t E_r, int64_t k, const float* gate_w,
+size_t moce_tc_stage_bytes(int64_t B, int64_t C);
+int moce_pool_stage(const void* x, int dtype, int64_t B, int64_t C,
+                    int64_t HW, const int32_t* mask, const int32_t* meta,
+                    float* z, void* y, int64_t E_r, void* xstage,
+                    void* stream);
+int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C,
+                int64_t HW, const float* z, const int32_t* idx,
+                const float* ln, int64_t E_r, int64_t k, const float* gate_w,
                 const float* gate_b, float tmin_tau, float trange_tau,
                 void* y, float* T_out, void* stream);
 int moce_tc_fault(int* flag, int clear);

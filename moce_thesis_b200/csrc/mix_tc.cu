@@ -133,7 +133,7 @@ __device__ __forceinline__ uint32_t b_off(int c, int p) {
 }
 
 struct TcArgs {
-  const void* x;
+  const void* xstage;             // [B, Kp, 128 B] operand-layout copy of X (pass 1)
   void* y;
   const float* z;
   const int32_t* idx;
@@ -146,304 +146,322 @@ struct TcArgs {
   int n_tiles, n_bsplit;
 };
 
-// Row-thread helpers --------------------------------------------------------
+constexpr int kQ = 4;             // K quarters: pipeline stages of the operands
 
-// Gate, temperature and softmax weights of this thread's expert for sample b
-// (z of the sample in s_zb); weights returned in w[].
-template <int KMAX>
-__device__ __forceinline__ void row_weights(const int* ch, const float* lnr, int k, const float* s_gw,
-                                            const float* s_zb, float bias, float tmin_tau, float trange_tau,
-                                            float* w, float* t_out) {
-  float g = bias;
-#pragma unroll
-  for (int i = 0; i < KMAX; ++i)
-    if (i < k) g += s_gw[i] * s_zb[ch[i]];
-  const float t = temperature(g, tmin_tau, trange_tau, nullptr);
-  *t_out = t;
-  const float it = 1.0f / t;
-  float m = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < KMAX; ++i)
-    if (i < k) m = nan_max(m, lnr[i] * it);
-  float zs = 0.0f;
-#pragma unroll
-  for (int i = 0; i < KMAX; ++i) {
-    w[i] = (i < k) ? expf(lnr[i] * it - m) : 0.0f;
-    zs += w[i];
-  }
-  const float iz = 1.0f / zs;
-#pragma unroll
-  for (int i = 0; i < KMAX; ++i) w[i] *= iz;
+struct TcBars {
+  uint64_t full_b[kQ];            // B quarter landed (bulk copy, tx bytes)
+  uint64_t mma_q[kQ];             // MMAs of a quarter done: A and B quarter free
+  uint64_t a_full[kQ];            // rows wrote the A quarter (128 arrivals)
+  uint64_t d_full[2];             // accumulator buffer complete
+  uint64_t d_empty[2];            // accumulator buffer drained (128 arrivals)
+  uint32_t tmem;
+  int abort;
+};
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Flat [C, HW] sample: 16-byte chunks q = tid + u * nthreads, u < XCAP.
-template <int XCAP>
-__device__ __forceinline__ void x_prefetch(const int4* src, int n16, int tid, int nthreads, int4* r) {
-#pragma unroll
-  for (int u = 0; u < XCAP; ++u) {
-    const int q = tid + u * nthreads;
-    if (q < n16) r[u] = __ldg(src + q);
-  }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
-template <typename T, int XCAP>
-__device__ __forceinline__ void x_scatter(unsigned char* sB, const int4* r, int n16, int HW, int tid, int nthreads) {
-  constexpr int V = 16 / sizeof(T);
-#pragma unroll
-  for (int u = 0; u < XCAP; ++u) {
-    const int q = tid + u * nthreads;
-    if (q < n16) {
-      const T* v = reinterpret_cast<const T*>(&r[u]);
-      const int f = q * V;
-      int c = f / HW;
-      int p = f - c * HW;
-#pragma unroll
-      for (int j = 0; j < V; ++j) {
-        *reinterpret_cast<T*>(sB + b_off(c, p)) = v[j];
-        if (++p == HW) {
-          p = 0;
-          ++c;
-        }
-      }
-    }
+// Bounded wait that also gives up when another role has aborted.
+__device__ __forceinline__ bool mbar_wait_abort(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  const uint32_t a = smem_u32(bar);
+  for (long long it = 0; it < kSpinLimit; ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((it & 1023) == 1023 && *abort) return false;
   }
+  *abort = 1;
+  atomicExch(&g_tc_fault, 1);
+  return false;
 }
 
-// 256 threads: threads 0..127 own expert rows (weights, accumulator drain,
-// output), all threads stage X, thread 128 issues the MMAs.  Software
-// pipeline per sample b:
-//   MMA(b) issued  ->  rows write out sample b-1, everyone prefetches X(b+1)
-//   into registers and the rows compute the weights of b+1  ->  wait MMA(b)
-//   -> rows drain D(b) into registers  ->  X(b+1), weights(b+1) stored into
-//   the operand buffers  ->  MMA(b+1) ...
-template <typename T, int KMAX, int XCAP>
-__global__ void __launch_bounds__(2 * kTcThreads, 1) mix_tc_kernel(TcArgs a) {
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_s2g(void* dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void row_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// 160 threads: warps 0..3 own the 128 expert rows of the tile (softmax
+// weights into A, accumulator drain, output), lane 0 of warp 4 moves the
+// operands (bulk copies of the staged X quarters) and issues the MMAs.
+template <typename T, int KMAX>
+__global__ void __launch_bounds__(160, 1) mix_tc_kernel(TcArgs a) {
   extern __shared__ unsigned char s_dyn[];
   unsigned char* base =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(s_dyn) + 1023) & ~uintptr_t(1023));
   const int C = a.C, HW = a.HW, k = a.k, Kp = a.Kp, E_r = a.E_r;
-  unsigned char* sA = base;                                  // 128 x Kp: Kp * 256 B
-  unsigned char* sB = base + (size_t)Kp * 256;               // Kp x 64: Kp * 128 B
-  T* stg = reinterpret_cast<T*>(sB + (size_t)Kp * 128);      // 128 x 64 output staging
+  const int Kq = Kp / kQ;                                     // channels per quarter (multiple of 16)
+  // kQ stages pipeline the X operand (bulk copies); the weight operand is
+  // rewritten per sample after the sample's last MMA (mma_q[kQ - 1])
+  unsigned char* sA = base;                                   // 128 x Kp : Kp * 256 B
+  unsigned char* sB = base + (size_t)Kp * 256;                // Kp x 64  : Kp * 128 B
+  T* stg = reinterpret_cast<T*>(sB + (size_t)Kp * 128);       // 128 x HW output block
   float* s_z = reinterpret_cast<float*>(sB + (size_t)Kp * 128 + 128 * kTcN * sizeof(T));  // 2 x Kp
   float* s_gw = s_z + 2 * Kp;
-  uint64_t* s_bar = reinterpret_cast<uint64_t*>(s_gw + KMAX);
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(s_bar + 1);
-  constexpr int NT = 2 * kTcThreads;
+  TcBars* bars = reinterpret_cast<TcBars*>(s_gw + KMAX);
+  volatile int* abort = &bars->abort;
 
   const int tid = threadIdx.x, warp = tid >> 5;
-  const bool row_thread = tid < kTcThreads;
   const int tile = blockIdx.x % a.n_tiles, bsplit = blockIdx.x / a.n_tiles;
   const int e0 = tile * 128;
   const int rows = min(128, E_r - e0);
-  const int e = e0 + tid;
-  const bool has_row = row_thread && tid < rows;
-  const int n16 = C * HW * (int)sizeof(T) / 16;
+  const int b0 = (int)((long long)bsplit * a.B / a.n_bsplit);
+  const int b1 = (int)((long long)(bsplit + 1) * a.B / a.n_bsplit);
+  const int nb = b1 - b0;
+  const int E = E_r + 1;
 
-  {
-    int4* p = reinterpret_cast<int4*>(sA);
-    for (int q = tid; q < Kp * 256 / 16; q += NT) p[q] = make_int4(0, 0, 0, 0);
-    int4* pb = reinterpret_cast<int4*>(sB);
-    for (int q = tid; q < Kp * 128 / 16; q += NT) pb[q] = make_int4(0, 0, 0, 0);
-  }
-  for (int i = tid; i < k; i += NT) s_gw[i] = a.gate_w[i];
+  for (int q = tid; q < Kp * 256 / 16; q += blockDim.x) reinterpret_cast<int4*>(sA)[q] = make_int4(0, 0, 0, 0);
+  for (int i = tid; i < k; i += blockDim.x) s_gw[i] = a.gate_w[i];
   if (tid == 0) {
-    mbar_init(s_bar, 1);
+    for (int q = 0; q < kQ; ++q) {
+      mbar_init(&bars->full_b[q], 1);
+      mbar_init(&bars->mma_q[q], 1);
+      mbar_init(&bars->a_full[q], 128);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->d_full[s], 1);
+      mbar_init(&bars->d_empty[s], 128);
+    }
+    bars->abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(s_tmem)),
-                 "r"(kTcN));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&bars->tmem)),
+                 "r"(2 * kTcN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
-  int ch[KMAX];
-  float lnr[KMAX];
-#pragma unroll
-  for (int i = 0; i < KMAX; ++i) {
-    ch[i] = 0;
-    lnr[i] = 0.0f;
-    if (i < k && has_row) {
-      ch[i] = a.idx[(size_t)e * k + i];
-      lnr[i] = a.ln[(size_t)e * k + i];
-    }
-  }
-  const float bias = a.gate_b[0];
-  const uint32_t idesc = umma_idesc(DTypeOf<T>::value == MOCE_BF16 ? 1 : 0, 128, kTcN);
-  const uint32_t aA = smem_u32(sA), aB = smem_u32(sB);
-  const int E = E_r + 1;
-  const int b0 = (int)((long long)bsplit * a.B / a.n_bsplit);
-  const int b1 = (int)((long long)(bsplit + 1) * a.B / a.n_bsplit);
-  const T* xg = static_cast<const T*>(a.x);
-  T* yg = static_cast<T*>(a.y);
-  const size_t xs = (size_t)C * HW;
-
-  // ---- operands of the first sample
-  int4 xr[XCAP];
-  float w[KMAX];
-  float v[kTcN];
-  if (b0 < b1) {
-    x_prefetch<XCAP>(reinterpret_cast<const int4*>(xg + (size_t)b0 * xs), n16, tid, NT, xr);
-    for (int c = tid; c < C; c += NT) s_z[c] = a.z[(size_t)b0 * C + c];
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *s_tmem;
-  if (b0 < b1) {
-    x_scatter<T, XCAP>(sB, xr, n16, HW, tid, NT);
-    if (has_row) {
-      float t;
-      row_weights<KMAX>(ch, lnr, k, s_gw, s_z, bias, a.tmin_tau, a.trange_tau, w, &t);
-      if (a.T_out) a.T_out[(size_t)b0 * E_r + e] = t;
-#pragma unroll
-      for (int i = 0; i < KMAX; ++i)
-        if (i < k) *reinterpret_cast<T*>(sA + a_off(tid, ch[i])) = from_f<T>(w[i]);
-    }
-  }
-  uint32_t phase = 0;
-  bool ok = true;
-  for (int b = b0; b < b1; ++b) {
-    const bool next = b + 1 < b1;
-    proxy_fence_smem();
-    tc_fence_before();
-    __syncthreads();                                // S1: operands of b are in place
-    tc_fence_after();
-    if (tid == kTcThreads) {
-      for (int j = 0; j < Kp / 16; ++j) {
-        const uint64_t da = umma_desc(aA + (uint32_t)((j >> 2) * 16384 + (j & 3) * 32), 16, 1024);
-        const uint64_t db = umma_desc(aB + (uint32_t)(j * 2048), (uint32_t)Kp * 128, 1024);
-        umma_f16(tmem, da, db, idesc, j > 0 ? 1u : 0u);
-      }
-      umma_commit(s_bar);
-    }
-    // ---- while MMA(b) runs: write out b-1, prefetch X(b+1), z(b+1)
-    if (row_thread && b > b0) {
-      if (has_row) {
-#pragma unroll
-        for (int p = 0; p < kTcN; ++p)
-          if (p < HW) stg[tid * HW + p] = from_f<T>(v[p]);
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      T* dst = yg + ((size_t)(b - 1) * E + e0) * HW;
-      const int n = rows * HW;
-      if (((((uintptr_t)dst) | (size_t)n * sizeof(T)) & 15) == 0) {
-        const int4* sp = reinterpret_cast<const int4*>(stg);
-        int4* dp = reinterpret_cast<int4*>(dst);
-        for (int q = tid; q < n * (int)sizeof(T) / 16; q += kTcThreads) dp[q] = sp[q];
-      } else {
-        for (int q = tid; q < n; q += kTcThreads) dst[q] = stg[q];
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-    }
-    if (next) {
-      x_prefetch<XCAP>(reinterpret_cast<const int4*>(xg + (size_t)(b + 1) * xs), n16, tid, NT, xr);
-      float* s_zn = s_z + ((b + 1 - b0) & 1) * Kp;
-      for (int c = tid; c < C; c += NT) s_zn[c] = a.z[(size_t)(b + 1) * C + c];
-    }
-    __syncthreads();                                // S2: z(b+1) visible
-    if (next && has_row) {
-      float t;
-      row_weights<KMAX>(ch, lnr, k, s_gw, s_z + ((b + 1 - b0) & 1) * Kp, bias, a.tmin_tau, a.trange_tau, w, &t);
-      if (a.T_out) a.T_out[(size_t)(b + 1) * E_r + e] = t;
-    }
-    // ---- MMA(b) done -> drain D, then refill the operands with b+1
-    const bool waited = mbar_wait(s_bar, phase);
-    if (!__syncthreads_and(waited)) {
-      ok = false;
-      if (tid == 0) atomicExch(&g_tc_fault, 1);
-      break;
-    }
-    phase ^= 1u;
-    tc_fence_after();
-    if (row_thread) tmem_ld64(tmem + ((uint32_t)(warp * 32) << 16), v);
-    if (next) {
-      x_scatter<T, XCAP>(sB, xr, n16, HW, tid, NT);
-      if (has_row) {
-#pragma unroll
-        for (int i = 0; i < KMAX; ++i)
-          if (i < k) *reinterpret_cast<T*>(sA + a_off(tid, ch[i])) = from_f<T>(w[i]);
+  const uint32_t tmem = bars->tmem;
+
+  if (warp == 4) {
+    // ===================== operand mover + MMA issuer (one thread)
+    if (tid == 128) {
+      const uint32_t idesc = umma_idesc(DTypeOf<T>::value == MOCE_BF16 ? 1 : 0, 128, kTcN);
+      const uint32_t aA = smem_u32(sA), aB = smem_u32(sB);
+      const unsigned char* xs = static_cast<const unsigned char*>(a.xstage);
+      const uint32_t qbytes = (uint32_t)Kq * 128;
+      const uint64_t da0 = umma_desc(aA, 16, 1024);
+      const uint64_t db0 = umma_desc(aB, (uint32_t)Kp * 128, 1024);
+      bool run = nb > 0;
+      if (run)
+        for (int q = 0; q < kQ; ++q) {
+          mbar_expect_tx(&bars->full_b[q], qbytes);
+          bulk_g2s(aB + q * qbytes, xs + (size_t)b0 * Kp * 128 + (size_t)q * qbytes, qbytes, &bars->full_b[q]);
+        }
+      for (int i = 0; i < nb && run; ++i) {
+        const int s = i & 1;
+        if (i >= 2 && !mbar_wait_abort(&bars->d_empty[s], ((i - 2) >> 1) & 1, abort)) break;
+        const uint32_t d = tmem + (uint32_t)(s * kTcN);
+        for (int q = 0; q < kQ && run; ++q) {
+          if (!mbar_wait_abort(&bars->full_b[q], i & 1, abort) || !mbar_wait_abort(&bars->a_full[q], i & 1, abort)) {
+            run = false;
+            break;
+          }
+          tc_fence_after();
+          for (int j = q * Kq / 16; j < (q + 1) * Kq / 16; ++j) {
+            // start-address fields advance in 16-byte units (no carry: shared
+            // addresses are below 2^18)
+            const uint64_t da = da0 + (uint64_t)(((j >> 2) * 16384 + (j & 3) * 32) >> 4);
+            const uint64_t db = db0 + (uint64_t)(j * 128);
+            umma_f16(d, da, db, idesc, j > 0 ? 1u : 0u);
+          }
+          umma_commit(&bars->mma_q[q]);
+        }
+        if (!run) break;
+        umma_commit(&bars->d_full[s]);
+        if (i + 1 < nb) {
+          for (int q = 0; q < kQ; ++q) {
+            if (!mbar_wait_abort(&bars->mma_q[q], i & 1, abort)) {
+              run = false;
+              break;
+            }
+            mbar_expect_tx(&bars->full_b[q], qbytes);
+            bulk_g2s(aB + q * qbytes, xs + (size_t)(b0 + i + 1) * Kp * 128 + (size_t)q * qbytes, qbytes,
+                     &bars->full_b[q]);
+          }
+        }
       }
     }
-    tc_fence_before();
-  }
-  // ---- write out the last sample
-  if (ok && b0 < b1 && row_thread) {
-    if (has_row) {
+  } else {
+    // ===================== expert rows: weights -> A, accumulator -> Y
+    const int e = e0 + tid;
+    const bool has_row = tid < rows;
+    int ch[KMAX];
+    float ln2[KMAX];
+    float mx2 = -INFINITY;
 #pragma unroll
-      for (int p = 0; p < kTcN; ++p)
-        if (p < HW) stg[tid * HW + p] = from_f<T>(v[p]);
+    for (int i = 0; i < KMAX; ++i) {
+      ch[i] = 0;
+      ln2[i] = -INFINITY;
+      if (i < k && has_row) {
+        ch[i] = a.idx[(size_t)e * k + i];
+        ln2[i] = a.ln[(size_t)e * k + i] * 1.4426950408889634f;   // log2(e)
+        mx2 = nan_max(mx2, ln2[i]);
+      }
     }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    T* dst = yg + ((size_t)(b1 - 1) * E + e0) * HW;
-    const int n = rows * HW;
-    if (((((uintptr_t)dst) | (size_t)n * sizeof(T)) & 15) == 0) {
-      const int4* sp = reinterpret_cast<const int4*>(stg);
-      int4* dp = reinterpret_cast<int4*>(dst);
-      for (int q = tid; q < n * (int)sizeof(T) / 16; q += kTcThreads) dp[q] = sp[q];
-    } else {
-      for (int q = tid; q < n; q += kTcThreads) dst[q] = stg[q];
+    const float bias = a.gate_b[0];
+    T* yg = static_cast<T*>(a.y);
+    float w[KMAX];
+    constexpr int ZPT = 4;                           // z values per thread (C <= 512)
+    float zr[ZPT];
+#pragma unroll
+    for (int u = 0; u < ZPT; ++u) {
+      const int c = tid + u * 128;
+      zr[u] = (nb > 0 && c < C) ? a.z[(size_t)b0 * C + c] : 0.0f;
     }
+    for (int i = 0; i <= nb; ++i) {
+      if (i < nb) {
+        const int b = b0 + i;
+        float* szb = s_z + (i & 1) * Kp;
+#pragma unroll
+        for (int u = 0; u < ZPT; ++u)
+          if (tid + u * 128 < C) szb[tid + u * 128] = zr[u];
+        row_bar();
+        if (i + 1 < nb) {
+#pragma unroll
+          for (int u = 0; u < ZPT; ++u) {
+            const int c = tid + u * 128;
+            if (c < C) zr[u] = a.z[(size_t)(b + 1) * C + c];
+          }
+        }
+        if (has_row) {
+          float g = bias;
+#pragma unroll
+          for (int j = 0; j < KMAX; ++j)
+            if (j < k) g += s_gw[j] * szb[ch[j]];
+          const float t = temperature(g, a.tmin_tau, a.trange_tau, nullptr);
+          if (a.T_out) a.T_out[(size_t)b * E_r + e] = t;
+          const float it = 1.0f / t;
+          const float m2 = mx2 * it;
+          float zs = 0.0f;
+#pragma unroll
+          for (int j = 0; j < KMAX; ++j) {
+            w[j] = exp2f(ln2[j] * it - m2);
+            zs += w[j];
+          }
+          const float iz = 1.0f / zs;
+#pragma unroll
+          for (int j = 0; j < KMAX; ++j) w[j] *= iz;
+        }
+        // A is rewritten once the previous sample's MMAs are all done; one
+        // proxy fence makes the new weights visible to the tensor cores
+        if (i >= 1 && !mbar_wait_abort(&bars->mma_q[kQ - 1], (i - 1) & 1, abort)) break;
+        if (has_row) {
+#pragma unroll
+          for (int j = 0; j < KMAX; ++j)
+            if (j < k) *reinterpret_cast<T*>(sA + a_off(tid, ch[j])) = from_f<T>(w[j]);
+        }
+        proxy_fence_smem();
+        for (int q = 0; q < kQ; ++q) mbar_arrive(&bars->a_full[q]);
+      }
+      if (i >= 1) {
+        // drain sample i-1
+        const int j = i - 1, s = j & 1;
+        if (!mbar_wait_abort(&bars->d_full[s], (j >> 1) & 1, abort)) break;
+        tc_fence_after();
+        float v[kTcN];
+        tmem_ld64(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(s * kTcN), v);
+        tc_fence_before();
+        mbar_arrive(&bars->d_empty[s]);
+        if (tid == 0) bulk_wait_read();               // previous block left the staging area
+        row_bar();
+        if (has_row) {
+#pragma unroll
+          for (int p = 0; p < kTcN; ++p)
+            if (p < HW) stg[tid * HW + p] = from_f<T>(v[p]);
+        }
+        proxy_fence_smem();
+        row_bar();
+        T* dst = yg + ((size_t)(b0 + j) * E + e0) * HW;
+        const uint32_t nbytes = (uint32_t)(rows * HW * sizeof(T));
+        if (((((uintptr_t)dst) | nbytes) & 15) == 0) {
+          if (tid == 0) bulk_s2g(dst, smem_u32(stg), nbytes);
+        } else {
+          for (int q = tid; q < rows * HW; q += 128) dst[q] = stg[q];
+          row_bar();
+        }
+      }
+    }
+    if (tid == 0) bulk_wait_all();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kTcN));
 }
 
 }  // namespace
 
 int tc_supported(int dtype, int64_t C, int64_t HW, int64_t k) {
-  // whole sample prefetched as 16-byte chunks: C*HW*2 a multiple of 16 and
-  // at most 16 chunks per thread
-  return (dtype == MOCE_BF16 || dtype == MOCE_F16) && HW >= 1 && HW <= kTcN && k <= 64 && C <= 512 &&
-         (C * HW) % 8 == 0 && C * HW * 2 / 16 <= 16 * 2 * kTcThreads;
+  return (dtype == MOCE_BF16 || dtype == MOCE_F16) && HW >= 1 && HW <= kTcN && k <= 64 && C <= 512;
 }
 
 }  // namespace moce
 
 using namespace moce;
 
-extern "C" int moce_mix_tc(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
+extern "C" size_t moce_tc_stage_bytes(int64_t B, int64_t C) {
+  return (size_t)B * (size_t)((C + 63) / 64 * 64) * 128;
+}
+
+extern "C" int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
                            const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
                            const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out,
                            void* stream) {
   if (B == 0) return MOCE_OK;
-  MOCE_REQUIRE(x && z && idx && ln && gate_w && gate_b && y, MOCE_ERR_INVALID, "moce_mix_tc: null pointer argument");
+  MOCE_REQUIRE(xstage && z && idx && ln && gate_w && gate_b && y, MOCE_ERR_INVALID,
+               "moce_mix_tc: null pointer argument");
   MOCE_REQUIRE(B > 0 && C >= 1 && HW >= 1 && E_r >= 1 && k >= 1 && k <= C, MOCE_ERR_INVALID,
                "moce_mix_tc: invalid shape");
   MOCE_REQUIRE(tc_supported(dtype, C, HW, k), MOCE_ERR_UNSUPPORTED,
-               "moce_mix_tc: needs bf16/fp16, H*W <= 64, C <= 512, k <= 64, C*H*W a multiple of 8");
-  MOCE_REQUIRE(((uintptr_t)x & 15) == 0, MOCE_ERR_UNSUPPORTED, "moce_mix_tc: x must be 16-byte aligned");
+               "moce_mix_tc: needs bf16/fp16, H*W <= 64, C <= 512, k <= 64");
+  MOCE_REQUIRE(((uintptr_t)xstage & 15) == 0, MOCE_ERR_INVALID, "moce_mix_tc: xstage must be 16-byte aligned");
   MOCE_REQUIRE(B < 65536 && (E_r + 1) * HW < (int64_t)1 << 31, MOCE_ERR_UNSUPPORTED, "moce_mix_tc: shape too large");
   const int Kp = (int)((C + 63) / 64 * 64);
   const int KMAX = k <= 16 ? 16 : k <= 32 ? 32 : 64;
   const size_t smem = 1024 + (size_t)Kp * 256 + (size_t)Kp * 128 + (size_t)128 * 64 * 2 + (size_t)Kp * 8 +
-                      (size_t)KMAX * 4 + 16;
+                      (size_t)KMAX * 4 + sizeof(TcBars) + 16;
   const int n_tiles = (int)((E_r + 127) / 128);
   int n_bsplit = num_sms() / n_tiles;
   if (n_bsplit < 1) n_bsplit = 1;
   if (n_bsplit > B) n_bsplit = (int)B;
-  TcArgs a{x, y, z, idx, ln, gate_w, gate_b, T_out, tmin_tau, trange_tau,
+  TcArgs a{xstage, y, z, idx, ln, gate_w, gate_b, T_out, tmin_tau, trange_tau,
            (int)B, (int)C, (int)HW, (int)E_r, (int)k, Kp, n_tiles, n_bsplit};
   return dispatch_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
     if constexpr (sizeof(T) != 2) {
       return set_error(MOCE_ERR_UNSUPPORTED, "moce_mix_tc: 16-bit inputs only");
     } else {
-      const int n16 = (int)(C * HW * 2 / 16);
-      const int xcap = (n16 + 2 * kTcThreads - 1) / (2 * kTcThreads);   // 16-byte chunks per thread
-      void (*kern)(TcArgs) = nullptr;
-      if (xcap <= 8) {
-        kern = KMAX == 16 ? mix_tc_kernel<T, 16, 8> : KMAX == 32 ? mix_tc_kernel<T, 32, 8> : mix_tc_kernel<T, 64, 8>;
-      } else if (xcap <= 13) {
-        kern = KMAX == 16 ? mix_tc_kernel<T, 16, 13> : KMAX == 32 ? mix_tc_kernel<T, 32, 13> : mix_tc_kernel<T, 64, 13>;
-      } else {
-        kern = KMAX == 16 ? mix_tc_kernel<T, 16, 16> : KMAX == 32 ? mix_tc_kernel<T, 32, 16> : mix_tc_kernel<T, 64, 16>;
-      }
+      void (*kern)(TcArgs) = KMAX == 16 ? mix_tc_kernel<T, 16> : KMAX == 32 ? mix_tc_kernel<T, 32>
+                                                                            : mix_tc_kernel<T, 64>;
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return set_error(MOCE_ERR_CUDA, "moce_mix_tc: cannot reserve %zu B shared memory", smem);
-      kern<<<(unsigned)(n_tiles * n_bsplit), 2 * kTcThreads, smem, (cudaStream_t)stream>>>(a);
+      kern<<<(unsigned)(n_tiles * n_bsplit), 160, smem, (cudaStream_t)stream>>>(a);
       return check_launch("mix_tc_kernel");
     }
   });

@@ -32,7 +32,7 @@ def relerr(a, b):
     (2, 64, 5, 5, 16, 4, torch.bfloat16),       # smallest: one K block, uncovered channels
     (3, 32, 3, 5, 33, 8, torch.float16),        # C < 64 (K padding), odd pixels
     (4, 512, 7, 7, 300, 32, torch.bfloat16),    # stage-4 widths, partial last expert tile
-    (2, 136, 3, 7, 140, 33, torch.bfloat16),    # C not a multiple of 64, k > 32
+    (2, 130, 3, 7, 140, 33, torch.bfloat16),    # ragged C (not a multiple of 8), k > 32
     (2, 16, 1, 1, 2, 16, torch.float16),        # k == C, HW == 1
     (2, 96, 8, 8, 129, 40, torch.bfloat16),     # HW == 64 exactly
 ])
