@@ -163,9 +163,10 @@ def run_ours(args):
     xs = [x0] + [(x0 * (1.0 + 0.001 * i)).contiguous() for i in range(1, nsets)]
     ys = [torch.empty(B, E, H, W, device=dev, dtype=dtype) for _ in range(nsets)]
 
+    use_tc = bool(mc.tc_supported(x0, K))
+
     def step(i):
-        return mc.forward_scheduled(xs[i % nsets], r.ln, r.mask, r.meta, r.group_expert, r.sched, gwf, gbf,
-                                    tmin_tau, trange_tau, False, ys[i % nsets])
+        return r.forward(xs[i % nsets], gwf, gbf, tmin_tau, trange_tau, False, ys[i % nsets])
 
     for i in range(args.warmup):
         step(i)
@@ -199,14 +200,28 @@ def run_ours(args):
     zs = [torch.empty(B, C, device=dev) for _ in range(nsets)]
     reps = max(args.steps, 20)
 
-    def pass1(i):
-        capi.call("moce_pool_residual", xs[i % nsets].data_ptr(), dcode, B, C, H * W, r.mask.data_ptr(),
-                  r.meta.data_ptr(), zs[i % nsets].data_ptr(), ys[i % nsets].data_ptr(), E - 1, sh)
+    if use_tc:
+        nst = capi.lib().moce_tc_stage_bytes(B, C)
+        sts = [torch.empty(nst, dtype=torch.uint8, device=dev) for _ in range(nsets)]
 
-    def pass2(i):
-        capi.call("moce_mix_scheduled", xs[i % nsets].data_ptr(), dcode, B, C, H * W, zs[i % nsets].data_ptr(),
-                  r.ln.data_ptr(), E - 1, K, r.group_expert.data_ptr(), r.sched.data_ptr(), gwf.data_ptr(),
-                  gbf.data_ptr(), tmin_tau, trange_tau, ys[i % nsets].data_ptr(), None, sh)
+        def pass1(i):
+            capi.call("moce_pool_stage", xs[i % nsets].data_ptr(), dcode, B, C, H * W, r.mask.data_ptr(),
+                      r.meta.data_ptr(), zs[i % nsets].data_ptr(), ys[i % nsets].data_ptr(), E - 1,
+                      sts[i % nsets].data_ptr(), sh)
+
+        def pass2(i):
+            capi.call("moce_mix_tc", sts[i % nsets].data_ptr(), dcode, B, C, H * W, zs[i % nsets].data_ptr(),
+                      r.idx.data_ptr(), r.ln.data_ptr(), E - 1, K, gwf.data_ptr(), gbf.data_ptr(), tmin_tau,
+                      trange_tau, ys[i % nsets].data_ptr(), None, sh)
+    else:
+        def pass1(i):
+            capi.call("moce_pool_residual", xs[i % nsets].data_ptr(), dcode, B, C, H * W, r.mask.data_ptr(),
+                      r.meta.data_ptr(), zs[i % nsets].data_ptr(), ys[i % nsets].data_ptr(), E - 1, sh)
+
+        def pass2(i):
+            capi.call("moce_mix_scheduled", xs[i % nsets].data_ptr(), dcode, B, C, H * W, zs[i % nsets].data_ptr(),
+                      r.ln.data_ptr(), E - 1, K, r.group_expert.data_ptr(), r.sched.data_ptr(), gwf.data_ptr(),
+                      gbf.data_ptr(), tmin_tau, trange_tau, ys[i % nsets].data_ptr(), None, sh)
 
     def time_loop(fn):
         for i in range(3):
@@ -222,7 +237,10 @@ def run_ours(args):
 
     gate_ms = time_loop(pass1)
     mix_ms = time_loop(pass2)
-    mix_bytes = xb + B * (E - 1) * H * W * esize + B * C * 4 + r.sched.numel() * 4 + (E - 1) * K * 4
+    # algorithmic bytes of pass 2: its X operand in, routed Y out, z in,
+    # supports (int32) and normalised logits (fp32)
+    x_in = capi.lib().moce_tc_stage_bytes(B, C) if use_tc else xb
+    mix_bytes = x_in + B * (E - 1) * H * W * esize + B * C * 4 + (E - 1) * K * 8
 
     # end to end through the public API: pinned host X -> layer -> host Y
     xh = x0.cpu().pin_memory()
@@ -269,10 +287,12 @@ def run_ours(args):
         "config": {"workload": WORKLOAD, "global_batch": B * world, "C": C, "HW": H * W, "E": E, "k": K,
                    "parallelism": f"batch-sharded x{world}, no data-path collective",
                    "l2": f"{nsets} rotating X/Y sets ({nsets * (xb + yb) / 2**20:.0f} MiB > 126 MiB L2)"},
-        "kernels_ms": {"pass1_pool_residual": round(gate_ms, 5), "pass2_mix_scheduled": round(mix_ms, 5)},
+        "kernels_ms": {("pass1_pool_stage" if use_tc else "pass1_pool_residual"): round(gate_ms, 5),
+                       ("pass2_mix_tc" if use_tc else "pass2_mix_scheduled"): round(mix_ms, 5)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "kernel": "mix_sched_kernel (pass 2)", "peak_kind": f"{peak_kind} copy bandwidth"},
+                     "kernel": "mix_tc_kernel (pass 2, tcgen05)" if use_tc else "mix_sched_kernel (pass 2)",
+                     "peak_kind": f"{peak_kind} copy bandwidth"},
         "e2e": {"value": round(e2e, 3), "unit": "GB/s", "h2d_bytes_per_step": xb, "d2h_bytes_per_step": yb,
                 "api": "moce_thesis_b200.MoCE.forward_eval, pinned host X in, host Y out"},
         "gpu_launches": 2 * args.steps,

@@ -49,15 +49,24 @@ class _Route:
         if m.schedule_supported(int(k)):
             self.group_expert, self.sched = m.schedule_build(self.idx, L.shape[1], bool(balance))
 
-    def forward(self, x, gate_w, gate_b, tmin_tau, trange_tau, want_T=False):
-        """Both forward passes; returns (y, z, T).  T is None unless wanted."""
+    def forward(self, x, gate_w, gate_b, tmin_tau, trange_tau, want_T=False, out=None):
+        """Both forward passes; returns (y, z, T).  T is None unless wanted.
+
+        bf16/fp16 inputs with H*W <= 64 and C <= 512 run the tensor-core
+        mix; other shapes the scheduled CUDA-core mix (k <= 44) or the general
+        two passes.
+        """
         m = native()
+        if m.tc_supported(x, self.idx.shape[1]):
+            y, z, T = m.forward_tc(x, self.idx, self.ln, self.mask, self.meta, gate_w, gate_b, float(tmin_tau),
+                                   float(trange_tau), bool(want_T), out)
+            return y, z, (T if want_T else None)
         if self.sched is not None:
             y, z, T = m.forward_scheduled(x, self.ln, self.mask, self.meta, self.group_expert, self.sched, gate_w,
-                                          gate_b, float(tmin_tau), float(trange_tau), bool(want_T))
+                                          gate_b, float(tmin_tau), float(trange_tau), bool(want_T), out)
             return y, z, (T if want_T else None)
         z, T = m.gate_temperature(x, self.idx, gate_w, gate_b, float(tmin_tau), float(trange_tau))
-        return m.mix(x, self.idx, self.ln, T, self.mask), z, T
+        return m.mix(x, self.idx, self.ln, T, self.mask, out), z, T
 
 
 class MoCEFunction(torch.autograd.Function):
