@@ -202,6 +202,31 @@ int moce_gate_route(const void* x, int dtype, const float* pooled,
                     size_t workspace_bytes, void* stream);
 
 /*
+ * moce_gate_route without a workspace argument.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory at the
+ * call (for example a plugin inside an inference engine that gets a fixed
+ * memory budget and no allocator, or a latency-critical path that cannot
+ * take cudaMalloc's device-wide synchronisation).  Same arguments and results
+ * as moce_gate_route minus the workspace; the scratch it needs comes from a
+ * fixed array inside the library of moce_noalloc_scratch_bytes() bytes
+ * (4 MiB), which every GPU that loads the library holds until exit.  Shapes
+ * needing more (moce_gate_route_workspace_bytes) fail with
+ * MOCE_ERR_UNSUPPORTED.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress) with that device current; make that
+ * first call before any stream capture.  All calls share the array: calls
+ * that overlap on the GPU race and must be serialised by the caller.  It
+ * never calls cudaMalloc or cudaFree.
+ */
+size_t moce_noalloc_scratch_bytes(void);
+int moce_gate_route_noalloc(const void* x, int dtype, const float* pooled,
+                            const void* indices, int index_bits,
+                            const float* logits_norm, const float* gate_w,
+                            const float* gate_b, const int32_t* mask,
+                            float temp_min, float temp_max, float tau,
+                            void* y, int64_t B, int64_t C, int64_t HW,
+                            int64_t E_r, int64_t K, void* stream);
+
+/*
  * Backward of the layer (no reference kernel: the reference trains through
  * autograd over MoCE.forward_train, MoCE.py:153-201).  Given dY [B, E, HW]
  * (dtype of X), the forward's z and T, and the route cache (including the

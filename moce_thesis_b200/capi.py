@@ -44,6 +44,9 @@ SIGNATURES = {
     "moce_gate_route_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "moce_gate_route": (_i32, [_p, _i32, _p, _p, _i32, _p, _p, _p, _p, _f32, _f32, _f32, _p, _i64, _i64, _i64,
                                _i64, _i64, _p, _sz, _p]),
+    "moce_noalloc_scratch_bytes": (_sz, []),
+    "moce_gate_route_noalloc": (_i32, [_p, _i32, _p, _p, _i32, _p, _p, _p, _p, _f32, _f32, _f32, _p, _i64, _i64,
+                                       _i64, _i64, _i64, _p]),
     "moce_backward_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),
     "moce_backward": (_i32, [_p, _p, _i32, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _p, _p,
                              _f32, _f32, _p, _p, _p, _p, _p, _p, _p, _sz, _p]),
