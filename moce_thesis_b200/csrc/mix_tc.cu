@@ -15,15 +15,21 @@
 //   B  MN-major: 8-channel groups of 1024 B, each channel row = 64 pixels x 2 B
 // The CTA owns one expert tile for a range of samples.  The sparsity pattern
 // of A is fixed, so A is zeroed once and each sample rewrites only its k
-// nonzeros per row.  One thread per expert row computes the gate, the
-// temperature and the softmax weights of its expert (MoCE.py:216-221 /
-// 175-188) and writes them into A; the warps stage X_b into B; one thread
-// issues the MMAs and commits them to an mbarrier; all threads then drain the
-// accumulator with tcgen05.ld and write the rows through a shared staging
-// block as contiguous stores.
+// nonzeros per row.  X_b arrives already in the B layout (pass 1 stages it),
+// so the operand moves are plain bulk copies into a ring of K-quarter slots.
 //
-// Every wait is bounded: a wait that runs out sets g_tc_fault and the kernel
-// returns after releasing its tensor memory.
+// An M=128, N=64, K=16 MMA reads 6 KB of operands from shared memory, so the
+// loop is bound by shared-memory bandwidth (about 48 cycles per MMA at
+// 128 B/clk), and a single issuing thread reaches only about one MMA per 70
+// cycles.  Hence two issuers (one per K-half, each into its own partial
+// accumulator), A rewritten per K-half as soon as the previous sample's MMAs
+// release it, and the staged-X copies running several quarters ahead.
+//
+// Every wait is bounded: a wait that runs out sets g_tc_fault, the roles
+// leave their loops together, copies and MMAs in flight complete, and the
+// kernel returns after releasing its tensor memory.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace moce {
@@ -32,7 +38,6 @@ __device__ int g_tc_fault = 0;
 
 namespace {
 
-constexpr int kTcThreads = 128;           // one thread per expert row
 constexpr int kTcN = 64;                  // padded pixels
 constexpr long long kSpinLimit = 1ll << 28;
 
@@ -98,38 +103,10 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
-// 32 lanes x 32 bit x 64 columns: thread t of warp w gets row 32w + t.
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
-  uint32_t r[64];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "
-      "%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
-      "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
-        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
-        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
-        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
-        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 // byte offset of A[row, c] in the K-major 128B-swizzled layout
 __device__ __forceinline__ uint32_t a_off(int row, int c) {
   return (uint32_t)((c >> 6) * 16384 + (row >> 3) * 1024 + (row & 7) * 128 + ((((c & 63) >> 3) ^ (row & 7)) << 4) +
                     ((c & 7) << 1));
-}
-
-// byte offset of B[c, p] (channel c, pixel p) in the MN-major 128B-swizzled layout
-__device__ __forceinline__ uint32_t b_off(int c, int p) {
-  return (uint32_t)((c >> 3) * 1024 + (c & 7) * 128 + ((((p >> 3) ^ (c & 7))) << 4) + ((p & 7) << 1));
 }
 
 struct TcArgs {
@@ -144,16 +121,19 @@ struct TcArgs {
   float tmin_tau, trange_tau;
   int B, C, HW, E_r, k, Kp;       // Kp: C rounded up to 64
   int n_tiles, n_bsplit;
+  int ns;                         // X quarter slots in the ring
 };
 
-constexpr int kQ = 4;             // K quarters: pipeline stages of the operands
+constexpr int kMaxSlots = 8;
 
 struct TcBars {
-  uint64_t full_b[kQ];            // B quarter landed (bulk copy, tx bytes)
-  uint64_t mma_q[kQ];             // MMAs of a quarter done: A and B quarter free
-  uint64_t a_full[kQ];            // rows wrote the A quarter (128 arrivals)
-  uint64_t d_full[2];             // accumulator buffer complete
+  uint64_t full_b[kMaxSlots];     // X quarter landed in the slot (bulk copy, tx bytes)
+  uint64_t slot_free[kMaxSlots];  // MMAs reading the slot done
+  uint64_t a_full[2];             // weight rows wrote the A half (128 arrivals)
+  uint64_t a_free[2];             // MMAs reading the A half done
+  uint64_t d_full[2];             // accumulator buffer complete (one commit per issuer)
   uint64_t d_empty[2];            // accumulator buffer drained (128 arrivals)
+  uint64_t fin[2];                // per issuer: every MMA it issued has completed
   uint32_t tmem;
   int abort;
 };
@@ -201,29 +181,99 @@ __device__ __forceinline__ void bulk_s2g(void* dst, uint32_t src, uint32_t bytes
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-__device__ __forceinline__ void row_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier over the 128 threads of one role that also ANDs a flag, so
+// that every thread of the role takes the same branch after a bounded wait.
+__device__ __forceinline__ bool role_sync_and(int id, int nthreads, bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)ok), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
 
-// 160 threads: warps 0..3 own the 128 expert rows of the tile (softmax
-// weights into A, accumulator drain, output), lane 0 of warp 4 moves the
-// operands (bulk copies of the staged X quarters) and issues the MMAs.
+// 2^x on the MUFU unit (ex2.approx, relative error about 2^-22; results that
+// would be subnormal flush to zero).  The weights it feeds are rounded to
+// 16 bits right after.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ void st_shared_u16(uint32_t addr, unsigned short v) {
+  asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ unsigned short bits16(T v) {
+  static_assert(sizeof(T) == 2, "16-bit element");
+  return *reinterpret_cast<const unsigned short*>(&v);
+}
+
+__device__ __forceinline__ void role_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// 32 lanes x 32 bit x 32 columns, no wait (the caller waits once for several).
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+constexpr int kTcThreads = 480;           // 15 warps, roles below
+constexpr int kWeightThreads = 256, kDrainThreads = 128;
+constexpr int kBarWeights = 1, kBarDrain = 2;
+constexpr int kWarpIssuer0 = 12, kWarpProducer = 14;
+
+__host__ __device__ constexpr size_t tc_stage_out_bytes(int HW, int esize) {
+  return ((size_t)128 * HW * esize + 15) & ~size_t(15);
+}
+
+// Roles (warp-specialized, one CTA per SM):
+//   warps 0-7   weight rows: threads 2r and 2r+1 share expert row e0 + r,
+//               each with half of its supports (a pair of adjacent lanes
+//               combines sums by shuffle); per sample the gate, temperature
+//               and softmax (MoCE.py:216-221 / 175-188), written as bf16/fp16
+//               into A one K-half at a time, as soon as the MMAs of the
+//               previous sample have released that half
+//   warps 8-11  drain: sum of the two partial accumulators (tcgen05.ld),
+//               output rows through a shared staging block, one bulk store
+//   warp 12, 13 lane 0: MMA issuers, K-half 0 / 1, each into its own partial
+//               accumulator (one thread issues a tcgen05.mma only about
+//               every 70 cycles, two keep the tensor pipe fed)
+//   warp 14     lane 0: producer, bulk copies of the staged X quarters into
+//               a ring of `ns` slots, running ahead of the MMAs
+// Tensor memory: 2 accumulator buffers x 2 partials x 64 columns.
 template <typename T, int KMAX>
-__global__ void __launch_bounds__(160, 1) mix_tc_kernel(TcArgs a) {
+__global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   extern __shared__ unsigned char s_dyn[];
-  unsigned char* base =
-      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(s_dyn) + 1023) & ~uintptr_t(1023));
-  const int C = a.C, HW = a.HW, k = a.k, Kp = a.Kp, E_r = a.E_r;
-  const int Kq = Kp / kQ;                                     // channels per quarter (multiple of 16)
-  // kQ stages pipeline the X operand (bulk copies); the weight operand is
-  // rewritten per sample after the sample's last MMA (mma_q[kQ - 1])
+  // 1024-byte aligned operand base, offset from s_dyn so that every pointer
+  // below stays in the shared address space (LDS/STS, not generic accesses)
+  unsigned char* base = s_dyn + ((1024u - (smem_u32(s_dyn) & 1023u)) & 1023u);
+  const int C = a.C, HW = a.HW, k = a.k, Kp = a.Kp, E_r = a.E_r, NS = a.ns;
+  const uint32_t qbytes = (uint32_t)Kp * 32;                  // a quarter of the channels x 128 B
   unsigned char* sA = base;                                   // 128 x Kp : Kp * 256 B
-  unsigned char* sB = base + (size_t)Kp * 256;                // Kp x 64  : Kp * 128 B
-  T* stg = reinterpret_cast<T*>(sB + (size_t)Kp * 128);       // 128 x HW output block
-  float* s_z = reinterpret_cast<float*>(sB + (size_t)Kp * 128 + 128 * kTcN * sizeof(T));  // 2 x Kp
+  unsigned char* sB = sA + (size_t)Kp * 256;                  // NS quarter slots
+  T* stg = reinterpret_cast<T*>(sB + (size_t)NS * qbytes);    // 128 x HW output block
+  float* s_z = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(stg) + tc_stage_out_bytes(HW, sizeof(T)));
   float* s_gw = s_z + 2 * Kp;
   TcBars* bars = reinterpret_cast<TcBars*>(s_gw + KMAX);
   volatile int* abort = &bars->abort;
 
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x % a.n_tiles, bsplit = blockIdx.x / a.n_tiles;
   const int e0 = tile * 128;
   const int rows = min(128, E_r - e0);
@@ -235,184 +285,232 @@ __global__ void __launch_bounds__(160, 1) mix_tc_kernel(TcArgs a) {
   for (int q = tid; q < Kp * 256 / 16; q += blockDim.x) reinterpret_cast<int4*>(sA)[q] = make_int4(0, 0, 0, 0);
   for (int i = tid; i < k; i += blockDim.x) s_gw[i] = a.gate_w[i];
   if (tid == 0) {
-    for (int q = 0; q < kQ; ++q) {
-      mbar_init(&bars->full_b[q], 1);
-      mbar_init(&bars->mma_q[q], 1);
-      mbar_init(&bars->a_full[q], 128);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&bars->full_b[s], 1);
+      mbar_init(&bars->slot_free[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&bars->d_full[s], 1);
-      mbar_init(&bars->d_empty[s], 128);
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&bars->a_full[h], kWeightThreads);
+      mbar_init(&bars->a_free[h], 1);
+      mbar_init(&bars->d_full[h], 2);
+      mbar_init(&bars->d_empty[h], kDrainThreads);
+      mbar_init(&bars->fin[h], 1);
     }
     bars->abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&bars->tmem)),
-                 "r"(2 * kTcN));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(&bars->tmem)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
+  proxy_fence_smem();                                         // zeroed A visible to the tensor cores
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem;
 
-  if (warp == 4) {
-    // ===================== operand mover + MMA issuer (one thread)
-    if (tid == 128) {
+  if (warp == kWarpProducer) {
+    // ===================== producer
+    if (lane == 0) {
+      const unsigned char* xs = static_cast<const unsigned char*>(a.xstage) + (size_t)b0 * Kp * 128;
+      const uint32_t aB = smem_u32(sB);
+      const int total = 4 * nb;
+      int n = 0;
+      for (; n < total; ++n) {
+        const int slot = n % NS, use = n / NS;
+        if (use >= 1 && !mbar_wait_abort(&bars->slot_free[slot], (use - 1) & 1, abort)) break;
+        mbar_expect_tx(&bars->full_b[slot], qbytes);
+        bulk_g2s(aB + (uint32_t)slot * qbytes, xs + (size_t)(n >> 2) * Kp * 128 + (size_t)(n & 3) * qbytes, qbytes,
+                 &bars->full_b[slot]);
+      }
+      // copies still in flight land before the block can exit (no-op on the
+      // normal path: the issuers consumed every slot)
+      for (int m = (n > NS ? n - NS : 0); m < n; ++m) mbar_wait(&bars->full_b[m % NS], (m / NS) & 1);
+    }
+  } else if (warp == kWarpIssuer0 || warp == kWarpIssuer0 + 1) {
+    // ===================== MMA issuers: K-half h into partial accumulator h
+    if (lane == 0) {
+      const int h = warp - kWarpIssuer0;
       const uint32_t idesc = umma_idesc(DTypeOf<T>::value == MOCE_BF16 ? 1 : 0, 128, kTcN);
-      const uint32_t aA = smem_u32(sA), aB = smem_u32(sB);
-      const unsigned char* xs = static_cast<const unsigned char*>(a.xstage);
-      const uint32_t qbytes = (uint32_t)Kq * 128;
-      const uint64_t da0 = umma_desc(aA, 16, 1024);
-      const uint64_t db0 = umma_desc(aB, (uint32_t)Kp * 128, 1024);
-      bool run = nb > 0;
-      if (run)
-        for (int q = 0; q < kQ; ++q) {
-          mbar_expect_tx(&bars->full_b[q], qbytes);
-          bulk_g2s(aB + q * qbytes, xs + (size_t)b0 * Kp * 128 + (size_t)q * qbytes, qbytes, &bars->full_b[q]);
-        }
+      const uint64_t da0 = umma_desc(smem_u32(sA), 16, 1024);
+      const uint32_t aB = smem_u32(sB);
+      const int kq = Kp / 64;                                 // K-steps (16 channels) per quarter
+      bool run = true;
       for (int i = 0; i < nb && run; ++i) {
         const int s = i & 1;
         if (i >= 2 && !mbar_wait_abort(&bars->d_empty[s], ((i - 2) >> 1) & 1, abort)) break;
-        const uint32_t d = tmem + (uint32_t)(s * kTcN);
-        for (int q = 0; q < kQ && run; ++q) {
-          if (!mbar_wait_abort(&bars->full_b[q], i & 1, abort) || !mbar_wait_abort(&bars->a_full[q], i & 1, abort)) {
+        if (!mbar_wait_abort(&bars->a_full[h], i & 1, abort)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(s * 2 * kTcN + h * kTcN);
+        for (int qq = 0; qq < 2; ++qq) {
+          const int q = 2 * h + qq, n = 4 * i + q, slot = n % NS;
+          if (!mbar_wait_abort(&bars->full_b[slot], (n / NS) & 1, abort)) {
             run = false;
             break;
           }
           tc_fence_after();
-          for (int j = q * Kq / 16; j < (q + 1) * Kq / 16; ++j) {
+          const uint64_t db0 = umma_desc(aB + (uint32_t)slot * qbytes, qbytes, 1024);
+          for (int jj = 0; jj < kq; ++jj) {
+            const int j = q * kq + jj;                        // K-step over all channels
             // start-address fields advance in 16-byte units (no carry: shared
             // addresses are below 2^18)
             const uint64_t da = da0 + (uint64_t)(((j >> 2) * 16384 + (j & 3) * 32) >> 4);
-            const uint64_t db = db0 + (uint64_t)(j * 128);
-            umma_f16(d, da, db, idesc, j > 0 ? 1u : 0u);
+            const uint64_t db = db0 + (uint64_t)(jj * 128);
+            umma_f16(d, da, db, idesc, (qq > 0 || jj > 0) ? 1u : 0u);
           }
-          umma_commit(&bars->mma_q[q]);
+          umma_commit(&bars->slot_free[slot]);
         }
         if (!run) break;
+        umma_commit(&bars->a_free[h]);
         umma_commit(&bars->d_full[s]);
-        if (i + 1 < nb) {
-          for (int q = 0; q < kQ; ++q) {
-            if (!mbar_wait_abort(&bars->mma_q[q], i & 1, abort)) {
-              run = false;
-              break;
-            }
-            mbar_expect_tx(&bars->full_b[q], qbytes);
-            bulk_g2s(aB + q * qbytes, xs + (size_t)(b0 + i + 1) * Kp * 128 + (size_t)q * qbytes, qbytes,
-                     &bars->full_b[q]);
-          }
-        }
       }
+      // every MMA of this thread completes before the block exits
+      umma_commit(&bars->fin[h]);
+      mbar_wait(&bars->fin[h], 0);
     }
-  } else {
-    // ===================== expert rows: weights -> A, accumulator -> Y
-    const int e = e0 + tid;
-    const bool has_row = tid < rows;
-    int ch[KMAX];
-    float ln2[KMAX];
+  } else if (tid < kWeightThreads) {
+    // ===================== weight rows (pairs of threads per row)
+    constexpr int KH = KMAX / 2;                              // supports per thread
+    const int row = tid >> 1, part = tid & 1;
+    const int e = e0 + row;
+    const bool has_row = row < rows;
+    const int Kh = Kp / 2;                                    // first channel of K-half 1
+    const uint32_t sAu = smem_u32(sA);
+    // the unnormalized weights of the sample stay in registers between the
+    // softmax sum and the two half writes (k <= 32); for k <= 64 they are
+    // recomputed per half to stay within the register budget
+    constexpr bool kKeepW = KMAX <= 32;
+    uint32_t chp[KH];                                         // channel << 17 | byte offset in A
+    float ln2[KH];
     float mx2 = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < KMAX; ++i) {
-      ch[i] = 0;
-      ln2[i] = -INFINITY;
-      if (i < k && has_row) {
-        ch[i] = a.idx[(size_t)e * k + i];
-        ln2[i] = a.ln[(size_t)e * k + i] * 1.4426950408889634f;   // log2(e)
-        mx2 = nan_max(mx2, ln2[i]);
+    for (int jj = 0; jj < KH; ++jj) {
+      const int j = part * KH + jj;
+      chp[jj] = 0;
+      ln2[jj] = -INFINITY;
+      if (j < k && has_row) {
+        const int c = a.idx[(size_t)e * k + j];
+        chp[jj] = ((uint32_t)c << 17) | a_off(row, c);
+        ln2[jj] = a.ln[(size_t)e * k + j] * 1.4426950408889634f;   // log2(e)
+        mx2 = nan_max(mx2, ln2[jj]);
       }
     }
+    mx2 = nan_max(mx2, __shfl_xor_sync(kFull, mx2, 1));
     const float bias = a.gate_b[0];
-    T* yg = static_cast<T*>(a.y);
-    float w[KMAX];
-    constexpr int ZPT = 4;                           // z values per thread (C <= 512)
+    constexpr int ZPT = 2;                                    // z values per thread (C <= 512)
     float zr[ZPT];
 #pragma unroll
     for (int u = 0; u < ZPT; ++u) {
-      const int c = tid + u * 128;
+      const int c = tid + u * kWeightThreads;
       zr[u] = (nb > 0 && c < C) ? a.z[(size_t)b0 * C + c] : 0.0f;
     }
-    for (int i = 0; i <= nb; ++i) {
-      if (i < nb) {
-        const int b = b0 + i;
-        float* szb = s_z + (i & 1) * Kp;
+    bool ok = true;
+    for (int i = 0; i < nb && ok; ++i) {
+      const int b = b0 + i;
+      float* szb = s_z + (i & 1) * Kp;
 #pragma unroll
-        for (int u = 0; u < ZPT; ++u)
-          if (tid + u * 128 < C) szb[tid + u * 128] = zr[u];
-        row_bar();
-        if (i + 1 < nb) {
+      for (int u = 0; u < ZPT; ++u)
+        if (tid + u * kWeightThreads < C) szb[tid + u * kWeightThreads] = zr[u];
+      role_sync(kBarWeights, kWeightThreads);
+      if (i + 1 < nb) {
 #pragma unroll
-          for (int u = 0; u < ZPT; ++u) {
-            const int c = tid + u * 128;
-            if (c < C) zr[u] = a.z[(size_t)(b + 1) * C + c];
-          }
+        for (int u = 0; u < ZPT; ++u) {
+          const int c = tid + u * kWeightThreads;
+          if (c < C) zr[u] = a.z[(size_t)(b + 1) * C + c];
         }
-        if (has_row) {
-          float g = bias;
-#pragma unroll
-          for (int j = 0; j < KMAX; ++j)
-            if (j < k) g += s_gw[j] * szb[ch[j]];
-          const float t = temperature(g, a.tmin_tau, a.trange_tau, nullptr);
-          if (a.T_out) a.T_out[(size_t)b * E_r + e] = t;
-          const float it = 1.0f / t;
-          const float m2 = mx2 * it;
-          float zs = 0.0f;
-#pragma unroll
-          for (int j = 0; j < KMAX; ++j) {
-            w[j] = exp2f(ln2[j] * it - m2);
-            zs += w[j];
-          }
-          const float iz = 1.0f / zs;
-#pragma unroll
-          for (int j = 0; j < KMAX; ++j) w[j] *= iz;
-        }
-        // A is rewritten once the previous sample's MMAs are all done; one
-        // proxy fence makes the new weights visible to the tensor cores
-        if (i >= 1 && !mbar_wait_abort(&bars->mma_q[kQ - 1], (i - 1) & 1, abort)) break;
-        if (has_row) {
-#pragma unroll
-          for (int j = 0; j < KMAX; ++j)
-            if (j < k) *reinterpret_cast<T*>(sA + a_off(tid, ch[j])) = from_f<T>(w[j]);
-        }
-        proxy_fence_smem();
-        for (int q = 0; q < kQ; ++q) mbar_arrive(&bars->a_full[q]);
       }
-      if (i >= 1) {
-        // drain sample i-1
-        const int j = i - 1, s = j & 1;
-        if (!mbar_wait_abort(&bars->d_full[s], (j >> 1) & 1, abort)) break;
-        tc_fence_after();
-        float v[kTcN];
-        tmem_ld64(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(s * kTcN), v);
-        tc_fence_before();
-        mbar_arrive(&bars->d_empty[s]);
-        if (tid == 0) bulk_wait_read();               // previous block left the staging area
-        row_bar();
+      float gp = 0.0f;
+#pragma unroll
+      for (int jj = 0; jj < KH; ++jj)
+        if (part * KH + jj < k && has_row) gp += s_gw[part * KH + jj] * szb[chp[jj] >> 17];
+      const float g = bias + gp + __shfl_xor_sync(kFull, gp, 1);
+      const float t = temperature(g, a.tmin_tau, a.trange_tau, nullptr);
+      if (a.T_out && has_row && part == 0) a.T_out[(size_t)b * E_r + e] = t;
+      const float it = 1.0f / t;
+      const float m2 = mx2 * it;
+      float wv[kKeepW ? KH : 1];
+      float zp = 0.0f;
+#pragma unroll
+      for (int jj = 0; jj < KH; ++jj) {
+        const float ev = ex2_approx(ln2[jj] * it - m2);
+        if constexpr (kKeepW) wv[jj] = ev;
+        zp += ev;
+      }
+      const float iz = 1.0f / (zp + __shfl_xor_sync(kFull, zp, 1));
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        // the previous sample's MMAs have released this half of A
+        bool w_ok = true;
+        if (i >= 1 && tid == 0) w_ok = mbar_wait_abort(&bars->a_free[h], (i - 1) & 1, abort);
+        if (i >= 1) w_ok = role_sync_and(kBarWeights, kWeightThreads, w_ok);
+        if (!w_ok) {
+          ok = false;
+          break;
+        }
         if (has_row) {
 #pragma unroll
-          for (int p = 0; p < kTcN; ++p)
-            if (p < HW) stg[tid * HW + p] = from_f<T>(v[p]);
+          for (int jj = 0; jj < KH; ++jj) {
+            const int c = (int)(chp[jj] >> 17);
+            if (part * KH + jj < k && (c >= Kh) == (h == 1)) {
+              float ev;
+              if constexpr (kKeepW) ev = wv[jj];
+              else ev = ex2_approx(ln2[jj] * it - m2);
+              st_shared_u16(sAu + (chp[jj] & 0x1FFFFu), bits16(from_f<T>(ev * iz)));
+            }
+          }
         }
         proxy_fence_smem();
-        row_bar();
-        T* dst = yg + ((size_t)(b0 + j) * E + e0) * HW;
-        const uint32_t nbytes = (uint32_t)(rows * HW * sizeof(T));
-        if (((((uintptr_t)dst) | nbytes) & 15) == 0) {
-          if (tid == 0) bulk_s2g(dst, smem_u32(stg), nbytes);
-        } else {
-          for (int q = tid; q < rows * HW; q += 128) dst[q] = stg[q];
-          row_bar();
-        }
+        mbar_arrive(&bars->a_full[h]);
       }
     }
-    if (tid == 0) bulk_wait_all();
+  } else if (tid < kWeightThreads + kDrainThreads) {
+    // ===================== drain (warps 8-11): TMEM lane quarter = warp % 4
+    const int dt = tid - kWeightThreads;                      // row within the tile
+    const bool has_row = dt < rows;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    T* yg = static_cast<T*>(a.y);
+    for (int i = 0; i < nb; ++i) {
+      const int s = i & 1;
+      bool ok = true;
+      if (dt == 0) {
+        ok = mbar_wait_abort(&bars->d_full[s], (i >> 1) & 1, abort);
+        bulk_wait_read();                                     // previous block left the staging area
+      }
+      if (!role_sync_and(kBarDrain, kDrainThreads, ok)) break;
+      tc_fence_after();
+      const uint32_t tb = tmem + lane_base + (uint32_t)(s * 2 * kTcN);
+#pragma unroll
+      for (int cb = 0; cb < kTcN; cb += 32) {
+        if (cb >= HW) break;                                  // uniform across the warp
+        uint32_t r0[32], r1[32];
+        tmem_ld32_nowait(tb + cb, r0);
+        tmem_ld32_nowait(tb + kTcN + cb, r1);
+        tmem_wait_ld();
+        if (has_row) {
+#pragma unroll
+          for (int p = 0; p < 32; ++p)
+            if (cb + p < HW) stg[dt * HW + cb + p] = from_f<T>(__uint_as_float(r0[p]) + __uint_as_float(r1[p]));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bars->d_empty[s]);
+      proxy_fence_smem();
+      role_sync(kBarDrain, kDrainThreads);
+      T* dst = yg + ((size_t)(b0 + i) * E + e0) * HW;
+      const uint32_t nbytes = (uint32_t)(rows * HW * sizeof(T));
+      if (((((uintptr_t)dst) | nbytes) & 15) == 0) {
+        if (dt == 0) bulk_s2g(dst, smem_u32(stg), nbytes);
+      } else {
+        for (int q = dt; q < rows * HW; q += kDrainThreads) dst[q] = stg[q];
+        role_sync(kBarDrain, kDrainThreads);
+      }
+    }
+    if (dt == 0) bulk_wait_all();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kTcN));
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
 }
 
 }  // namespace
@@ -444,14 +542,21 @@ extern "C" int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C, 
   MOCE_REQUIRE(B < 65536 && (E_r + 1) * HW < (int64_t)1 << 31, MOCE_ERR_UNSUPPORTED, "moce_mix_tc: shape too large");
   const int Kp = (int)((C + 63) / 64 * 64);
   const int KMAX = k <= 16 ? 16 : k <= 32 ? 32 : 64;
-  const size_t smem = 1024 + (size_t)Kp * 256 + (size_t)Kp * 128 + (size_t)128 * 64 * 2 + (size_t)Kp * 8 +
-                      (size_t)KMAX * 4 + sizeof(TcBars) + 16;
+  const size_t qbytes = (size_t)Kp * 32;
+  const size_t fixed = 1024 + (size_t)Kp * 256 + tc_stage_out_bytes((int)HW, 2) + (size_t)Kp * 8 +
+                       (size_t)KMAX * 4 + sizeof(TcBars);
+  int dev = 0, smem_max = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  const int ns = (int)std::min<size_t>((size_t)kMaxSlots, ((size_t)smem_max > fixed ? smem_max - fixed : 0) / qbytes);
+  MOCE_REQUIRE(ns >= 2, MOCE_ERR_UNSUPPORTED, "moce_mix_tc: not enough shared memory (%d B)", smem_max);
+  const size_t smem = fixed + (size_t)ns * qbytes;
   const int n_tiles = (int)((E_r + 127) / 128);
   int n_bsplit = num_sms() / n_tiles;
   if (n_bsplit < 1) n_bsplit = 1;
   if (n_bsplit > B) n_bsplit = (int)B;
   TcArgs a{xstage, y, z, idx, ln, gate_w, gate_b, T_out, tmin_tau, trange_tau,
-           (int)B, (int)C, (int)HW, (int)E_r, (int)k, Kp, n_tiles, n_bsplit};
+           (int)B, (int)C, (int)HW, (int)E_r, (int)k, Kp, n_tiles, n_bsplit, ns};
   return dispatch_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
     if constexpr (sizeof(T) != 2) {
@@ -461,7 +566,7 @@ extern "C" int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C, 
                                                                             : mix_tc_kernel<T, 64>;
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return set_error(MOCE_ERR_CUDA, "moce_mix_tc: cannot reserve %zu B shared memory", smem);
-      kern<<<(unsigned)(n_tiles * n_bsplit), 160, smem, (cudaStream_t)stream>>>(a);
+      kern<<<(unsigned)(n_tiles * n_bsplit), kTcThreads, smem, (cudaStream_t)stream>>>(a);
       return check_launch("mix_tc_kernel");
     }
   });
