@@ -109,8 +109,7 @@ template <typename T>
 __global__ void __launch_bounds__(256) pool_residual_kernel(const T* __restrict__ x, int C, int HW, int cc,
                                                             const int32_t* __restrict__ mask,
                                                             const int32_t* __restrict__ meta, float* __restrict__ z,
-                                                            T* __restrict__ y, int E, int4* __restrict__ xstage,
-                                                            int Kp) {
+                                                            T* __restrict__ y, int E) {
   extern __shared__ __align__(16) unsigned char s_raw[];
   T* s_x = reinterpret_cast<T*>(s_raw);                                  // cc * HW
   float* s_res = reinterpret_cast<float*>(s_raw + (((size_t)cc * HW * sizeof(T) + 15) & ~size_t(15)));  // HW
@@ -149,23 +148,6 @@ __global__ void __launch_bounds__(256) pool_residual_kernel(const T* __restrict_
         for (int p = lane; p < HW; p += 32) s += to_f(s_x[(size_t)c * HW + p]);
         s = warp_sum(s);
         if (lane == 0) z[(size_t)b * C + c0 + c] = s * inv_hw;
-      }
-    }
-    if (xstage) {
-      // the chunk's channel rows in the tensor-core operand layout: per row
-      // 128 bytes = 64 pixels (zero padded), 16-byte unit j holds pixels
-      // 8 (j ^ (c & 7)) .. +7; 8-row groups of 1024 bytes; the last chunk
-      // also writes the zero rows C .. Kp-1
-      int4* xs = xstage + (size_t)b * Kp * 8;
-      const int crow_end = (c0 + cn == C) ? Kp : c0 + cn;
-      for (int q = threadIdx.x; q < (crow_end - c0) * 8; q += blockDim.x) {
-        const int c = c0 + (q >> 3), j = q & 7;
-        const int pb = (j ^ (c & 7)) * 8;
-        union { int4 v; T e[8]; } u;
-#pragma unroll
-        for (int t = 0; t < 8; ++t)
-          u.e[t] = (c < C && pb + t < HW) ? s_x[(size_t)(c - c0) * HW + pb + t] : from_f<T>(0.0f);
-        xs[(size_t)c * 8 + j] = u.v;
       }
     }
     if (n_u > 0) {
@@ -510,26 +492,8 @@ int sched_supported(int64_t k) { return moce_schedule_steps(k) <= 52; }
 
 using namespace moce;
 
-static int pool_residual_impl(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
-                              const int32_t* meta, float* z, void* y, int64_t E_r, void* xstage, void* stream);
-
 extern "C" int moce_pool_residual(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
                                   const int32_t* meta, float* z, void* y, int64_t E_r, void* stream) {
-  return pool_residual_impl(x, dtype, B, C, HW, mask, meta, z, y, E_r, nullptr, stream);
-}
-
-extern "C" int moce_pool_stage(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
-                               const int32_t* meta, float* z, void* y, int64_t E_r, void* xstage, void* stream) {
-  if (B == 0) return MOCE_OK;
-  MOCE_REQUIRE(xstage && ((uintptr_t)xstage & 15) == 0, MOCE_ERR_INVALID,
-               "moce_pool_stage: xstage must be a 16-byte aligned buffer");
-  MOCE_REQUIRE(dtype == MOCE_BF16 || dtype == MOCE_F16, MOCE_ERR_UNSUPPORTED, "moce_pool_stage: 16-bit inputs only");
-  MOCE_REQUIRE(HW <= 64, MOCE_ERR_UNSUPPORTED, "moce_pool_stage: H*W must be <= 64");
-  return pool_residual_impl(x, dtype, B, C, HW, mask, meta, z, y, E_r, xstage, stream);
-}
-
-static int pool_residual_impl(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
-                              const int32_t* meta, float* z, void* y, int64_t E_r, void* xstage, void* stream) {
   if (B == 0) return MOCE_OK;  // an empty batch is a no-op
   MOCE_REQUIRE(x && z, MOCE_ERR_INVALID, "moce_pool_residual: null pointer argument");
   MOCE_REQUIRE(!y || (mask && meta), MOCE_ERR_INVALID, "moce_pool_residual: the residual needs mask and meta");
@@ -554,8 +518,7 @@ static int pool_residual_impl(const void* x, int dtype, int64_t B, int64_t C, in
             cudaSuccess)
       return set_error(MOCE_ERR_CUDA, "moce_pool_residual: smem %zu", smem);
     pool_residual_kernel<T><<<(unsigned)B, 256, smem, (cudaStream_t)stream>>>(
-        static_cast<const T*>(x), (int)C, (int)HW, (int)cc, mask, meta, z, static_cast<T*>(y), (int)(E_r + 1),
-        reinterpret_cast<int4*>(xstage), (int)((C + 63) / 64 * 64));
+        static_cast<const T*>(x), (int)C, (int)HW, (int)cc, mask, meta, z, static_cast<T*>(y), (int)(E_r + 1));
     return check_launch("pool_residual_kernel");
   });
 }

@@ -282,9 +282,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   const int nb = b1 - b0;
   const int E = E_r + 1;
 
-  for (int q = tid; q < Kp * 256 / 16; q += blockDim.x) reinterpret_cast<int4*>(sA)[q] = make_int4(0, 0, 0, 0);
-  for (int i = tid; i < k; i += blockDim.x) s_gw[i] = a.gate_w[i];
-  if (tid == 0) {
+  // ---- prologue.  The producer initializes the barriers and starts the
+  // first X copies, and the weight rows start their register loads, before
+  // all threads zero A, so that those latencies overlap the zeroing.
+  const unsigned char* xs = static_cast<const unsigned char*>(a.xstage) + (size_t)b0 * Kp * 128;
+  const int n_pre = min(NS, 4 * nb);                          // copies issued in the prologue
+  if (tid == kWarpProducer * 32) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&bars->full_b[s], 1);
       mbar_init(&bars->slot_free[s], 1);
@@ -298,7 +301,49 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     }
     bars->abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int n = 0; n < n_pre; ++n) {
+      mbar_expect_tx(&bars->full_b[n], qbytes);
+      bulk_g2s(smem_u32(sB) + (uint32_t)n * qbytes, xs + (size_t)(n >> 2) * Kp * 128 + (size_t)(n & 3) * qbytes,
+               qbytes, &bars->full_b[n]);
+    }
   }
+  // weight rows: threads 2r and 2r+1 share expert row e0 + r, each with KH
+  // of its supports
+  constexpr int KH = KMAX / 2;
+  const int row = tid >> 1, part = tid & 1;
+  const bool w_row = tid < kWeightThreads && row < rows;
+  uint32_t chp[KH];                                           // channel << 17 | byte offset in A
+  float ln2[KH];
+  float mx2 = -INFINITY;
+  // gate weights of this thread's supports in registers (k <= 32), else
+  // read from shared memory per sample
+  constexpr bool kGwReg = KMAX <= 32;
+  float gwr[kGwReg ? KH : 1];
+  constexpr int ZPT = 2;                                      // z values per weight thread (C <= 512)
+  float zr[ZPT];
+  if (tid < kWeightThreads) {
+#pragma unroll
+    for (int jj = 0; jj < KH; ++jj) {
+      const int j = part * KH + jj;
+      chp[jj] = 0;
+      ln2[jj] = -INFINITY;
+      if (j < k && w_row) {
+        const size_t o = (size_t)(e0 + row) * k + j;
+        const int c = a.idx[o];
+        chp[jj] = ((uint32_t)c << 17) | a_off(row, c);
+        ln2[jj] = a.ln[o] * 1.4426950408889634f;            // log2(e)
+        mx2 = nan_max(mx2, ln2[jj]);
+      }
+      if constexpr (kGwReg) gwr[jj] = (j < k) ? a.gate_w[j] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < ZPT; ++u) {
+      const int c = tid + u * kWeightThreads;
+      zr[u] = (nb > 0 && c < C) ? a.z[(size_t)b0 * C + c] : 0.0f;
+    }
+  }
+  for (int q = tid; q < Kp * 256 / 16; q += blockDim.x) reinterpret_cast<int4*>(sA)[q] = make_int4(0, 0, 0, 0);
+  for (int i = tid; i < k; i += blockDim.x) s_gw[i] = a.gate_w[i];
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(&bars->tmem)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -312,10 +357,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   if (warp == kWarpProducer) {
     // ===================== producer
     if (lane == 0) {
-      const unsigned char* xs = static_cast<const unsigned char*>(a.xstage) + (size_t)b0 * Kp * 128;
       const uint32_t aB = smem_u32(sB);
       const int total = 4 * nb;
-      int n = 0;
+      int n = n_pre;
       for (; n < total; ++n) {
         const int slot = n % NS, use = n / NS;
         if (use >= 1 && !mbar_wait_abort(&bars->slot_free[slot], (use - 1) & 1, abort)) break;
@@ -370,40 +414,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     }
   } else if (tid < kWeightThreads) {
     // ===================== weight rows (pairs of threads per row)
-    constexpr int KH = KMAX / 2;                              // supports per thread
-    const int row = tid >> 1, part = tid & 1;
     const int e = e0 + row;
-    const bool has_row = row < rows;
+    const bool has_row = w_row;
     const int Kh = Kp / 2;                                    // first channel of K-half 1
     const uint32_t sAu = smem_u32(sA);
     // the unnormalized weights of the sample stay in registers between the
     // softmax sum and the two half writes (k <= 32); for k <= 64 they are
     // recomputed per half to stay within the register budget
     constexpr bool kKeepW = KMAX <= 32;
-    uint32_t chp[KH];                                         // channel << 17 | byte offset in A
-    float ln2[KH];
-    float mx2 = -INFINITY;
-#pragma unroll
-    for (int jj = 0; jj < KH; ++jj) {
-      const int j = part * KH + jj;
-      chp[jj] = 0;
-      ln2[jj] = -INFINITY;
-      if (j < k && has_row) {
-        const int c = a.idx[(size_t)e * k + j];
-        chp[jj] = ((uint32_t)c << 17) | a_off(row, c);
-        ln2[jj] = a.ln[(size_t)e * k + j] * 1.4426950408889634f;   // log2(e)
-        mx2 = nan_max(mx2, ln2[jj]);
-      }
-    }
     mx2 = nan_max(mx2, __shfl_xor_sync(kFull, mx2, 1));
     const float bias = a.gate_b[0];
-    constexpr int ZPT = 2;                                    // z values per thread (C <= 512)
-    float zr[ZPT];
-#pragma unroll
-    for (int u = 0; u < ZPT; ++u) {
-      const int c = tid + u * kWeightThreads;
-      zr[u] = (nb > 0 && c < C) ? a.z[(size_t)b0 * C + c] : 0.0f;
-    }
     bool ok = true;
     for (int i = 0; i < nb && ok; ++i) {
       const int b = b0 + i;
@@ -422,7 +442,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       float gp = 0.0f;
 #pragma unroll
       for (int jj = 0; jj < KH; ++jj)
-        if (part * KH + jj < k && has_row) gp += s_gw[part * KH + jj] * szb[chp[jj] >> 17];
+        if (part * KH + jj < k && has_row) gp += (kGwReg ? gwr[jj] : s_gw[part * KH + jj]) * szb[chp[jj] >> 17];
       const float g = bias + gp + __shfl_xor_sync(kFull, gp, 1);
       const float t = temperature(g, a.tmin_tau, a.trange_tau, nullptr);
       if (a.T_out && has_row && part == 0) a.T_out[(size_t)b * E_r + e] = t;

@@ -1,0 +1,177 @@
+// Pass 1 of the tensor-core path (16-bit inputs, H*W <= 64): one read of X
+// gives
+//   z[b,c]       = mean_p X[b,c,p]                     (MoCE.py:174 / 212)
+//   Y[b,E_r,p]   = mean over uncovered channels of X   (MoCE.py:191-196,
+//                  0 when every channel is covered      moce_kernel.cu:148-231)
+//   xstage[b]    = X_b in the tensor-core operand layout of the mix
+// Each sample is one cluster of kStageCtas CTAs, one channel quarter per CTA,
+// so that a sample's loads spread over several SMs and many loads are in
+// flight per SM.  The per-pixel residual sums of the quarters are added up
+// by cluster rank 0 through distributed shared memory.
+//
+// Operand layout (matches the B operand of mix_tc.cu): per sample Kp rows of
+// 128 bytes, row c = 64 pixels (zero padded); the 16-byte unit j of row c
+// holds pixels 8 (j ^ (c & 7)) .. +7; rows C .. Kp-1 are zero.
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace moce {
+namespace {
+
+constexpr int kStageCtas = 4;
+constexpr int kStageThreads = 256;
+
+template <typename T>
+__global__ void __cluster_dims__(kStageCtas, 1, 1) __launch_bounds__(kStageThreads)
+    pool_stage_kernel(const T* __restrict__ x, int C, int HW, int cc, const int32_t* __restrict__ mask,
+                      const int32_t* __restrict__ meta, float* __restrict__ z, T* __restrict__ y, int E,
+                      int4* __restrict__ xstage, int Kp) {
+  extern __shared__ __align__(16) unsigned char s_raw[];
+  T* s_x = reinterpret_cast<T*>(s_raw);                                            // cc x HW
+  float* s_res = reinterpret_cast<float*>(s_raw + (((size_t)cc * HW * sizeof(T) + 15) & ~size_t(15)));  // 64
+  int* s_ulist = reinterpret_cast<int*>(s_res + 64);                               // cc
+  __shared__ int s_nu;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = blockIdx.x, b = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c0 = rank * cc;
+  const int c1 = min(C, c0 + cc);
+  const int cn = max(0, c1 - c0);
+  const int n_u = (mask && meta) ? meta[0] : 0;
+  const T* src = x + ((size_t)b * C + c0) * HW;
+  const size_t n = (size_t)cn * HW;
+
+  for (int p = tid; p < 64; p += kStageThreads) s_res[p] = 0.0f;
+  if (cn > 0) {
+    // contiguous rows c0 .. c1-1: 16-byte loads, eight in flight per thread
+    if ((((uintptr_t)src) | (n * sizeof(T))) % 16 == 0) {
+      const int4* s4 = reinterpret_cast<const int4*>(src);
+      int4* d4 = reinterpret_cast<int4*>(s_x);
+      const int n16 = (int)(n * sizeof(T) / 16);
+      for (int q0 = tid; q0 < n16; q0 += 8 * kStageThreads) {
+        int4 r[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int q = q0 + u * kStageThreads;
+          if (q < n16) r[u] = __ldg(s4 + q);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int q = q0 + u * kStageThreads;
+          if (q < n16) d4[q] = r[u];
+        }
+      }
+    } else {
+#pragma unroll 4
+      for (size_t q = tid; q < n; q += kStageThreads) s_x[q] = src[q];
+    }
+  }
+  if (tid == 0) s_nu = 0;
+  __syncthreads();
+  // z: two threads per channel, one half of the pixels each
+  const float inv_hw = 1.0f / (float)HW;
+  for (int c = tid >> 1; c - (tid >> 1) < cn; c += kStageThreads / 2) {
+    float s = 0.0f;
+    if (c < cn)
+      for (int p = tid & 1; p < HW; p += 2) s += to_f(s_x[(size_t)c * HW + p]);
+    s += __shfl_xor_sync(kFull, s, 1);
+    if (c < cn && (tid & 1) == 0) z[(size_t)b * C + c0 + c] = s * inv_hw;
+  }
+  // residual: partial sums over this quarter's uncovered channels
+  if (n_u > 0 && cn > 0) {
+    if (warp == 0) {
+      int base = 0;
+      for (int c = lane; c - lane < cn; c += 32) {
+        const bool un = c < cn && mask[c0 + c] == 1;
+        const unsigned bal = __ballot_sync(kFull, un);
+        if (un) s_ulist[base + __popc(bal & ((1u << lane) - 1u))] = c;
+        base += __popc(bal);
+      }
+      if (lane == 0) s_nu = base;
+    }
+    __syncthreads();
+    const int nl = s_nu;
+    for (int p = tid; p < HW; p += kStageThreads) {
+      float r = 0.0f;
+      for (int j = 0; j < nl; ++j) r += to_f(s_x[(size_t)s_ulist[j] * HW + p]);
+      s_res[p] = r;
+    }
+  }
+  // the partial sums are published before the (much larger) operand stores,
+  // so that the cluster barrier's release does not wait for those stores
+  if (n_u > 0) asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  // operand layout; the CTA holding channel C-1 also writes the zero rows
+  {
+    int4* xs = xstage + (size_t)b * Kp * 8;
+    const int row_end = (cn > 0 && c1 == C) ? Kp : c1;
+    for (int q = tid; q < (row_end - c0) * 8; q += kStageThreads) {
+      const int c = c0 + (q >> 3), j = q & 7;
+      const int pb = (j ^ (c & 7)) * 8;
+      union {
+        int4 v;
+        T e[8];
+      } u;
+#pragma unroll
+      for (int t = 0; t < 8; ++t)
+        u.e[t] = (c < C && pb + t < HW) ? s_x[(size_t)(c - c0) * HW + pb + t] : from_f<T>(0.0f);
+      xs[(size_t)c * 8 + j] = u.v;
+    }
+  }
+  if (n_u > 0) {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (rank == 0 && y) {
+      T* yr = y + ((size_t)b * E + (E - 1)) * HW;
+      for (int p = tid; p < HW; p += kStageThreads) {
+        float r = 0.0f;
+        for (int q = 0; q < kStageCtas; ++q) r += cluster.map_shared_rank(s_res, q)[p];
+        yr[p] = from_f<T>(r / (float)n_u);
+      }
+    }
+    cluster.sync();                                 // peers' shared memory stays until rank 0 has read it
+  } else if (rank == 0 && y) {
+    T* yr = y + ((size_t)b * E + (E - 1)) * HW;
+    for (int p = tid; p < HW; p += kStageThreads) yr[p] = from_f<T>(0.0f);
+  }
+}
+
+}  // namespace
+}  // namespace moce
+
+using namespace moce;
+
+extern "C" int moce_pool_stage(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
+                               const int32_t* meta, float* z, void* y, int64_t E_r, void* xstage, void* stream) {
+  if (B == 0) return MOCE_OK;  // an empty batch is a no-op
+  MOCE_REQUIRE(x && z && xstage, MOCE_ERR_INVALID, "moce_pool_stage: null pointer argument");
+  MOCE_REQUIRE(((uintptr_t)xstage & 15) == 0, MOCE_ERR_INVALID,
+               "moce_pool_stage: xstage must be a 16-byte aligned buffer");
+  MOCE_REQUIRE(!y || (mask && meta), MOCE_ERR_INVALID, "moce_pool_stage: the residual needs mask and meta");
+  MOCE_REQUIRE(dtype == MOCE_BF16 || dtype == MOCE_F16, MOCE_ERR_UNSUPPORTED, "moce_pool_stage: 16-bit inputs only");
+  MOCE_REQUIRE(B > 0 && C >= 1 && HW >= 1 && E_r >= 0, MOCE_ERR_INVALID, "moce_pool_stage: invalid shape");
+  MOCE_REQUIRE(HW <= 64, MOCE_ERR_UNSUPPORTED, "moce_pool_stage: H*W must be <= 64");
+  MOCE_REQUIRE(B < 65536 && C <= 4096, MOCE_ERR_UNSUPPORTED, "moce_pool_stage: shape too large");
+  // channels per CTA: a multiple of 8, so that every chunk starts on a
+  // 16-byte boundary of the sample
+  const int cc = (int)(((C + kStageCtas - 1) / kStageCtas + 7) / 8 * 8);
+  const size_t smem = (((size_t)cc * HW * 2 + 15) & ~size_t(15)) + 64 * 4 + (size_t)cc * 4;
+  const int Kp = (int)((C + 63) / 64 * 64);
+  return dispatch_dtype(dtype, [&](auto tag) {
+    using T = decltype(tag);
+    if constexpr (sizeof(T) != 2) {
+      return set_error(MOCE_ERR_UNSUPPORTED, "moce_pool_stage: 16-bit inputs only");
+    } else {
+      if (smem > 48 * 1024 &&
+          cudaFuncSetAttribute(pool_stage_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+              cudaSuccess)
+        return set_error(MOCE_ERR_CUDA, "moce_pool_stage: cannot reserve %zu B shared memory", smem);
+      const dim3 grid(kStageCtas, (unsigned)B);
+      pool_stage_kernel<T><<<grid, kStageThreads, smem, (cudaStream_t)stream>>>(
+          static_cast<const T*>(x), (int)C, (int)HW, cc, mask, meta, z, static_cast<T*>(y), (int)(E_r + 1),
+          reinterpret_cast<int4*>(xstage), Kp);
+      return check_launch("pool_stage_kernel");
+    }
+  });
+}

@@ -35,6 +35,8 @@ def relerr(a, b):
     (2, 130, 3, 7, 140, 33, torch.bfloat16),    # ragged C (not a multiple of 8), k > 32
     (2, 16, 1, 1, 2, 16, torch.float16),        # k == C, HW == 1
     (2, 96, 8, 8, 129, 40, torch.bfloat16),     # HW == 64 exactly
+    (3, 64, 3, 11, 40, 8, torch.bfloat16),      # HW == 33: odd rows carry column 31 to the last column
+    (2, 192, 6, 6, 70, 12, torch.float16),      # HW == 36, even rows
 ])
 def test_tc_mix_matches_oracle(B, C, H_, W_, E, k, dtype):
     gen = torch.Generator().manual_seed(B * 100 + C + k)
