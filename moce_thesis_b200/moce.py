@@ -37,17 +37,26 @@ def native():
 class _Route:
     """Native route cache of one logits tensor: int32 supports, normalised
     logits, coverage, optional transposed lists (backward) and, when k fits
-    the scheduled mix kernel, the warp groups and support schedule."""
+    the scheduled mix kernel, the warp groups and support schedule.  The
+    schedule is built on the first call that runs the scheduled mix, so
+    inputs that take the tensor-core mix never pay for it."""
 
-    __slots__ = ("idx", "ln", "mask", "meta", "toff", "tslot", "group_expert", "sched")
+    __slots__ = ("idx", "ln", "mask", "meta", "toff", "tslot", "group_expert", "sched", "channels", "balance")
 
     def __init__(self, logits: torch.Tensor, k: int, transposed: bool, balance: bool = True):
         m = native()
         L = logits.detach().float().contiguous()
         self.idx, self.ln, self.mask, self.meta, self.toff, self.tslot = m.route_build(L, int(k), bool(transposed))
         self.group_expert = self.sched = None
-        if m.schedule_supported(int(k)):
-            self.group_expert, self.sched = m.schedule_build(self.idx, L.shape[1], bool(balance))
+        self.channels = int(L.shape[1])
+        self.balance = bool(balance)
+
+    def schedule(self):
+        """(group_expert, sched) for the scheduled mix, or None if k does not fit it."""
+        m = native()
+        if self.sched is None and m.schedule_supported(int(self.idx.shape[1])):
+            self.group_expert, self.sched = m.schedule_build(self.idx, self.channels, self.balance)
+        return None if self.sched is None else (self.group_expert, self.sched)
 
     def forward(self, x, gate_w, gate_b, tmin_tau, trange_tau, want_T=False, out=None):
         """Both forward passes; returns (y, z, T).  T is None unless wanted.
@@ -61,7 +70,7 @@ class _Route:
             y, z, T = m.forward_tc(x, self.idx, self.ln, self.mask, self.meta, gate_w, gate_b, float(tmin_tau),
                                    float(trange_tau), bool(want_T), out)
             return y, z, (T if want_T else None)
-        if self.sched is not None:
+        if self.schedule() is not None:
             y, z, T = m.forward_scheduled(x, self.ln, self.mask, self.meta, self.group_expert, self.sched, gate_w,
                                           gate_b, float(tmin_tau), float(trange_tau), bool(want_T), out)
             return y, z, (T if want_T else None)
