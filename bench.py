@@ -12,6 +12,16 @@ per second, whole job; also reported as % of 8 TB/s.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--dtype bf16|fp32]
     python bench.py --impl reference ...   # the CPU oracle port, host cores
+
+Two further workloads print their own JSON lines (not the headline):
+
+    python bench.py --workload train   # fp32 training step of one layer:
+        N=512/GPU, C_in=256, 14x14, E=1024, k=16, forward + aux loss +
+        backward (dX, dL, dgate), supports re-selected every step, and with
+        N>1 GPUs the all-reduce of the L and gate gradients
+    python bench.py --workload sweep   # per-stage sweep of ResNet-50 expand
+        projections, bf16, N=256: (64, 56x56, E=256, k=8),
+        (128, 28x28, 512, 16), (256, 14x14, 1024, 16), (512, 7x7, 2048, 32)
 """
 from __future__ import annotations
 
@@ -376,6 +386,157 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+def _dist_setup():
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    return world, rank, local, dev
+
+
+def _max_over_ranks(ms, world, dev):
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def run_train(args):
+    """fp32 training step of one MoCE layer (ResNet-101 stage-3 shape)."""
+    import torch
+    import torch.distributed as dist
+    world, rank, local, dev = _dist_setup()
+    from moce_thesis_b200 import MoCE
+    from moce_thesis_b200.dist import allreduce_moce_grads
+    Bt, Ct, Ht, Wt, Et, Kt = 512, 256, 14, 14, 1024, 16
+    g = torch.Generator().manual_seed(2000 + rank)
+    x = torch.randn(Bt, Ct, Ht, Wt, generator=g).abs().to(dev)
+    dy = torch.randn(Bt, Et, Ht, Wt, generator=g).to(dev)
+    torch.manual_seed(0)
+    layer = MoCE(in_channels=Ct, sampling_factor=1, k=Kt, temp_min=TMIN, temp_max=TMAX)
+    layer.num_experts = Et
+    layer.routing_logits = torch.nn.Parameter(torch.randn(Et - 1, Ct, generator=torch.Generator().manual_seed(1)))
+    layer = layer.to(dev).train()
+    x.requires_grad_(True)
+    one = torch.ones((), device=dev)
+
+    def step():
+        for prm in layer.parameters():
+            prm.grad = None
+        x.grad = None
+        y = layer(x)
+        torch.autograd.backward([y, layer.aux_loss], [dy, one])
+        if world > 1:
+            allreduce_moce_grads(layer)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(st)
+        for _ in range(args.steps):
+            step()
+        e1.record(st)
+        torch.cuda.synchronize()
+    ms = _max_over_ranks(e0.elapsed_time(e1), world, dev) / args.steps
+    xb, yb = Bt * Ct * Ht * Wt * 4, Bt * Et * Ht * Wt * 4
+    nbytes = (xb + yb) + (yb + xb + xb)          # forward X+Y, backward dY+X+dX
+    out = {"metric": "MoCE training step HBM GB/s", "value": round(world * nbytes / (ms * 1e-3) / 1e9, 2),
+           "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "fp32", "data": "synthetic (seeded half-normal X, N(0,1) dY and logits)",
+           "config": {"workload": "MoCE layer training step: N=512/GPU C=256 14x14 E=1024 k=16, fwd + aux + bwd",
+                      "global_batch": Bt * world,
+                      "parallelism": f"batch-sharded x{world}, L/gate grads all-reduced (NCCL)" if world > 1
+                      else "single GPU"},
+           "clocks": clk.summary()}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+SWEEP = [(64, 56, 256, 8), (128, 28, 512, 16), (256, 14, 1024, 16), (512, 7, 2048, 32)]
+
+
+def run_sweep(args):
+    """Per-stage forward sweep, bf16, N=256 per GPU; one JSON line per shape."""
+    import torch
+    import torch.distributed as dist
+    world, rank, local, dev = _dist_setup()
+    from moce_thesis_b200 import MoCE, native
+    mc = native()
+    Bs = 256
+    for (Cs, Hs, Es, Ks) in SWEEP:
+        g = torch.Generator().manual_seed(3000 + rank)
+        x0 = torch.randn(Bs, Cs, Hs, Hs, generator=g).abs().to(dev, torch.bfloat16)
+        layer = MoCE(in_channels=Cs, sampling_factor=1, k=Ks, temp_min=TMIN, temp_max=TMAX)
+        layer.num_experts = Es
+        layer.routing_logits = torch.nn.Parameter(
+            torch.randn(Es - 1, Cs, generator=torch.Generator().manual_seed(1)))
+        layer = layer.to(dev).eval()
+        layer.build_eval_cache()
+        xb, yb = x0.numel() * 2, Bs * Es * Hs * Hs * 2
+        nsets = max(2, int(3 * L2_BYTES // (xb + yb)) + 1)
+        xs = [x0] + [(x0 * (1.0 + 0.001 * i)).contiguous() for i in range(1, nsets)]
+        ys = [torch.empty(Bs, Es, Hs, Hs, device=dev, dtype=torch.bfloat16) for _ in range(nsets)]
+        r = layer._route
+        gwf = layer.cached_gate_weight.detach().reshape(-1).float().contiguous()
+        gbf = layer.cached_gate_bias.detach().reshape(-1).float().contiguous()
+
+        def step(i):
+            r.forward(xs[i % nsets], gwf, gbf, layer.cached_temp_min_tau, layer.cached_temp_range_tau, False,
+                      ys[i % nsets])
+
+        for i in range(args.warmup):
+            step(i)
+        torch.cuda.synchronize()
+        st = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(local) as clk:
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            e0.record(st)
+            for i in range(args.steps):
+                step(i)
+            e1.record(st)
+            torch.cuda.synchronize()
+        ms = _max_over_ranks(e0.elapsed_time(e1), world, dev) / args.steps
+        nbytes = xb + yb + (Es - 1) * Ks * 8 + Cs * 4
+        path = "tensor-core" if mc.tc_supported(x0, Ks) else (
+            "scheduled" if r.schedule() is not None else "general")
+        out = {"metric": "MoCE fwd HBM GB/s (% of 8 TB/s)", "value": round(world * nbytes / (ms * 1e-3) / 1e9, 2),
+               "unit": "GB/s", "pct_of_8tbs": round(100 * nbytes / (ms * 1e-3) / 1e9 / NOMINAL_HBM_GBS, 2),
+               "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+               "higher_is_better": True, "scaling": "weak", "dtype": "bf16", "data": "synthetic",
+               "config": {"workload": f"ResNet-50 expand projection C={Cs} {Hs}x{Hs} E={Es} k={Ks}, N={Bs}/GPU",
+                          "path": path, "l2": f"{nsets} rotating X/Y sets"},
+               "clocks": clk.summary()}
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        del xs, ys, layer, x0
+        torch.cuda.empty_cache()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -384,11 +545,16 @@ def main():
     ap.add_argument("--dtype", choices=["bf16", "fp32"], default="bf16")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["stage4", "train", "sweep"], default="stage4")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "train":
+        run_train(args)
+    elif args.workload == "sweep":
+        run_sweep(args)
     else:
         run_ours(args)
 
