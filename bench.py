@@ -174,6 +174,7 @@ def run_ours(args):
     ys = [torch.empty(B, E, H, W, device=dev, dtype=dtype) for _ in range(nsets)]
 
     use_tc = bool(mc.tc_supported(x0, K))
+    use_px = (not use_tc) and bool(mc.px_supported(x0, K))
 
     def step(i):
         return r.forward(xs[i % nsets], gwf, gbf, tmin_tau, trange_tau, False, ys[i % nsets])
@@ -222,6 +223,15 @@ def run_ours(args):
 
         def pass2(i):
             capi.call("moce_mix_tc", sts[i % nsets].data_ptr(), dcode, B, C, H * W, zs[i % nsets].data_ptr(),
+                      r.idx.data_ptr(), r.ln.data_ptr(), E - 1, K, gwf.data_ptr(), gbf.data_ptr(), tmin_tau,
+                      trange_tau, ys[i % nsets].data_ptr(), None, capi.stream_handle())
+    elif use_px:
+        def pass1(i):
+            capi.call("moce_pool_residual", xs[i % nsets].data_ptr(), dcode, B, C, H * W, r.mask.data_ptr(),
+                      r.meta.data_ptr(), zs[i % nsets].data_ptr(), ys[i % nsets].data_ptr(), E - 1, capi.stream_handle())
+
+        def pass2(i):
+            capi.call("moce_mix_px", xs[i % nsets].data_ptr(), dcode, B, C, H * W, zs[i % nsets].data_ptr(),
                       r.idx.data_ptr(), r.ln.data_ptr(), E - 1, K, gwf.data_ptr(), gbf.data_ptr(), tmin_tau,
                       trange_tau, ys[i % nsets].data_ptr(), None, capi.stream_handle())
     else:
@@ -311,10 +321,12 @@ def run_ours(args):
                    "parallelism": f"batch-sharded x{world}, no data-path collective",
                    "l2": f"{nsets} rotating X/Y sets ({nsets * (xb + yb) / 2**20:.0f} MiB > 126 MiB L2)"},
         "kernels_ms": {("pass1_pool_stage" if use_tc else "pass1_pool_residual"): round(gate_ms, 5),
-                       ("pass2_mix_tc" if use_tc else "pass2_mix_scheduled"): round(mix_ms, 5)},
+                       ("pass2_mix_tc" if use_tc else "pass2_mix_px" if use_px else "pass2_mix_scheduled"):
+                           round(mix_ms, 5)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "kernel": "mix_tc_kernel (pass 2, tcgen05)" if use_tc else "mix_sched_kernel (pass 2)",
+                     "kernel": "mix_tc_kernel (pass 2, tcgen05)" if use_tc else
+                         "mix_px kernel (pass 2, CUDA cores, lanes over pixels)" if use_px else "mix_sched_kernel (pass 2)",
                      "peak_kind": f"{peak_kind} copy bandwidth"},
         "e2e": {"value": round(e2e, 3), "unit": "GB/s", "h2d_bytes_per_step": xb, "d2h_bytes_per_step": yb,
                 "api": "moce_thesis_b200.MoCE.forward_eval, pinned host X in, host Y out"},
@@ -519,7 +531,7 @@ def run_sweep(args):
             torch.cuda.synchronize()
         ms = _max_over_ranks(e0.elapsed_time(e1), world, dev) / args.steps
         nbytes = xb + yb + (Es - 1) * Ks * 8 + Cs * 4
-        path = "tensor-core" if mc.tc_supported(x0, Ks) else (
+        path = "tensor-core" if mc.tc_supported(x0, Ks) else "lanes-over-pixels" if mc.px_supported(x0, Ks) else (
             "scheduled" if r.schedule() is not None else "general")
         out = {"metric": "MoCE fwd HBM GB/s (% of 8 TB/s)", "value": round(world * nbytes / (ms * 1e-3) / 1e9, 2),
                "unit": "GB/s", "pct_of_8tbs": round(100 * nbytes / (ms * 1e-3) / 1e9 / NOMINAL_HBM_GBS, 2),

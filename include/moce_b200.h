@@ -136,6 +136,23 @@ int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C,
 int moce_tc_fault(int* flag, int clear);
 
 /*
+ * CUDA-core pass 2 with lanes over pixels, any dtype, H*W <= 512, k <= 64,
+ * for maps of a few hundred pixels (14x14, 28x28 stages; fp32 anywhere).
+ * Same inputs and outputs as moce_mix_tc with X itself in place of the
+ * staged copy (pass 1 is moce_pool_residual): a warp per expert computes the
+ * gate, temperature and softmax (MoCE.py:216-221 / 175-188) and sums its k
+ * support rows (moce_kernel.cu:57-141) from X_b held in shared memory.
+ * moce_px_supported returns 1 when the shape fits (X_b within the shared
+ * memory of one CTA).
+ */
+int moce_px_supported(int dtype, int64_t C, int64_t HW, int64_t k);
+int moce_mix_px(const void* x, int dtype, int64_t B, int64_t C, int64_t HW,
+                const float* z, const int32_t* idx, const float* ln,
+                int64_t E_r, int64_t k, const float* gate_w,
+                const float* gate_b, float tmin_tau, float trange_tau,
+                void* y, float* T_out, void* stream);
+
+/*
  * Global average pool: pooled[b,c] = mean_p X[b,c,p] (fp32 out).
  * Replaces moce_pool (moce_layer_cuda.cpp:8-10, moce_kernel.cu:849-861).
  * pooled has the dtype of X in the reference; here it is always fp32.

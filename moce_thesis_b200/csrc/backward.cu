@@ -12,7 +12,7 @@
 //   dL[e,S_e] = backward of ln = (sel - mean) / max(std, 1) applied to sum_b dln_b
 // Batch reductions run in a fixed order (no atomics), so results are
 // deterministic.
-#include "common.cuh"
+#include "px.cuh"
 
 namespace moce {
 namespace {
@@ -200,6 +200,218 @@ __global__ void __launch_bounds__(kThreads) bwd_dx_kernel(
   }
 }
 
+// ---------------------------------------------------------------------
+// Lanes over pixels (H*W <= 512, k <= 32): the same gradients with X_b
+// staged in shared memory once per CTA and every support row read as
+// consecutive words by the whole warp (no bank conflicts), four pixels per
+// lane per 128-pixel slab.
+
+constexpr int kPxThreadsB = 512;
+constexpr int kPxWarpsB = kPxThreadsB / 32;
+
+// lane L of the result holds sum over the 32 lanes of v[L] (31 shuffles)
+__device__ __forceinline__ float reduce_scatter32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool up = (lane & off) != 0;
+#pragma unroll
+    for (int j = 0; j < off; ++j) {
+      const float send = up ? v[j] : v[j + off];
+      const float keep = up ? v[j + off] : v[j];
+      v[j] = keep + __shfl_xor_sync(kFull, send, off);
+    }
+  }
+  return v[0];
+}
+
+size_t px_route_smem(int64_t C, int64_t HW, int64_t k, size_t esize) {
+  const int64_t HWp = (HW + 3) / 4 * 4;
+  return (((size_t)C * HWp * esize + 15) & ~size_t(15)) + (size_t)(C + k + kPxWarpsB * k + kPxWarpsB) * 4;
+}
+
+// grid (nch, B): warp per expert; the dY row in registers, the k dot
+// products against the support rows, one reduce-scatter, then the softmax /
+// temperature / gate chain of bwd_route_kernel.
+template <typename T, int NSLAB>
+__global__ void __launch_bounds__(kPxThreadsB, 1) bwd_px_route_kernel(
+    const T* __restrict__ x, const T* __restrict__ dy, int C, int HW, int HWp, const int32_t* __restrict__ idx,
+    const float* __restrict__ ln, int E_r, int k, const float* __restrict__ gate_w,
+    const float* __restrict__ gate_b, float tmin_tau, float trange_tau, const float* __restrict__ z,
+    const float* __restrict__ Tb, BwdWs ws, int vec_dy) {
+  extern __shared__ __align__(16) unsigned char s_raw[];
+  T* s_x = reinterpret_cast<T*>(s_raw);                                                 // C x HWp
+  float* s_z = reinterpret_cast<float*>(s_raw + (((size_t)C * HWp * sizeof(T) + 15) & ~size_t(15)));  // C
+  float* s_w = s_z + C;                                                                 // k
+  float* s_pw = s_w + k;                                                                // warps x k
+  float* s_pb = s_pw + kPxWarpsB * k;                                                   // warps
+  const int b = blockIdx.y, ch = blockIdx.x, nch = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  px_stage_rows<T>(s_x, x + (size_t)b * C * HW, C, HW, HWp);
+  for (int c = threadIdx.x; c < C; c += kPxThreadsB) s_z[c] = z[(size_t)b * C + c];
+  for (int i = threadIdx.x; i < k; i += kPxThreadsB) s_w[i] = gate_w[i];
+  for (int i = threadIdx.x; i < kPxWarpsB * k; i += kPxThreadsB) s_pw[i] = 0.0f;
+  if (threadIdx.x < kPxWarpsB) s_pb[threadIdx.x] = 0.0f;
+  __syncthreads();
+  const float bias = gate_b[0];
+  const int per = (E_r + nch - 1) / nch;
+  const int e0 = ch * per, e1 = min(E_r, e0 + per);
+  const int E = E_r + 1;
+  const bool valid = lane < k;
+  // the expert's dY row (four pixels per lane per slab), supports, logits and
+  // temperature are loaded one expert ahead, overlapping the current one
+  auto load_dy = [&](int e, float (&d)[NSLAB][4]) {
+    const T* dyr = dy + ((size_t)b * E + e) * HW;
+#pragma unroll
+    for (int sl = 0; sl < NSLAB; ++sl) {
+      const int p = 128 * sl + 4 * lane;
+      if (p + 3 < HW && vec_dy) {
+        ld4<T>(dyr + p, d[sl]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) d[sl][j] = (p + j < HW) ? to_f(dyr[p + j]) : 0.0f;
+      }
+    }
+  };
+  float d_n[NSLAB][4];
+  int c_n = 0;
+  float ln_n = 0.0f, t_n = 1.0f;
+  if (e0 + warp < e1) {
+    load_dy(e0 + warp, d_n);
+    c_n = valid ? idx[(size_t)(e0 + warp) * k + lane] : 0;
+    ln_n = valid ? ln[(size_t)(e0 + warp) * k + lane] : 0.0f;
+    t_n = Tb[(size_t)b * E_r + e0 + warp];
+  }
+  for (int e = e0 + warp; e < e1; e += kPxWarpsB) {
+    const size_t be = (size_t)b * E_r + e;
+    const float t = t_n;
+    const int c_l = c_n;
+    const float ln_l = ln_n;
+    float d[NSLAB][4];
+#pragma unroll
+    for (int sl = 0; sl < NSLAB; ++sl)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) d[sl][j] = d_n[sl][j];
+    if (e + kPxWarpsB < e1) {
+      load_dy(e + kPxWarpsB, d_n);
+      c_n = valid ? idx[(size_t)(e + kPxWarpsB) * k + lane] : 0;
+      ln_n = valid ? ln[(size_t)(e + kPxWarpsB) * k + lane] : 0.0f;
+      t_n = Tb[be + kPxWarpsB];
+    }
+    const float g = warp_sum(valid ? s_w[lane] * s_z[c_l] : 0.0f) + bias;
+    const float u = valid ? ln_l / t : -INFINITY;
+    const float m = warp_max(u);
+    const float ex = valid ? expf(u - m) : 0.0f;
+    const float a_l = ex / warp_sum(ex);
+    float part[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      float sum = 0.0f;
+      if (i < k) {
+        const int c = __shfl_sync(kFull, c_l, i);
+        const T* row = s_x + (size_t)c * HWp + 4 * lane;
+#pragma unroll
+        for (int sl = 0; sl < NSLAB; ++sl) {
+          if (128 * sl + 4 * lane < HW) {
+            float f[4];
+            ld4<T>(row + 128 * sl, f);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) sum = fmaf(d[sl][j], f[j], sum);
+          }
+        }
+      }
+      part[i] = sum;
+    }
+    const float da = reduce_scatter32(part, lane);
+    const float S = warp_sum(valid ? a_l * da : 0.0f);
+    const float du = valid ? a_l * (da - S) : 0.0f;
+    float dT = -warp_sum(du * (valid ? u : 0.0f)) / t;
+    const float sig = 1.0f / (1.0f + expf(-g));
+    const float t_raw = tmin_tau + trange_tau * sig;
+    if (!(t_raw >= 1e-3f)) dT = 0.0f;
+    const float dg = dT * trange_tau * sig * (1.0f - sig);
+    if (valid) {
+      ws.a[be * k + lane] = a_l;
+      ws.dlnb[be * k + lane] = du / t;
+      s_pw[warp * k + lane] += dg * s_z[c_l];
+    }
+    if (lane == 0) {
+      ws.dg[be] = dg;
+      s_pb[warp] += dg;
+    }
+  }
+  __syncthreads();
+  const size_t q = (size_t)b * nch + ch;
+  for (int i = threadIdx.x; i < k; i += kPxThreadsB) {
+    float s = 0.0f;
+    for (int w = 0; w < kPxWarpsB; ++w) s += s_pw[w * k + i];
+    ws.part_w[q * k + i] = s;
+  }
+  if (threadIdx.x == 0) {
+    float s = 0.0f;
+    for (int w = 0; w < kPxWarpsB; ++w) s += s_pb[w];
+    ws.part_b[q] = s;
+  }
+}
+
+// grid (ceil(HW / 32), B): a 32-pixel tile of dY for all E experts, as fp32,
+// in shared memory (dY read from HBM once); warp per input channel, lane per
+// pixel, the channel's transposed list gathered in list order as in
+// bwd_dx_kernel.
+template <typename T>
+__global__ void __launch_bounds__(kPxThreadsB, 1) bwd_px_dx_kernel(
+    const T* __restrict__ dy, int C, int HW, int E_r, int k, const int32_t* __restrict__ mask,
+    const int32_t* __restrict__ meta, const int32_t* __restrict__ toff, const int32_t* __restrict__ tslot,
+    const float* __restrict__ gate_w, BwdWs ws, T* __restrict__ dx) {
+  extern __shared__ __align__(16) unsigned char s_raw[];
+  float* s_dy = reinterpret_cast<float*>(s_raw);            // E x 32
+  const int b = blockIdx.y, p0 = blockIdx.x * 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = E_r + 1;
+  const T* dyb = dy + (size_t)b * E * HW;
+  for (int q = threadIdx.x; q < E * 32; q += kPxThreadsB) {
+    const int p = p0 + (q & 31);
+    s_dy[q] = (p < HW) ? to_f(dyb[(size_t)(q >> 5) * HW + p]) : 0.0f;
+  }
+  __syncthreads();
+  const int n_u = meta[0];
+  const int p = p0 + lane;
+  const size_t bek = (size_t)b * E_r * k;
+  for (int c = warp; c < C; c += kPxWarpsB) {
+    const int s0 = toff[c], s1 = toff[c + 1];
+    float acc = 0.0f, dzp = 0.0f;
+    for (int sc = s0; sc < s1; sc += 32) {
+      const int s = sc + lane;
+      int e_l = 0;
+      float a_l = 0.0f;
+      if (s < s1) {
+        const int slot = tslot[s];
+        e_l = slot / k;
+        a_l = ws.a[bek + slot];
+        dzp += ws.dg[(size_t)b * E_r + e_l] * gate_w[slot - e_l * k];
+      }
+      const int n = min(32, s1 - sc);
+      for (int j = 0; j < n; ++j) {
+        const int e = __shfl_sync(kFull, e_l, j);
+        const float a = __shfl_sync(kFull, a_l, j);
+        acc = fmaf(a, s_dy[e * 32 + lane], acc);
+      }
+    }
+    const float dz = warp_sum(dzp);
+    const float rw = (mask[c] == 1 && n_u > 0) ? 1.0f / (float)n_u : 0.0f;
+    if (p < HW) {
+      if (rw != 0.0f) acc += rw * s_dy[E_r * 32 + lane];
+      dx[((size_t)b * C + c) * HW + p] = from_f<T>(acc + dz / (float)HW);
+    }
+  }
+}
+
+int smem_optin() {
+  int dev = 0, smem_max = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  return smem_max;
+}
+
 // grid ceil(E_r / 8): warp per expert.  Sums d ln over the batch in order,
 // then back-propagates the centring / std normalisation into dL[e, S_e].
 __global__ void __launch_bounds__(kThreads) bwd_logits_kernel(
@@ -316,19 +528,47 @@ extern "C" int moce_backward(const void* x, const void* dy, int dtype, int64_t B
   }
   rc = dispatch_dtype(dtype, [&](auto tag) {
     using Tt = decltype(tag);
-    const size_t smem = (size_t)(C + k + kWarps * k + kWarps) * 4;
-    if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(bwd_route_kernel<Tt>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-            cudaSuccess)
-      return set_error(MOCE_ERR_UNSUPPORTED, "moce_backward: route smem %zu", smem);
-    bwd_route_kernel<Tt><<<dim3(nch, (unsigned)B), kThreads, smem, st>>>(
-        static_cast<const Tt*>(x), static_cast<const Tt*>(dy), (int)C, (int)HW, idx, ln, (int)E_r, (int)k,
-        gate_w, gate_b, tmin_tau, trange_tau, z, T, ws);
+    const int smem_max = smem_optin();
+    const size_t es = sizeof(Tt);
+    const size_t smem_pr = px_route_smem(C, HW, k, es);
+    if (HW <= 512 && k <= 32 && smem_pr <= (size_t)smem_max) {
+      const int HWp = (int)((HW + 3) / 4 * 4);
+      const int nslab = (int)((HW + 127) / 128);
+      const int vec = (HW % 4 == 0) && (((uintptr_t)dy) % 16 == 0);
+      void (*kern)(const Tt*, const Tt*, int, int, int, const int32_t*, const float*, int, int, const float*,
+                   const float*, float, float, const float*, const float*, BwdWs, int) =
+          nslab == 1 ? bwd_px_route_kernel<Tt, 1> : nslab == 2 ? bwd_px_route_kernel<Tt, 2>
+          : nslab == 3 ? bwd_px_route_kernel<Tt, 3> : bwd_px_route_kernel<Tt, 4>;
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_pr) != cudaSuccess)
+        return set_error(MOCE_ERR_CUDA, "moce_backward: route smem %zu", smem_pr);
+      kern<<<dim3(nch, (unsigned)B), kPxThreadsB, smem_pr, st>>>(
+          static_cast<const Tt*>(x), static_cast<const Tt*>(dy), (int)C, (int)HW, HWp, idx, ln, (int)E_r, (int)k,
+          gate_w, gate_b, tmin_tau, trange_tau, z, T, ws, vec);
+    } else {
+      const size_t smem = (size_t)(C + k + kWarps * k + kWarps) * 4;
+      if (smem > 48 * 1024 &&
+          cudaFuncSetAttribute(bwd_route_kernel<Tt>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+              cudaSuccess)
+        return set_error(MOCE_ERR_UNSUPPORTED, "moce_backward: route smem %zu", smem);
+      bwd_route_kernel<Tt><<<dim3(nch, (unsigned)B), kThreads, smem, st>>>(
+          static_cast<const Tt*>(x), static_cast<const Tt*>(dy), (int)C, (int)HW, idx, ln, (int)E_r, (int)k,
+          gate_w, gate_b, tmin_tau, trange_tau, z, T, ws);
+    }
     int r = check_launch("moce_backward/route");
     if (r) return r;
-    bwd_dx_kernel<Tt><<<dim3((unsigned)((C + kWarps - 1) / kWarps), (unsigned)B), kThreads, 0, st>>>(
-        static_cast<const Tt*>(dy), (int)C, (int)HW, (int)E_r, (int)k, mask, meta, toff, tslot, gate_w, ws,
-        static_cast<Tt*>(dx));
+    const size_t smem_dx = (size_t)(E_r + 1) * 32 * 4;
+    if (smem_dx <= (size_t)smem_max) {
+      if (cudaFuncSetAttribute(bwd_px_dx_kernel<Tt>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_dx) !=
+          cudaSuccess)
+        return set_error(MOCE_ERR_CUDA, "moce_backward: dx smem %zu", smem_dx);
+      bwd_px_dx_kernel<Tt><<<dim3((unsigned)((HW + 31) / 32), (unsigned)B), kPxThreadsB, smem_dx, st>>>(
+          static_cast<const Tt*>(dy), (int)C, (int)HW, (int)E_r, (int)k, mask, meta, toff, tslot, gate_w, ws,
+          static_cast<Tt*>(dx));
+    } else {
+      bwd_dx_kernel<Tt><<<dim3((unsigned)((C + kWarps - 1) / kWarps), (unsigned)B), kThreads, 0, st>>>(
+          static_cast<const Tt*>(dy), (int)C, (int)HW, (int)E_r, (int)k, mask, meta, toff, tslot, gate_w, ws,
+          static_cast<Tt*>(dx));
+    }
     return check_launch("moce_backward/dx");
   });
   if (rc) return rc;

@@ -451,6 +451,41 @@ std::vector<torch::Tensor> forward_tc(torch::Tensor x, torch::Tensor idx, torch:
   return {y, z, T};
 }
 
+bool px_supported(torch::Tensor x, int64_t k) {
+  if (x.dim() != 4) return false;
+  return moce_px_supported(dtype_of(x), x.size(1), x.size(2) * x.size(3), k) != 0;
+}
+
+// pass 1 (pool + residual) and the lanes-over-pixels CUDA-core pass 2
+std::vector<torch::Tensor> forward_px(torch::Tensor x, torch::Tensor idx, torch::Tensor ln, torch::Tensor mask,
+                                      torch::Tensor meta, torch::Tensor gate_w, torch::Tensor gate_b,
+                                      double tmin_tau, double trange_tau, bool want_T,
+                                      c10::optional<torch::Tensor> out_opt) {
+  for (auto* t : {&x, &idx, &ln, &mask, &meta, &gate_w, &gate_b}) {
+    CHECK_INPUT(*t);
+  }
+  TORCH_CHECK(idx.scalar_type() == torch::kInt32 && ln.scalar_type() == torch::kFloat32, "idx int32, ln float32");
+  const c10::cuda::CUDAGuard guard(x.device());
+  Dims d = dims(x, idx);
+  torch::Tensor y;
+  if (out_opt.has_value()) {
+    y = *out_opt;
+    CHECK_INPUT(y);
+    TORCH_CHECK(y.scalar_type() == x.scalar_type() && y.numel() == d.B * (d.E_r + 1) * d.HW, "out mismatch");
+  } else {
+    y = torch::empty({d.B, d.E_r + 1, d.H, d.W}, x.options());
+  }
+  auto z = f32_opts_like(x, {d.B, d.C});
+  auto T = want_T ? f32_opts_like(x, {d.B, d.E_r}) : f32_opts_like(x, {0});
+  ok(moce_pool_residual(x.data_ptr(), dtype_of(x), d.B, d.C, d.HW, mask.data_ptr<int32_t>(),
+                        meta.data_ptr<int32_t>(), z.data_ptr<float>(), y.data_ptr(), d.E_r, cur_stream()));
+  ok(moce_mix_px(x.data_ptr(), dtype_of(x), d.B, d.C, d.HW, z.data_ptr<float>(), idx.data_ptr<int32_t>(),
+                 ln.data_ptr<float>(), d.E_r, d.K, gate_w.data_ptr<float>(), gate_b.data_ptr<float>(),
+                 (float)tmin_tau, (float)trange_tau, y.data_ptr(), want_T ? T.data_ptr<float>() : nullptr,
+                 cur_stream()));
+  return {y, z, T};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -483,5 +518,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("forward_tc", &forward_tc, "Pool + residual, then the tensor-core mix: (y, z, T)", py::arg("x"),
         py::arg("idx"), py::arg("ln"), py::arg("mask"), py::arg("meta"), py::arg("gate_w"), py::arg("gate_b"),
         py::arg("tmin_tau"), py::arg("trange_tau"), py::arg("want_T") = false, py::arg("out") = py::none());
+  m.def("px_supported", &px_supported, "Whether the lanes-over-pixels CUDA-core mix takes this input");
+  m.def("forward_px", &forward_px, "Pool + residual, then the lanes-over-pixels CUDA-core mix: (y, z, T)",
+        py::arg("x"), py::arg("idx"), py::arg("ln"), py::arg("mask"), py::arg("meta"), py::arg("gate_w"),
+        py::arg("gate_b"), py::arg("tmin_tau"), py::arg("trange_tau"), py::arg("want_T") = false,
+        py::arg("out") = py::none());
   m.def("version", []() { return std::string(moce_version()); });
 }

@@ -1,0 +1,321 @@
+// Pass 2 on CUDA cores with lanes over pixels (any dtype, H*W <= 512).
+//
+// The scheduled mix (mix.cu) puts experts on lanes, so every lane gathers a
+// different channel row and a bank-conflict-free order of the supports has to
+// be planned per route.  Here a warp owns one expert at a time and its lanes
+// own the pixels: every support is one warp-uniform channel row, read as
+// consecutive 16-byte (fp32) or 8-byte (16-bit) words, conflict-free by
+// construction, four pixels per lane per 128-pixel slab.  This suits maps of
+// a few hundred pixels (the 14x14 and 28x28 stages); X_b sits whole in shared
+// memory, so the sample is read from HBM once per CTA.
+//
+// Per expert (MoCE.py:216-221 / 175-188): lane i holds support i (i and
+// i + 32 for k <= 64); the gate Linear(k,1) on z[S_e], the temperature, and
+// the softmax of ln / T are warp reductions; then the k weighted rows are
+// summed pixel by pixel in support order and the row of Y is stored directly.
+#include "px.cuh"
+
+namespace moce {
+namespace {
+
+constexpr int kPxThreads = 512;
+constexpr int kPxWarps = kPxThreads / 32;
+
+struct PxArgs {
+  const void* x;
+  void* y;
+  const float* z;
+  const int32_t* idx;
+  const float* ln;
+  const float* gate_w;
+  const float* gate_b;
+  float* T_out;
+  float tmin_tau, trange_tau;
+  int B, C, HW, HWp, E_r, k;
+  int vec_out;                    // Y rows allow 4-element vector stores
+};
+
+// grid (n_echunks, B); kPxThreads threads; warp per expert.
+template <typename T, int NSLAB, int KL>
+__global__ void __launch_bounds__(kPxThreads, 1) mix_px_kernel(PxArgs a) {
+  extern __shared__ __align__(16) unsigned char s_raw[];
+  const int C = a.C, HW = a.HW, HWp = a.HWp, k = a.k, E_r = a.E_r;
+  T* s_x = reinterpret_cast<T*>(s_raw);                                                // C x HWp
+  float* s_z = reinterpret_cast<float*>(s_raw + (((size_t)C * HWp * sizeof(T) + 15) & ~size_t(15)));  // C
+  float* s_gw = s_z + C;                                                               // k
+  const int b = blockIdx.y, ch = blockIdx.x, nch = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const T* xg = static_cast<const T*>(a.x);
+  px_stage_rows<T>(s_x, xg + (size_t)b * C * HW, C, HW, HWp);
+  for (int c = threadIdx.x; c < C; c += kPxThreads) s_z[c] = a.z[(size_t)b * C + c];
+  for (int i = threadIdx.x; i < k; i += kPxThreads) s_gw[i] = a.gate_w[i];
+  __syncthreads();
+  const float bias = a.gate_b[0];
+  const int per = (E_r + nch - 1) / nch;
+  const int e0 = ch * per, e1 = min(E_r, e0 + per);
+  const int E = E_r + 1;
+  T* yg = static_cast<T*>(a.y);
+  // the next expert's supports and logits are loaded one iteration ahead,
+  // so that their global-memory latency overlaps the current expert's mix
+  int c_n[KL];
+  float ln_n[KL];
+#pragma unroll
+  for (int q = 0; q < KL; ++q) {
+    const int i = lane + 32 * q;
+    const bool v = i < k && e0 + warp < e1;
+    c_n[q] = v ? a.idx[(size_t)(e0 + warp) * k + i] : 0;
+    ln_n[q] = v ? a.ln[(size_t)(e0 + warp) * k + i] : -INFINITY;
+  }
+  for (int e = e0 + warp; e < e1; e += kPxWarps) {
+    int c_l[KL];
+    float u_l[KL];
+#pragma unroll
+    for (int q = 0; q < KL; ++q) {
+      c_l[q] = c_n[q];
+      u_l[q] = ln_n[q];
+      const int i = lane + 32 * q;
+      const bool v = i < k && e + kPxWarps < e1;
+      c_n[q] = v ? a.idx[(size_t)(e + kPxWarps) * k + i] : 0;
+      ln_n[q] = v ? a.ln[(size_t)(e + kPxWarps) * k + i] : -INFINITY;
+    }
+    float gp = 0.0f;
+#pragma unroll
+    for (int q = 0; q < KL; ++q) {
+      const int i = lane + 32 * q;
+      if (i < k) gp += s_gw[i] * s_z[c_l[q]];
+      else u_l[q] = -INFINITY;
+    }
+    const float g = warp_sum(gp) + bias;
+    const float t = temperature(g, a.tmin_tau, a.trange_tau, nullptr);
+    if (a.T_out && lane == 0) a.T_out[(size_t)b * E_r + e] = t;
+    float m = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < KL; ++q) {
+      if (lane + 32 * q < k) u_l[q] = u_l[q] / t;
+      m = nan_max(m, u_l[q]);
+    }
+    m = warp_max(m);
+    float a_l[KL], s = 0.0f;
+#pragma unroll
+    for (int q = 0; q < KL; ++q) {
+      a_l[q] = (lane + 32 * q < k) ? expf(u_l[q] - m) : 0.0f;
+      s += a_l[q];
+    }
+    s = warp_sum(s);
+#pragma unroll
+    for (int q = 0; q < KL; ++q) a_l[q] /= s;
+
+    float acc[NSLAB][4];
+#pragma unroll
+    for (int sl = 0; sl < NSLAB; ++sl)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[sl][j] = 0.0f;
+#pragma unroll
+    for (int q = 0; q < KL; ++q) {
+      const int nq = min(32, k - 32 * q);
+#pragma unroll 4
+      for (int j = 0; j < nq; ++j) {
+        const int c = __shfl_sync(kFull, c_l[q], j);
+        const float w = __shfl_sync(kFull, a_l[q], j);
+        const T* row = s_x + (size_t)c * HWp + 4 * lane;
+#pragma unroll
+        for (int sl = 0; sl < NSLAB; ++sl) {
+          if (128 * sl + 4 * lane < HW) {
+            float f[4];
+            ld4<T>(row + 128 * sl, f);
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) acc[sl][jj] = fmaf(w, f[jj], acc[sl][jj]);
+          }
+        }
+      }
+    }
+    T* yr = yg + ((size_t)b * E + e) * HW;
+#pragma unroll
+    for (int sl = 0; sl < NSLAB; ++sl) {
+      const int p = 128 * sl + 4 * lane;
+      if (p + 3 < HW && a.vec_out) {
+        st4<T>(yr + p, acc[sl]);
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj)
+          if (p + jj < HW) yr[p + jj] = from_f<T>(acc[sl][jj]);
+      }
+    }
+  }
+}
+
+// k <= 32: the weights of 32 experts are computed at once with lanes over
+// experts (each lane runs its expert's gate, temperature and softmax alone,
+// no warp reductions), then the warp walks those experts with lanes over
+// pixels, taking each support's channel and weight by shuffle from the
+// expert's lane.  KMAX = 16 or 32 supports per lane in registers.
+template <typename T, int NSLAB, int KMAX>
+__global__ void __launch_bounds__(kPxThreads, 1) mix_px_grouped_kernel(PxArgs a) {
+  extern __shared__ __align__(16) unsigned char s_raw[];
+  const int C = a.C, HW = a.HW, HWp = a.HWp, k = a.k, E_r = a.E_r;
+  T* s_x = reinterpret_cast<T*>(s_raw);                                                // C x HWp
+  float* s_z = reinterpret_cast<float*>(s_raw + (((size_t)C * HWp * sizeof(T) + 15) & ~size_t(15)));  // C
+  float* s_gw = s_z + C;                                                               // k
+  const int b = blockIdx.y, ch = blockIdx.x, nch = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const T* xg = static_cast<const T*>(a.x);
+  px_stage_rows<T>(s_x, xg + (size_t)b * C * HW, C, HW, HWp);
+  for (int c = threadIdx.x; c < C; c += kPxThreads) s_z[c] = a.z[(size_t)b * C + c];
+  for (int i = threadIdx.x; i < k; i += kPxThreads) s_gw[i] = a.gate_w[i];
+  __syncthreads();
+  const float bias = a.gate_b[0];
+  const int per = (E_r + nch - 1) / nch;
+  const int e0 = ch * per, e1 = min(E_r, e0 + per);
+  const int E = E_r + 1;
+  T* yg = static_cast<T*>(a.y);
+  // warp w owns the G consecutive experts [e0 + w G, e0 + (w + 1) G) of the chunk
+  const int G = min(32, (e1 - e0 + kPxWarps - 1) / kPxWarps);
+  const int gb = e0 + warp * G;
+  const int ge = min(e1, gb + G);
+  if (gb < ge) {
+    // ---- weights, lane = expert gb + lane
+    const int em = gb + lane;
+    const bool has = em < ge;
+    int cr[KMAX];
+    float ar[KMAX];
+#pragma unroll
+    for (int i = 0; i < KMAX; ++i) {
+      const bool v = has && i < k;
+      cr[i] = v ? a.idx[(size_t)em * k + i] : 0;
+      ar[i] = v ? a.ln[(size_t)em * k + i] : -INFINITY;
+    }
+    float g = 0.0f;
+#pragma unroll
+    for (int i = 0; i < KMAX; ++i)
+      if (i < k) g += s_gw[i] * s_z[cr[i]];
+    const float t = temperature(g + bias, a.tmin_tau, a.trange_tau, nullptr);
+    if (a.T_out && has) a.T_out[(size_t)b * E_r + em] = t;
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < KMAX; ++i) {
+      if (i < k) ar[i] = ar[i] / t;
+      m = nan_max(m, ar[i]);
+    }
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < KMAX; ++i) {
+      ar[i] = (i < k) ? expf(ar[i] - m) : 0.0f;
+      sum += ar[i];
+    }
+    const float is = 1.0f / sum;
+#pragma unroll
+    for (int i = 0; i < KMAX; ++i) ar[i] *= is;
+    // ---- mix, lanes = pixels, one expert of the group at a time
+    for (int j = 0; j < ge - gb; ++j) {
+      float acc[NSLAB][4];
+#pragma unroll
+      for (int sl = 0; sl < NSLAB; ++sl)
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) acc[sl][jj] = 0.0f;
+#pragma unroll
+      for (int i = 0; i < KMAX; ++i) {
+        if (i < k) {
+          const int c = __shfl_sync(kFull, cr[i], j);
+          const float w = __shfl_sync(kFull, ar[i], j);
+          const T* row = s_x + (size_t)c * HWp + 4 * lane;
+#pragma unroll
+          for (int sl = 0; sl < NSLAB; ++sl) {
+            if (128 * sl + 4 * lane < HW) {
+              float f[4];
+              ld4<T>(row + 128 * sl, f);
+#pragma unroll
+              for (int jj = 0; jj < 4; ++jj) acc[sl][jj] = fmaf(w, f[jj], acc[sl][jj]);
+            }
+          }
+        }
+      }
+      T* yr = yg + ((size_t)b * E + gb + j) * HW;
+#pragma unroll
+      for (int sl = 0; sl < NSLAB; ++sl) {
+        const int p = 128 * sl + 4 * lane;
+        if (p + 3 < HW && a.vec_out) {
+          st4<T>(yr + p, acc[sl]);
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj)
+            if (p + jj < HW) yr[p + jj] = from_f<T>(acc[sl][jj]);
+        }
+      }
+    }
+  }
+}
+
+}  // namespace
+
+size_t px_smem_bytes(int64_t C, int64_t HW, int64_t k, size_t esize) {
+  const int64_t HWp = (HW + 3) / 4 * 4;
+  return (((size_t)C * HWp * esize + 15) & ~size_t(15)) + (size_t)C * 4 + (size_t)k * 4;
+}
+
+int px_supported(int dtype, int64_t C, int64_t HW, int64_t k) {
+  if (!dtype_ok(dtype) || HW < 1 || HW > 512 || k < 1 || k > 64) return 0;
+  int dev = 0, smem_max = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  return px_smem_bytes(C, HW, k, dtype_size(dtype)) <= (size_t)smem_max ? 1 : 0;
+}
+
+}  // namespace moce
+
+using namespace moce;
+
+extern "C" int moce_px_supported(int dtype, int64_t C, int64_t HW, int64_t k) { return px_supported(dtype, C, HW, k); }
+
+extern "C" int moce_mix_px(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
+                           const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
+                           const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out,
+                           void* stream) {
+  if (B == 0) return MOCE_OK;  // an empty batch is a no-op
+  MOCE_REQUIRE(x && z && idx && ln && gate_w && gate_b && y, MOCE_ERR_INVALID, "moce_mix_px: null pointer argument");
+  MOCE_REQUIRE(dtype_ok(dtype), MOCE_ERR_INVALID, "moce_mix_px: unknown dtype %d", dtype);
+  MOCE_REQUIRE(B > 0 && C >= 1 && HW >= 1 && E_r >= 1 && k >= 1 && k <= C, MOCE_ERR_INVALID,
+               "moce_mix_px: invalid shape");
+  MOCE_REQUIRE(B < 65536 && (E_r + 1) * HW < (int64_t)1 << 31 && C * HW < (int64_t)1 << 31, MOCE_ERR_UNSUPPORTED,
+               "moce_mix_px: shape too large");
+  MOCE_REQUIRE(px_supported(dtype, C, HW, k), MOCE_ERR_UNSUPPORTED,
+               "moce_mix_px: needs H*W <= 512, k <= 64 and X_b within shared memory");
+  const size_t esize = dtype_size(dtype);
+  const int HWp = (int)((HW + 3) / 4 * 4);
+  const size_t smem = px_smem_bytes(C, HW, k, esize);
+  const int nslab = (int)((HW + 127) / 128);
+  // CTAs per sample so that the grid covers the SMs several times over
+  const int per_sm = smem <= 110 * 1024 ? 2 : 1;
+  int64_t nch = (4LL * per_sm * num_sms() + B - 1) / B;
+  const int64_t max_ch = (E_r + kPxWarps - 1) / kPxWarps;
+  if (nch > max_ch) nch = max_ch;
+  if (nch < 1) nch = 1;
+  // grouped weights (k <= 16) pay off with at least 8 experts per warp; a
+  // group holds at most 32
+  const int64_t per = (E_r + nch - 1) / nch;
+  const bool grouped = k <= 16 && per >= 8 * kPxWarps;
+  if (grouped && per > 32 * kPxWarps) nch = (E_r + 32 * kPxWarps - 1) / (32 * kPxWarps);
+  const int vec = (HW % 4 == 0) && (((uintptr_t)y) % 16 == 0);
+  PxArgs a{x, y, z, idx, ln, gate_w, gate_b, T_out, tmin_tau, trange_tau,
+           (int)B, (int)C, (int)HW, HWp, (int)E_r, (int)k, vec};
+  return dispatch_dtype(dtype, [&](auto tag) {
+    using T = decltype(tag);
+    void (*kern)(PxArgs) = nullptr;
+#define MOCE_PX_PICK(NS)                                                                          \
+  case NS:                                                                                        \
+    kern = grouped ? mix_px_grouped_kernel<T, NS, 16>                                             \
+           : k <= 32 ? mix_px_kernel<T, NS, 1> : mix_px_kernel<T, NS, 2>;                         \
+    break;
+    switch (nslab) {
+      MOCE_PX_PICK(1)
+      MOCE_PX_PICK(2)
+      MOCE_PX_PICK(3)
+      MOCE_PX_PICK(4)
+      default: return set_error(MOCE_ERR_UNSUPPORTED, "moce_mix_px: H*W=%lld", (long long)HW);
+    }
+#undef MOCE_PX_PICK
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return set_error(MOCE_ERR_CUDA, "moce_mix_px: cannot reserve %zu B shared memory", smem);
+    kern<<<dim3((unsigned)nch, (unsigned)B), kPxThreads, smem, (cudaStream_t)stream>>>(a);
+    return check_launch("mix_px_kernel");
+  });
+}

@@ -62,12 +62,18 @@ class _Route:
         """Both forward passes; returns (y, z, T).  T is None unless wanted.
 
         bf16/fp16 inputs with H*W <= 64 and C <= 512 run the tensor-core
-        mix; other shapes the scheduled CUDA-core mix (k <= 44) or the general
-        two passes.
+        mix; shapes with H*W <= 512 and k <= 64 whose sample fits shared
+        memory the lanes-over-pixels CUDA-core mix; other shapes the
+        scheduled CUDA-core mix (k <= 44) or the general two passes.
         """
         m = native()
-        if m.tc_supported(x, self.idx.shape[1]):
+        k = int(self.idx.shape[1])
+        if m.tc_supported(x, k):
             y, z, T = m.forward_tc(x, self.idx, self.ln, self.mask, self.meta, gate_w, gate_b, float(tmin_tau),
+                                   float(trange_tau), bool(want_T), out)
+            return y, z, (T if want_T else None)
+        if m.px_supported(x, k):
+            y, z, T = m.forward_px(x, self.idx, self.ln, self.mask, self.meta, gate_w, gate_b, float(tmin_tau),
                                    float(trange_tau), bool(want_T), out)
             return y, z, (T if want_T else None)
         if self.schedule() is not None:

@@ -97,10 +97,12 @@ def test_route_build_large_rows(E_r, C, k):
 
 # ---------------------------------------------------------------- forward
 
-PATHS = ["general", "fast"]
+PATHS = ["general", "fast", "px"]
 
 
 def path_ok(path, k):
+    if path == "px":
+        return k <= 64
     return path == "general" or H.schedule_supported(k)
 
 
@@ -217,11 +219,15 @@ def test_cfg1_against_pins(path):
     (2, 2048, 7, 7, 64, 128, torch.bfloat16),
     (5, 130, 3, 7, 40, 33, torch.float32),     # ragged everything
     (1, 16, 1, 1, 2, 16, torch.float32),       # k == C, HW == 1, one routed expert
+    (1, 64, 2, 2, 2048, 8, torch.float32),     # E > 1800: the dX kernel without a staged dY tile
+    (2, 96, 13, 11, 50, 20, torch.float32),    # HW = 143: two pixel slabs, rows padded to 144
 ])
 @pytest.mark.parametrize("path", PATHS)
 def test_forward_backward_odd_shapes(B, C, H_, W_, E, k, dtype, path):
     if not path_ok(path, k):
         pytest.skip("k beyond the scheduled kernel")
+    if path == "px" and not H.px_supported(torch.empty(1, C, H_, W_, dtype=dtype), k):
+        pytest.skip("shape beyond the lanes-over-pixels kernel")
     gen = torch.Generator().manual_seed(B * 1000 + C)
     X = torch.randn(B, C, H_, W_, generator=gen).abs()
     L = torch.randn(E - 1, C, generator=gen)
