@@ -376,32 +376,60 @@ __global__ void __launch_bounds__(kPxThreadsB, 1) bwd_px_dx_kernel(
   const int n_u = meta[0];
   const int p = p0 + lane;
   const size_t bek = (size_t)b * E_r * k;
-  for (int c = warp; c < C; c += kPxWarpsB) {
-    const int s0 = toff[c], s1 = toff[c + 1];
-    float acc = 0.0f, dzp = 0.0f;
-    for (int sc = s0; sc < s1; sc += 32) {
-      const int s = sc + lane;
-      int e_l = 0;
-      float a_l = 0.0f;
-      if (s < s1) {
-        const int slot = tslot[s];
-        e_l = slot / k;
-        a_l = ws.a[bek + slot];
-        dzp += ws.dg[(size_t)b * E_r + e_l] * gate_w[slot - e_l * k];
-      }
-      const int n = min(32, s1 - sc);
-      for (int j = 0; j < n; ++j) {
-        const int e = __shfl_sync(kFull, e_l, j);
-        const float a = __shfl_sync(kFull, a_l, j);
-        acc = fmaf(a, s_dy[e * 32 + lane], acc);
-      }
+  // metadata of 32 list entries per lane-load: (expert, weight, gate term);
+  // the next chunk (of this channel or the warp's next one) is fetched
+  // before the current chunk's 32 entries are summed
+  auto fetch = [&](int c, int sc, int& e_l, float& a_l, float& g_l) {
+    const int s1 = toff[c + 1];
+    const int s = sc + lane;
+    e_l = 0;
+    a_l = 0.0f;
+    g_l = 0.0f;
+    if (s < s1) {
+      const int slot = tslot[s];
+      e_l = slot / k;
+      a_l = ws.a[bek + slot];
+      g_l = ws.dg[(size_t)b * E_r + e_l] * gate_w[slot - e_l * k];
     }
+  };
+  int c = warp, sc = (c < C) ? toff[c] : 0;
+  int e_n = 0;
+  float a_n = 0.0f, g_n = 0.0f;
+  if (c < C) fetch(c, sc, e_n, a_n, g_n);
+  float acc = 0.0f, dzp = 0.0f;
+  while (c < C) {
+    const int s1 = toff[c + 1];
+    const int e_l = e_n;
+    const float a_l = a_n;
+    dzp += g_n;
+    const int n = min(32, s1 - sc);
+    // advance to the next chunk and prefetch it
+    int c2 = c, sc2 = sc + 32;
+    if (sc2 >= s1) {
+      c2 = c + kPxWarpsB;
+      sc2 = (c2 < C) ? toff[c2] : 0;
+    }
+    if (c2 < C) fetch(c2, sc2, e_n, a_n, g_n);
+    for (int j = 0; j < n; ++j) {
+      const int e = __shfl_sync(kFull, e_l, j);
+      const float a = __shfl_sync(kFull, a_l, j);
+      acc = fmaf(a, s_dy[e * 32 + lane], acc);
+    }
+    if (c2 == c) {
+      sc = sc2;
+      continue;
+    }
+    // channel c complete
     const float dz = warp_sum(dzp);
     const float rw = (mask[c] == 1 && n_u > 0) ? 1.0f / (float)n_u : 0.0f;
     if (p < HW) {
       if (rw != 0.0f) acc += rw * s_dy[E_r * 32 + lane];
       dx[((size_t)b * C + c) * HW + p] = from_f<T>(acc + dz / (float)HW);
     }
+    acc = 0.0f;
+    dzp = 0.0f;
+    c = c2;
+    sc = sc2;
   }
 }
 
@@ -426,8 +454,18 @@ __global__ void __launch_bounds__(kThreads) bwd_logits_kernel(
   for (int c = lane; c < C; c += 32) dLe[c] = 0.0f;
   double ssel = 0.0;
   for (int i = lane; i < k; i += 32) {
-    float s = 0.0f;
-    for (int b = 0; b < B; ++b) s += ws.dlnb[((size_t)b * E_r + e) * k + i];
+    // eight independent partial sums over the batch (loads in flight),
+    // combined in a fixed order
+    float p8[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+    const size_t stride = (size_t)E_r * k;
+    const float* src = ws.dlnb + (size_t)e * k + i;
+    int b = 0;
+    for (; b + 8 <= B; b += 8) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) p8[u] += src[(size_t)(b + u) * stride];
+    }
+    for (; b < B; ++b) p8[b & 7] += src[(size_t)b * stride];
+    const float s = ((p8[0] + p8[1]) + (p8[2] + p8[3])) + ((p8[4] + p8[5]) + (p8[6] + p8[7]));
     ws.dln[(size_t)e * k + i] = s;
     ssel += (double)Le[ie[i]];
   }
@@ -465,17 +503,24 @@ __global__ void __launch_bounds__(kThreads) bwd_logits_kernel(
   }
 }
 
-// Single CTA: fixed-order sum of the per-CTA gate partials.
+// Fixed-order sum of the per-CTA gate partials: warp w handles gate weight
+// w (w == k: the bias); lane l sums the contiguous range l of the nq
+// partials, then the lanes combine in a fixed butterfly (deterministic).
 __global__ void bwd_gate_reduce_kernel(BwdWs ws, int nq, int k, float* __restrict__ dgw, float* __restrict__ dgb) {
-  for (int i = threadIdx.x; i < k; i += blockDim.x) {
-    float s = 0.0f;
-    for (int q = 0; q < nq; ++q) s += ws.part_w[(size_t)q * k + i];
-    dgw[i] = s;
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (w > k) return;
+  const int per = (nq + 31) / 32;
+  const int q0 = lane * per, q1 = min(nq, q0 + per);
+  float s = 0.0f;
+  if (w < k) {
+    for (int q = q0; q < q1; ++q) s += ws.part_w[(size_t)q * k + w];
+  } else {
+    for (int q = q0; q < q1; ++q) s += ws.part_b[q];
   }
-  if (threadIdx.x == 0) {
-    float s = 0.0f;
-    for (int q = 0; q < nq; ++q) s += ws.part_b[q];
-    dgb[0] = s;
+  s = warp_sum(s);
+  if (lane == 0) {
+    if (w < k) dgw[w] = s;
+    else dgb[0] = s;
   }
 }
 
@@ -576,6 +621,6 @@ extern "C" int moce_backward(const void* x, const void* dy, int dtype, int64_t B
                                                                                   (int)E_r, (int)k, ws, dL);
   rc = check_launch("moce_backward/logits");
   if (rc) return rc;
-  bwd_gate_reduce_kernel<<<1, 256, 0, st>>>(ws, (int)(B * nch), (int)k, dgate_w, dgate_b);
+  bwd_gate_reduce_kernel<<<(unsigned)((k + 1 + 7) / 8), 256, 0, st>>>(ws, (int)(B * nch), (int)k, dgate_w, dgate_b);
   return check_launch("moce_backward/gate");
 }

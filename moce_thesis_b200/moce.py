@@ -195,9 +195,11 @@ class MoCE(nn.Module):
         target = math.log(max(float(self.target_experts_per_channel), 1.0))
         specialization = F.relu(entropy - target).mean()
         if E_routed > 1:
+            # mean of the off-diagonal entries of P P^T (MoCE.py:145-148), as
+            # (sum - trace) / (E (E - 1)): the same quantity without the
+            # boolean-mask gather, whose backward is a sorted scatter
             overlap = P @ P.t()
-            off = ~torch.eye(E_routed, dtype=torch.bool, device=P.device)
-            diversity = overlap[off].mean()
+            diversity = (overlap.sum() - overlap.diagonal().sum()) / float(E_routed * (E_routed - 1))
         else:
             diversity = P.new_zeros(())
         self.aux_loss = (self.balance_weight * balance + self.specialization_weight * specialization
