@@ -213,7 +213,7 @@ def run_ours(args):
     reps = max(args.steps, 20)
 
     if use_tc:
-        nst = capi.lib().moce_tc_stage_bytes(B, C)
+        nst = capi.lib().moce_tc_stage_bytes(B, C, H * W)
         sts = [torch.empty(nst, dtype=torch.uint8, device=dev) for _ in range(nsets)]
 
         def pass1(i):
@@ -272,7 +272,7 @@ def run_ours(args):
     mix_ms = time_loop(pass2)
     # algorithmic bytes of pass 2: its X operand in, routed Y out, z in,
     # supports (int32) and normalised logits (fp32)
-    x_in = capi.lib().moce_tc_stage_bytes(B, C) if use_tc else xb
+    x_in = capi.lib().moce_tc_stage_bytes(B, C, H * W) if use_tc else xb
     mix_bytes = x_in + B * (E - 1) * H * W * esize + B * C * 4 + (E - 1) * K * 8
 
     # end to end through the public API: pinned host X -> layer -> host Y

@@ -107,13 +107,16 @@ int moce_mix_scheduled(const void* x, int dtype, int64_t B, int64_t C,
                        void* y, float* T_out, void* stream);
 
 /*
- * Tensor-core fast path, for bf16 / fp16 inputs with H*W <= 64, C <= 512 and
- * k <= 64 (the 7x7 stage-4 maps).
+ * Tensor-core fast path, for bf16 / fp16 inputs with H*W <= 256, C <= 512 and
+ * k <= 64 whose operands fit the shared memory of one CTA (the 7x7 stage-4
+ * and 14x14 stage-3 maps); moce_tc_supported returns 1 for those.
  *
  * moce_pool_stage: pass 1 as moce_pool_residual, plus a copy of X in the
- * tensor-core operand layout: xstage [B, Kp, 64] 16-bit, Kp = C rounded up to
- * 64, each 128-byte channel row holding 64 zero-padded pixels in 16-byte
- * units swizzled by (channel mod 8).  moce_tc_stage_bytes gives its size.
+ * tensor-core operand layout: per sample, Kp = C rounded up to 64 channel
+ * rows in four K-quarters, the pixels padded to NA = ceil(round16(H*W) / 64)
+ * atoms of 64; stored [quarter][atom][Kp/4 rows][128 bytes], each row's
+ * 16-byte units swizzled by (channel mod 8).  moce_tc_stage_bytes gives its
+ * size.
  *
  * moce_mix_tc: pass 2.  Same outputs as moce_mix_scheduled; the routed
  * experts are computed per sample as a dense product of the 128-expert weight
@@ -123,7 +126,8 @@ int moce_mix_scheduled(const void* x, int dtype, int64_t B, int64_t C,
  * Waits inside the kernel are bounded; moce_tc_fault reads (and optionally
  * clears) the flag a wait that ran out sets.
  */
-size_t moce_tc_stage_bytes(int64_t B, int64_t C);
+int moce_tc_supported(int dtype, int64_t C, int64_t HW, int64_t k);
+size_t moce_tc_stage_bytes(int64_t B, int64_t C, int64_t HW);
 int moce_pool_stage(const void* x, int dtype, int64_t B, int64_t C,
                     int64_t HW, const int32_t* mask, const int32_t* meta,
                     float* z, void* y, int64_t E_r, void* xstage,

@@ -33,7 +33,8 @@ SIGNATURES = {
     "moce_pool_residual": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _p]),
     "moce_mix_scheduled": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _i64, _i64, _p, _p, _p, _p, _f32, _f32,
                                   _p, _p, _p]),
-    "moce_tc_stage_bytes": (_sz, [_i64, _i64]),
+    "moce_tc_stage_bytes": (_sz, [_i64, _i64, _i64]),
+    "moce_tc_supported": (_i32, [_i32, _i64, _i64, _i64]),
     "moce_pool_stage": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _p, _p]),
     "moce_mix_tc": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p, _f32, _f32, _p, _p, _p]),
     "moce_tc_fault": (_i32, [_p, _i32]),

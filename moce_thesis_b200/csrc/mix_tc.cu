@@ -38,7 +38,7 @@ __device__ int g_tc_fault = 0;
 
 namespace {
 
-constexpr int kTcN = 64;                  // padded pixels
+constexpr int kTcMaxN = 256;              // pixels per MMA (N), padded to 16
 constexpr long long kSpinLimit = 1ll << 28;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -122,6 +122,8 @@ struct TcArgs {
   int B, C, HW, E_r, k, Kp;       // Kp: C rounded up to 64
   int n_tiles, n_bsplit;
   int ns;                         // X quarter slots in the ring
+  int NP, NA, P;                  // MMA N (H*W rounded up to 16), 64-pixel atoms, partial accumulators
+  uint32_t tmem_cols;             // tensor-memory columns allocated (power of 2)
 };
 
 constexpr int kMaxSlots = 8;
@@ -264,7 +266,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   // below stays in the shared address space (LDS/STS, not generic accesses)
   unsigned char* base = s_dyn + ((1024u - (smem_u32(s_dyn) & 1023u)) & 1023u);
   const int C = a.C, HW = a.HW, k = a.k, Kp = a.Kp, E_r = a.E_r, NS = a.ns;
-  const uint32_t qbytes = (uint32_t)Kp * 32;                  // a quarter of the channels x 128 B
+  const int NP = a.NP, NA = a.NA, P = a.P;
+  const uint32_t sbytes = (uint32_t)Kp * NA * 128;            // one staged sample
+  const uint32_t qbytes = sbytes / 4;                         // a quarter of the channels, all atoms
   unsigned char* sA = base;                                   // 128 x Kp : Kp * 256 B
   unsigned char* sB = sA + (size_t)Kp * 256;                  // NS quarter slots
   T* stg = reinterpret_cast<T*>(sB + (size_t)NS * qbytes);    // 128 x HW output block
@@ -285,7 +289,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   // ---- prologue.  The producer initializes the barriers and starts the
   // first X copies, and the weight rows start their register loads, before
   // all threads zero A, so that those latencies overlap the zeroing.
-  const unsigned char* xs = static_cast<const unsigned char*>(a.xstage) + (size_t)b0 * Kp * 128;
+  const unsigned char* xs = static_cast<const unsigned char*>(a.xstage) + (size_t)b0 * sbytes;
   const int n_pre = min(NS, 4 * nb);                          // copies issued in the prologue
   if (tid == kWarpProducer * 32) {
     for (int s = 0; s < NS; ++s) {
@@ -295,7 +299,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     for (int h = 0; h < 2; ++h) {
       mbar_init(&bars->a_full[h], kWeightThreads);
       mbar_init(&bars->a_free[h], 1);
-      mbar_init(&bars->d_full[h], 2);
+      mbar_init(&bars->d_full[h], P);
       mbar_init(&bars->d_empty[h], kDrainThreads);
       mbar_init(&bars->fin[h], 1);
     }
@@ -303,7 +307,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     for (int n = 0; n < n_pre; ++n) {
       mbar_expect_tx(&bars->full_b[n], qbytes);
-      bulk_g2s(smem_u32(sB) + (uint32_t)n * qbytes, xs + (size_t)(n >> 2) * Kp * 128 + (size_t)(n & 3) * qbytes,
+      bulk_g2s(smem_u32(sB) + (uint32_t)n * qbytes, xs + (size_t)(n >> 2) * sbytes + (size_t)(n & 3) * qbytes,
                qbytes, &bars->full_b[n]);
     }
   }
@@ -345,7 +349,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   for (int q = tid; q < Kp * 256 / 16; q += blockDim.x) reinterpret_cast<int4*>(sA)[q] = make_int4(0, 0, 0, 0);
   for (int i = tid; i < k; i += blockDim.x) s_gw[i] = a.gate_w[i];
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(&bars->tmem)));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&bars->tmem)),
+                 "r"(a.tmem_cols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   proxy_fence_smem();                                         // zeroed A visible to the tensor cores
@@ -364,7 +369,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         const int slot = n % NS, use = n / NS;
         if (use >= 1 && !mbar_wait_abort(&bars->slot_free[slot], (use - 1) & 1, abort)) break;
         mbar_expect_tx(&bars->full_b[slot], qbytes);
-        bulk_g2s(aB + (uint32_t)slot * qbytes, xs + (size_t)(n >> 2) * Kp * 128 + (size_t)(n & 3) * qbytes, qbytes,
+        bulk_g2s(aB + (uint32_t)slot * qbytes, xs + (size_t)(n >> 2) * sbytes + (size_t)(n & 3) * qbytes, qbytes,
                  &bars->full_b[slot]);
       }
       // copies still in flight land before the block can exit (no-op on the
@@ -372,45 +377,58 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       for (int m = (n > NS ? n - NS : 0); m < n; ++m) mbar_wait(&bars->full_b[m % NS], (m / NS) & 1);
     }
   } else if (warp == kWarpIssuer0 || warp == kWarpIssuer0 + 1) {
-    // ===================== MMA issuers: K-half h into partial accumulator h
-    if (lane == 0) {
-      const int h = warp - kWarpIssuer0;
-      const uint32_t idesc = umma_idesc(DTypeOf<T>::value == MOCE_BF16 ? 1 : 0, 128, kTcN);
+    // ===================== MMA issuers.  P == 2: issuer h takes K-half h
+    // into partial accumulator h.  P == 1 (wide N, where two buffers of two
+    // partials would not fit tensor memory and one thread keeps the
+    // longer MMAs fed): issuer 0 takes both halves into one accumulator.
+    const int hi = warp - kWarpIssuer0;
+    if (lane == 0 && hi < P) {
+      const uint32_t idesc = umma_idesc(DTypeOf<T>::value == MOCE_BF16 ? 1 : 0, 128, NP);
       const uint64_t da0 = umma_desc(smem_u32(sA), 16, 1024);
       const uint32_t aB = smem_u32(sB);
       const int kq = Kp / 64;                                 // K-steps (16 channels) per quarter
+      // B slot: NA atoms of Kq channel rows x 128 B; atoms Kq * 128 B apart
+      // (leading byte offset), 8-row groups 1024 B apart (stride byte offset)
+      const uint32_t atom_stride = (uint32_t)(Kp / 4) * 128;
       bool run = true;
       for (int i = 0; i < nb && run; ++i) {
         const int s = i & 1;
         if (i >= 2 && !mbar_wait_abort(&bars->d_empty[s], ((i - 2) >> 1) & 1, abort)) break;
-        if (!mbar_wait_abort(&bars->a_full[h], i & 1, abort)) break;
-        tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(s * 2 * kTcN + h * kTcN);
-        for (int qq = 0; qq < 2; ++qq) {
-          const int q = 2 * h + qq, n = 4 * i + q, slot = n % NS;
-          if (!mbar_wait_abort(&bars->full_b[slot], (n / NS) & 1, abort)) {
+        for (int h = (P == 2 ? hi : 0); h < (P == 2 ? hi + 1 : 2) && run; ++h) {
+          if (!mbar_wait_abort(&bars->a_full[h], i & 1, abort)) {
             run = false;
             break;
           }
           tc_fence_after();
-          const uint64_t db0 = umma_desc(aB + (uint32_t)slot * qbytes, qbytes, 1024);
-          for (int jj = 0; jj < kq; ++jj) {
-            const int j = q * kq + jj;                        // K-step over all channels
-            // start-address fields advance in 16-byte units (no carry: shared
-            // addresses are below 2^18)
-            const uint64_t da = da0 + (uint64_t)(((j >> 2) * 16384 + (j & 3) * 32) >> 4);
-            const uint64_t db = db0 + (uint64_t)(jj * 128);
-            umma_f16(d, da, db, idesc, (qq > 0 || jj > 0) ? 1u : 0u);
+          const uint32_t d = tmem + (uint32_t)(s * P * NP + (P == 2 ? h : 0) * NP);
+          for (int qq = 0; qq < 2; ++qq) {
+            const int q = 2 * h + qq, n = 4 * i + q, slot = n % NS;
+            if (!mbar_wait_abort(&bars->full_b[slot], (n / NS) & 1, abort)) {
+              run = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t db0 = umma_desc(aB + (uint32_t)slot * qbytes, atom_stride, 1024);
+            for (int jj = 0; jj < kq; ++jj) {
+              const int j = q * kq + jj;                      // K-step over all channels
+              // start-address fields advance in 16-byte units (no carry:
+              // shared addresses are below 2^18)
+              const uint64_t da = da0 + (uint64_t)(((j >> 2) * 16384 + (j & 3) * 32) >> 4);
+              const uint64_t db = db0 + (uint64_t)(jj * 128);
+              const bool first = (P == 2 || h == 0) && qq == 0 && jj == 0;
+              umma_f16(d, da, db, idesc, first ? 0u : 1u);
+            }
+            umma_commit(&bars->slot_free[slot]);
           }
-          umma_commit(&bars->slot_free[slot]);
+          if (!run) break;
+          umma_commit(&bars->a_free[h]);
         }
         if (!run) break;
-        umma_commit(&bars->a_free[h]);
         umma_commit(&bars->d_full[s]);
       }
       // every MMA of this thread completes before the block exits
-      umma_commit(&bars->fin[h]);
-      mbar_wait(&bars->fin[h], 0);
+      umma_commit(&bars->fin[hi]);
+      mbar_wait(&bars->fin[hi], 0);
     }
   } else if (tid < kWeightThreads) {
     // ===================== weight rows (pairs of threads per row)
@@ -498,18 +516,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       }
       if (!role_sync_and(kBarDrain, kDrainThreads, ok)) break;
       tc_fence_after();
-      const uint32_t tb = tmem + lane_base + (uint32_t)(s * 2 * kTcN);
-#pragma unroll
-      for (int cb = 0; cb < kTcN; cb += 32) {
-        if (cb >= HW) break;                                  // uniform across the warp
+      const uint32_t tb = tmem + lane_base + (uint32_t)(s * P * NP);
+      for (int cb = 0; cb < HW; cb += 32) {                   // uniform across the warp
         uint32_t r0[32], r1[32];
         tmem_ld32_nowait(tb + cb, r0);
-        tmem_ld32_nowait(tb + kTcN + cb, r1);
+        if (P == 2) tmem_ld32_nowait(tb + NP + cb, r1);
         tmem_wait_ld();
         if (has_row) {
+          if (P == 2) {
 #pragma unroll
-          for (int p = 0; p < 32; ++p)
-            if (cb + p < HW) stg[dt * HW + cb + p] = from_f<T>(__uint_as_float(r0[p]) + __uint_as_float(r1[p]));
+            for (int p = 0; p < 32; ++p)
+              if (cb + p < HW) stg[dt * HW + cb + p] = from_f<T>(__uint_as_float(r0[p]) + __uint_as_float(r1[p]));
+          } else {
+#pragma unroll
+            for (int p = 0; p < 32; ++p)
+              if (cb + p < HW) stg[dt * HW + cb + p] = from_f<T>(__uint_as_float(r0[p]));
+          }
         }
       }
       tc_fence_before();
@@ -530,21 +552,58 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_cols));
 }
 
 }  // namespace
 
+struct TcShape {
+  int Kp, NP, NA, P, KMAX;
+  uint32_t tmem_cols;
+  size_t fixed, qbytes;           // shared memory without the X ring, bytes per ring slot
+};
+
+TcShape tc_shape(int64_t C, int64_t HW, int64_t k) {
+  TcShape t;
+  t.Kp = (int)((C + 63) / 64 * 64);
+  t.NP = (int)((HW + 15) / 16 * 16);
+  t.NA = (t.NP + 63) / 64;
+  t.P = (4 * t.NP <= 512) ? 2 : 1;
+  uint32_t cols = 32;
+  while (cols < (uint32_t)(2 * t.P * t.NP)) cols <<= 1;
+  t.tmem_cols = cols;
+  t.KMAX = k <= 16 ? 16 : k <= 32 ? 32 : 64;
+  t.qbytes = (size_t)t.Kp * t.NA * 32;
+  t.fixed = 1024 + (size_t)t.Kp * 256 + tc_stage_out_bytes((int)HW, 2) + (size_t)t.Kp * 8 + (size_t)t.KMAX * 4 +
+            sizeof(TcBars);
+  return t;
+}
+
+int smem_optin_tc() {
+  int dev = 0, smem_max = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  return smem_max;
+}
+
 int tc_supported(int dtype, int64_t C, int64_t HW, int64_t k) {
-  return (dtype == MOCE_BF16 || dtype == MOCE_F16) && HW >= 1 && HW <= kTcN && k <= 64 && C <= 512;
+  if (!(dtype == MOCE_BF16 || dtype == MOCE_F16) || HW < 1 || HW > kTcMaxN || k < 1 || k > 64 || C < 1 || C > 512)
+    return 0;
+  const TcShape t = tc_shape(C, HW, k);
+  return t.fixed + 2 * t.qbytes <= (size_t)smem_optin_tc() ? 1 : 0;
 }
 
 }  // namespace moce
 
 using namespace moce;
 
-extern "C" size_t moce_tc_stage_bytes(int64_t B, int64_t C) {
-  return (size_t)B * (size_t)((C + 63) / 64 * 64) * 128;
+extern "C" int moce_tc_supported(int dtype, int64_t C, int64_t HW, int64_t k) {
+  return tc_supported(dtype, C, HW, k);
+}
+
+extern "C" size_t moce_tc_stage_bytes(int64_t B, int64_t C, int64_t HW) {
+  const int64_t NA = ((HW + 15) / 16 * 16 + 63) / 64;
+  return (size_t)B * (size_t)((C + 63) / 64 * 64) * (size_t)(NA < 1 ? 1 : NA) * 128;
 }
 
 extern "C" int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
@@ -557,17 +616,13 @@ extern "C" int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C, 
   MOCE_REQUIRE(B > 0 && C >= 1 && HW >= 1 && E_r >= 1 && k >= 1 && k <= C, MOCE_ERR_INVALID,
                "moce_mix_tc: invalid shape");
   MOCE_REQUIRE(tc_supported(dtype, C, HW, k), MOCE_ERR_UNSUPPORTED,
-               "moce_mix_tc: needs bf16/fp16, H*W <= 64, C <= 512, k <= 64");
+               "moce_mix_tc: needs bf16/fp16, H*W <= 256, C <= 512, k <= 64 within shared memory");
   MOCE_REQUIRE(((uintptr_t)xstage & 15) == 0, MOCE_ERR_INVALID, "moce_mix_tc: xstage must be 16-byte aligned");
   MOCE_REQUIRE(B < 65536 && (E_r + 1) * HW < (int64_t)1 << 31, MOCE_ERR_UNSUPPORTED, "moce_mix_tc: shape too large");
-  const int Kp = (int)((C + 63) / 64 * 64);
-  const int KMAX = k <= 16 ? 16 : k <= 32 ? 32 : 64;
-  const size_t qbytes = (size_t)Kp * 32;
-  const size_t fixed = 1024 + (size_t)Kp * 256 + tc_stage_out_bytes((int)HW, 2) + (size_t)Kp * 8 +
-                       (size_t)KMAX * 4 + sizeof(TcBars);
-  int dev = 0, smem_max = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  const TcShape sh = tc_shape(C, HW, k);
+  const int Kp = sh.Kp, KMAX = sh.KMAX;
+  const size_t qbytes = sh.qbytes, fixed = sh.fixed;
+  const int smem_max = smem_optin_tc();
   const int ns = (int)std::min<size_t>((size_t)kMaxSlots, ((size_t)smem_max > fixed ? smem_max - fixed : 0) / qbytes);
   MOCE_REQUIRE(ns >= 2, MOCE_ERR_UNSUPPORTED, "moce_mix_tc: not enough shared memory (%d B)", smem_max);
   const size_t smem = fixed + (size_t)ns * qbytes;
@@ -576,7 +631,7 @@ extern "C" int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C, 
   if (n_bsplit < 1) n_bsplit = 1;
   if (n_bsplit > B) n_bsplit = (int)B;
   TcArgs a{xstage, y, z, idx, ln, gate_w, gate_b, T_out, tmin_tau, trange_tau,
-           (int)B, (int)C, (int)HW, (int)E_r, (int)k, Kp, n_tiles, n_bsplit, ns};
+           (int)B, (int)C, (int)HW, (int)E_r, (int)k, Kp, n_tiles, n_bsplit, ns, sh.NP, sh.NA, sh.P, sh.tmem_cols};
   return dispatch_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
     if constexpr (sizeof(T) != 2) {

@@ -416,8 +416,7 @@ std::vector<torch::Tensor> forward_scheduled(torch::Tensor x, torch::Tensor ln, 
 
 bool tc_supported(torch::Tensor x, int64_t k) {
   if (!(x.scalar_type() == torch::kBFloat16 || x.scalar_type() == torch::kFloat16) || x.dim() != 4) return false;
-  const int64_t C = x.size(1), HW = x.size(2) * x.size(3);
-  return C <= 512 && HW <= 64 && k >= 1 && k <= 64;
+  return moce_tc_supported(dtype_of(x), x.size(1), x.size(2) * x.size(3), k) != 0;
 }
 
 // pass 1 (pool + residual) and the tensor-core pass 2
@@ -441,7 +440,7 @@ std::vector<torch::Tensor> forward_tc(torch::Tensor x, torch::Tensor idx, torch:
   }
   auto z = f32_opts_like(x, {d.B, d.C});
   auto T = want_T ? f32_opts_like(x, {d.B, d.E_r}) : f32_opts_like(x, {0});
-  auto xstage = torch::empty({(int64_t)moce_tc_stage_bytes(d.B, d.C)}, x.options().dtype(torch::kUInt8));
+  auto xstage = torch::empty({(int64_t)moce_tc_stage_bytes(d.B, d.C, d.HW)}, x.options().dtype(torch::kUInt8));
   ok(moce_pool_stage(x.data_ptr(), dtype_of(x), d.B, d.C, d.HW, mask.data_ptr<int32_t>(), meta.data_ptr<int32_t>(),
                      z.data_ptr<float>(), y.data_ptr(), d.E_r, xstage.data_ptr(), cur_stream()));
   ok(moce_mix_tc(xstage.data_ptr(), dtype_of(x), d.B, d.C, d.HW, z.data_ptr<float>(), idx.data_ptr<int32_t>(),

@@ -9,9 +9,11 @@
 // flight per SM.  The per-pixel residual sums of the quarters are added up
 // by cluster rank 0 through distributed shared memory.
 //
-// Operand layout (matches the B operand of mix_tc.cu): per sample Kp rows of
-// 128 bytes, row c = 64 pixels (zero padded); the 16-byte unit j of row c
-// holds pixels 8 (j ^ (c & 7)) .. +7; rows C .. Kp-1 are zero.
+// Operand layout (matches the B operand of mix_tc.cu): the pixels, padded to
+// NA = ceil(round16(H*W) / 64) atoms of 64, and per sample four K-quarters of
+// Kq = Kp / 4 channels, stored [quarter][atom][Kq rows][128 bytes]; in row c
+// of atom a the 16-byte unit j holds pixels 64 a + 8 (j ^ (c & 7)) .. +7
+// (zero beyond H*W); rows C .. Kp-1 are zero.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -28,7 +30,7 @@ template <typename T>
 __global__ void __cluster_dims__(kStageCtas, 1, 1) __launch_bounds__(kStageThreads)
     pool_stage_kernel(const T* __restrict__ x, int C, int HW, int cc, const int32_t* __restrict__ mask,
                       const int32_t* __restrict__ meta, float* __restrict__ z, T* __restrict__ y, int E,
-                      int4* __restrict__ xstage, int Kp) {
+                      int4* __restrict__ xstage, int Kp, int NA) {
   extern __shared__ __align__(16) unsigned char s_raw[];
   T* s_x = reinterpret_cast<T*>(s_raw);                                            // cc x HW
   float* s_res = reinterpret_cast<float*>(s_raw + (((size_t)cc * HW * sizeof(T) + 15) & ~size_t(15)));  // 64
@@ -105,11 +107,13 @@ __global__ void __cluster_dims__(kStageCtas, 1, 1) __launch_bounds__(kStageThrea
   if (n_u > 0) asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   // operand layout; the CTA holding channel C-1 also writes the zero rows
   {
-    int4* xs = xstage + (size_t)b * Kp * 8;
+    int4* xs = xstage + (size_t)b * Kp * NA * 8;
+    const int Kq = Kp / 4;
     const int row_end = (cn > 0 && c1 == C) ? Kp : c1;
-    for (int q = tid; q < (row_end - c0) * 8; q += kStageThreads) {
-      const int c = c0 + (q >> 3), j = q & 7;
-      const int pb = (j ^ (c & 7)) * 8;
+    const int units = (row_end - c0) * NA * 8;               // 16-byte units: channel, atom, chunk
+    for (int q = tid; q < units; q += kStageThreads) {
+      const int j = q & 7, at = (q >> 3) % NA, c = c0 + (q >> 3) / NA;
+      const int pb = at * 64 + (j ^ (c & 7)) * 8;
       union {
         int4 v;
         T e[8];
@@ -117,7 +121,7 @@ __global__ void __cluster_dims__(kStageCtas, 1, 1) __launch_bounds__(kStageThrea
 #pragma unroll
       for (int t = 0; t < 8; ++t)
         u.e[t] = (c < C && pb + t < HW) ? s_x[(size_t)(c - c0) * HW + pb + t] : from_f<T>(0.0f);
-      xs[(size_t)c * 8 + j] = u.v;
+      xs[(((size_t)(c / Kq) * NA + at) * Kq + (c % Kq)) * 8 + j] = u.v;
     }
   }
   if (n_u > 0) {
@@ -151,13 +155,14 @@ extern "C" int moce_pool_stage(const void* x, int dtype, int64_t B, int64_t C, i
   MOCE_REQUIRE(!y || (mask && meta), MOCE_ERR_INVALID, "moce_pool_stage: the residual needs mask and meta");
   MOCE_REQUIRE(dtype == MOCE_BF16 || dtype == MOCE_F16, MOCE_ERR_UNSUPPORTED, "moce_pool_stage: 16-bit inputs only");
   MOCE_REQUIRE(B > 0 && C >= 1 && HW >= 1 && E_r >= 0, MOCE_ERR_INVALID, "moce_pool_stage: invalid shape");
-  MOCE_REQUIRE(HW <= 64, MOCE_ERR_UNSUPPORTED, "moce_pool_stage: H*W must be <= 64");
+  MOCE_REQUIRE(HW <= 256, MOCE_ERR_UNSUPPORTED, "moce_pool_stage: H*W must be <= 256");
   MOCE_REQUIRE(B < 65536 && C <= 4096, MOCE_ERR_UNSUPPORTED, "moce_pool_stage: shape too large");
   // channels per CTA: a multiple of 8, so that every chunk starts on a
   // 16-byte boundary of the sample
   const int cc = (int)(((C + kStageCtas - 1) / kStageCtas + 7) / 8 * 8);
   const size_t smem = (((size_t)cc * HW * 2 + 15) & ~size_t(15)) + 64 * 4 + (size_t)cc * 4;
   const int Kp = (int)((C + 63) / 64 * 64);
+  const int NA = (int)(((HW + 15) / 16 * 16 + 63) / 64);
   return dispatch_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
     if constexpr (sizeof(T) != 2) {
@@ -170,7 +175,7 @@ extern "C" int moce_pool_stage(const void* x, int dtype, int64_t B, int64_t C, i
       const dim3 grid(kStageCtas, (unsigned)B);
       pool_stage_kernel<T><<<grid, kStageThreads, smem, (cudaStream_t)stream>>>(
           static_cast<const T*>(x), (int)C, (int)HW, cc, mask, meta, z, static_cast<T*>(y), (int)(E_r + 1),
-          reinterpret_cast<int4*>(xstage), Kp);
+          reinterpret_cast<int4*>(xstage), Kp, NA);
       return check_launch("pool_stage_kernel");
     }
   });

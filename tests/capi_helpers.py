@@ -78,7 +78,7 @@ def forward_fast(x, r, gate_w, gate_b, tmin_tau, trange_tau, want_T=True):
 
 def tc_supported(x, k):
     C, HW = x.shape[1], x.shape[2] * x.shape[3]
-    return x.dtype in (torch.bfloat16, torch.float16) and C <= 512 and HW <= 64 and 1 <= k <= 64
+    return bool(capi.lib().moce_tc_supported(dtype_code(x), C, HW, k))
 
 
 def forward_tc(x, r, gate_w, gate_b, tmin_tau, trange_tau, want_T=True):
@@ -88,7 +88,7 @@ def forward_tc(x, r, gate_w, gate_b, tmin_tau, trange_tau, want_T=True):
     y = torch.empty(B, E_r + 1, H, W, dtype=x.dtype, device=x.device)
     z = torch.empty(B, C, dtype=torch.float32, device=x.device)
     T = torch.empty(B, E_r, dtype=torch.float32, device=x.device) if want_T else None
-    xs = torch.empty(capi.lib().moce_tc_stage_bytes(B, C), dtype=torch.uint8, device=x.device)
+    xs = torch.empty(capi.lib().moce_tc_stage_bytes(B, C, H * W), dtype=torch.uint8, device=x.device)
     call("moce_pool_stage", ptr(x), dtype_code(x), B, C, H * W, ptr(r["mask"]), ptr(r["meta"]), ptr(z), ptr(y),
          E_r, ptr(xs), stream_handle())
     call("moce_mix_tc", ptr(xs), dtype_code(x), B, C, H * W, ptr(z), ptr(r["idx"]), ptr(r["ln"]), E_r, k,

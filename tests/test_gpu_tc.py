@@ -37,6 +37,9 @@ def relerr(a, b):
     (2, 96, 8, 8, 129, 40, torch.bfloat16),     # HW == 64 exactly
     (3, 64, 3, 11, 40, 8, torch.bfloat16),      # HW == 33: odd rows carry column 31 to the last column
     (2, 192, 6, 6, 70, 12, torch.float16),      # HW == 36, even rows
+    (2, 256, 14, 14, 300, 16, torch.bfloat16),  # 14x14: N = 208 over four pixel atoms, one accumulator
+    (2, 128, 10, 10, 140, 8, torch.float16),    # HW == 100: N = 112 over two atoms, two partial accumulators
+    (2, 64, 16, 16, 40, 12, torch.bfloat16),    # HW == 256: N = 256, the largest tile
 ])
 def test_tc_mix_matches_oracle(B, C, H_, W_, E, k, dtype):
     gen = torch.Generator().manual_seed(B * 100 + C + k)
