@@ -122,8 +122,11 @@ struct TcArgs {
   int B, C, HW, E_r, k, Kp;       // Kp: C rounded up to 64
   int n_tiles, n_bsplit;
   int ns;                         // X quarter slots in the ring
-  int NP, NA, P;                  // MMA N (H*W rounded up to 16), 64-pixel atoms, partial accumulators
+  int NP, NA, P;                  // MMA N (pixel tile, a multiple of 16), 64-pixel atoms, partial accumulators
+  int NT;                         // pixel tiles per sample (NP pixels each, the last one shorter)
   uint32_t tmem_cols;             // tensor-memory columns allocated (power of 2)
+  int direct;                     // tiled rows go from registers to Y (no shared staging block)
+  int stg_pitch;                  // output staging row pitch (elements), 0 when direct
 };
 
 constexpr int kMaxSlots = 8;
@@ -217,6 +220,12 @@ __device__ __forceinline__ unsigned short bits16(T v) {
   return *reinterpret_cast<const unsigned short*>(&v);
 }
 
+// two outputs as one 32-bit word, the first in the low half (lower address)
+template <typename T>
+__device__ __forceinline__ uint32_t pack2_16(float lo, float hi) {
+  return (uint32_t)bits16(from_f<T>(lo)) | ((uint32_t)bits16(from_f<T>(hi)) << 16);
+}
+
 __device__ __forceinline__ void role_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
@@ -259,20 +268,22 @@ __host__ __device__ constexpr size_t tc_stage_out_bytes(int HW, int esize) {
 //   warp 14     lane 0: producer, bulk copies of the staged X quarters into
 //               a ring of `ns` slots, running ahead of the MMAs
 // Tensor memory: 2 accumulator buffers x 2 partials x 64 columns.
-template <typename T, int KMAX>
+// kGen: N, atoms, partials and tiles from the arguments; otherwise the 7x7
+// stage-4 case (N = 64, one atom, two partials, one tile) as constants.
+template <typename T, int KMAX, bool kGen>
 __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   extern __shared__ unsigned char s_dyn[];
   // 1024-byte aligned operand base, offset from s_dyn so that every pointer
   // below stays in the shared address space (LDS/STS, not generic accesses)
   unsigned char* base = s_dyn + ((1024u - (smem_u32(s_dyn) & 1023u)) & 1023u);
   const int C = a.C, HW = a.HW, k = a.k, Kp = a.Kp, E_r = a.E_r, NS = a.ns;
-  const int NP = a.NP, NA = a.NA, P = a.P;
-  const uint32_t sbytes = (uint32_t)Kp * NA * 128;            // one staged sample
+  const int NP = kGen ? a.NP : 64, NA = kGen ? a.NA : 1, P = kGen ? a.P : 2, NT = kGen ? a.NT : 1;
+  const uint32_t sbytes = (uint32_t)Kp * NA * 128;            // one staged (sample, pixel tile)
   const uint32_t qbytes = sbytes / 4;                         // a quarter of the channels, all atoms
   unsigned char* sA = base;                                   // 128 x Kp : Kp * 256 B
   unsigned char* sB = sA + (size_t)Kp * 256;                  // NS quarter slots
-  T* stg = reinterpret_cast<T*>(sB + (size_t)NS * qbytes);    // 128 x HW output block
-  float* s_z = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(stg) + tc_stage_out_bytes(HW, sizeof(T)));
+  T* stg = reinterpret_cast<T*>(sB + (size_t)NS * qbytes);    // 128 x (tile pixels) output block
+  float* s_z = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(stg) + tc_stage_out_bytes(a.stg_pitch, sizeof(T)));
   float* s_gw = s_z + 2 * Kp;
   TcBars* bars = reinterpret_cast<TcBars*>(s_gw + KMAX);
   volatile int* abort = &bars->abort;
@@ -289,8 +300,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   // ---- prologue.  The producer initializes the barriers and starts the
   // first X copies, and the weight rows start their register loads, before
   // all threads zero A, so that those latencies overlap the zeroing.
-  const unsigned char* xs = static_cast<const unsigned char*>(a.xstage) + (size_t)b0 * sbytes;
-  const int n_pre = min(NS, 4 * nb);                          // copies issued in the prologue
+  const unsigned char* xs = static_cast<const unsigned char*>(a.xstage) + (size_t)b0 * NT * sbytes;
+  const int nu = nb * NT;                                     // units (sample, pixel tile) of this CTA
+  const int n_pre = min(NS, 4 * nu);                          // copies issued in the prologue
   if (tid == kWarpProducer * 32) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&bars->full_b[s], 1);
@@ -363,7 +375,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     // ===================== producer
     if (lane == 0) {
       const uint32_t aB = smem_u32(sB);
-      const int total = 4 * nb;
+      const int total = 4 * nu;
       int n = n_pre;
       for (; n < total; ++n) {
         const int slot = n % NS, use = n / NS;
@@ -390,41 +402,56 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       // B slot: NA atoms of Kq channel rows x 128 B; atoms Kq * 128 B apart
       // (leading byte offset), 8-row groups 1024 B apart (stride byte offset)
       const uint32_t atom_stride = (uint32_t)(Kp / 4) * 128;
+      const int h0 = (P == 2) ? hi : 0, h1 = (P == 2) ? hi + 1 : 2;
       bool run = true;
       for (int i = 0; i < nb && run; ++i) {
-        const int s = i & 1;
-        if (i >= 2 && !mbar_wait_abort(&bars->d_empty[s], ((i - 2) >> 1) & 1, abort)) break;
-        for (int h = (P == 2 ? hi : 0); h < (P == 2 ? hi + 1 : 2) && run; ++h) {
-          if (!mbar_wait_abort(&bars->a_full[h], i & 1, abort)) {
-            run = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t d = tmem + (uint32_t)(s * P * NP + (P == 2 ? h : 0) * NP);
-          for (int qq = 0; qq < 2; ++qq) {
-            const int q = 2 * h + qq, n = 4 * i + q, slot = n % NS;
-            if (!mbar_wait_abort(&bars->full_b[slot], (n / NS) & 1, abort)) {
+        // one tile per sample: the accumulator buffer first, as it frees
+        // earlier than the next weights
+        if (NT == 1 && i >= 2 && !mbar_wait_abort(&bars->d_empty[i & 1], ((i - 2) >> 1) & 1, abort)) break;
+        // this sample's weights (A), both halves of this issuer
+        for (int h = h0; h < h1 && run; ++h)
+          if (!mbar_wait_abort(&bars->a_full[h], i & 1, abort)) run = false;
+        if (!run) break;
+        tc_fence_after();
+        for (int t = 0; t < NT && run; ++t) {
+          const int u = i * NT + t, s = u & 1;
+          if (NT > 1 && u >= 2) {
+            if (!mbar_wait_abort(&bars->d_empty[s], ((u - 2) >> 1) & 1, abort)) {
               run = false;
               break;
             }
             tc_fence_after();
-            const uint64_t db0 = umma_desc(aB + (uint32_t)slot * qbytes, atom_stride, 1024);
-            for (int jj = 0; jj < kq; ++jj) {
-              const int j = q * kq + jj;                      // K-step over all channels
-              // start-address fields advance in 16-byte units (no carry:
-              // shared addresses are below 2^18)
-              const uint64_t da = da0 + (uint64_t)(((j >> 2) * 16384 + (j & 3) * 32) >> 4);
-              const uint64_t db = db0 + (uint64_t)(jj * 128);
-              const bool first = (P == 2 || h == 0) && qq == 0 && jj == 0;
-              umma_f16(d, da, db, idesc, first ? 0u : 1u);
+          }
+          for (int h = h0; h < h1 && run; ++h) {
+            const uint32_t d = tmem + (uint32_t)(s * P * NP + (P == 2 ? h : 0) * NP);
+            for (int qq = 0; qq < 2; ++qq) {
+              const int q = 2 * h + qq, n = 4 * u + q, slot = n % NS;
+              if (!mbar_wait_abort(&bars->full_b[slot], (n / NS) & 1, abort)) {
+                run = false;
+                break;
+              }
+              tc_fence_after();
+              const uint64_t db0 = umma_desc(aB + (uint32_t)slot * qbytes, atom_stride, 1024);
+              for (int jj = 0; jj < kq; ++jj) {
+                const int j = q * kq + jj;                      // K-step over all channels
+                // start-address fields advance in 16-byte units (no carry:
+                // shared addresses are below 2^18)
+                const uint64_t da = da0 + (uint64_t)(((j >> 2) * 16384 + (j & 3) * 32) >> 4);
+                const uint64_t db = db0 + (uint64_t)(jj * 128);
+                const bool first = (P == 2 || h == 0) && qq == 0 && jj == 0;
+                umma_f16(d, da, db, idesc, first ? 0u : 1u);
+              }
+              umma_commit(&bars->slot_free[slot]);
             }
-            umma_commit(&bars->slot_free[slot]);
           }
           if (!run) break;
-          umma_commit(&bars->a_free[h]);
+          // the last tile of the sample releases its weights (first, for the
+          // weight rows wait on it) and every tile its accumulator buffer
+          if (t == NT - 1)
+            for (int h = h0; h < h1; ++h) umma_commit(&bars->a_free[h]);
+          umma_commit(&bars->d_full[s]);
         }
         if (!run) break;
-        umma_commit(&bars->d_full[s]);
       }
       // every MMA of this thread completes before the block exits
       umma_commit(&bars->fin[hi]);
@@ -507,17 +534,64 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     const bool has_row = dt < rows;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     T* yg = static_cast<T*>(a.y);
-    for (int i = 0; i < nb; ++i) {
-      const int s = i & 1;
+    // pixel-tiled samples with 16-byte aligned rows: the rows go straight from
+    // registers to Y with 16-byte stores (a shared staging block of rows
+    // 2 * NP bytes apart would put a warp's rows in a few banks)
+    const bool direct = kGen && a.direct != 0;
+    for (int u = 0; u < nu && direct; ++u) {
+      const int s = u & 1, i = u / NT, t = u - (u / NT) * NT;
+      const int p0 = t * NP, tp = min(NP, HW - p0);
       bool ok = true;
-      if (dt == 0) {
-        ok = mbar_wait_abort(&bars->d_full[s], (i >> 1) & 1, abort);
-        bulk_wait_read();                                     // previous block left the staging area
-      }
+      if (dt == 0) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
       if (!role_sync_and(kBarDrain, kDrainThreads, ok)) break;
       tc_fence_after();
       const uint32_t tb = tmem + lane_base + (uint32_t)(s * P * NP);
-      for (int cb = 0; cb < HW; cb += 32) {                   // uniform across the warp
+      T* dst = yg + ((size_t)(b0 + i) * E + e0 + dt) * HW + p0;
+      for (int cb = 0; cb < tp; cb += 32) {                   // uniform across the warp
+        uint32_t r0[32], r1[32];
+        tmem_ld32_nowait(tb + cb, r0);
+        if (P == 2) tmem_ld32_nowait(tb + NP + cb, r1);
+        tmem_wait_ld();
+        if (cb + 32 >= tp) {                                  // last read of the buffer
+          tc_fence_before();
+          mbar_arrive(&bars->d_empty[s]);
+        }
+        if (has_row) {
+          float v[32];
+#pragma unroll
+          for (int p = 0; p < 32; ++p)
+            v[p] = (P == 2) ? __uint_as_float(r0[p]) + __uint_as_float(r1[p]) : __uint_as_float(r0[p]);
+          if (cb + 32 <= tp) {
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              int4 w;
+              w.x = (int)pack2_16<T>(v[8 * g + 0], v[8 * g + 1]);
+              w.y = (int)pack2_16<T>(v[8 * g + 2], v[8 * g + 3]);
+              w.z = (int)pack2_16<T>(v[8 * g + 4], v[8 * g + 5]);
+              w.w = (int)pack2_16<T>(v[8 * g + 6], v[8 * g + 7]);
+              *reinterpret_cast<int4*>(dst + cb + 8 * g) = w;
+            }
+          } else {
+#pragma unroll
+            for (int p = 0; p < 32; ++p)
+              if (cb + p < tp) dst[cb + p] = from_f<T>(v[p]);
+          }
+        }
+      }
+    }
+    for (int u = 0; u < nu && !direct; ++u) {
+      const int s = u & 1, i = u / NT, t = u - (u / NT) * NT;
+      const int p0 = t * NP, tp = min(NP, HW - p0);           // this tile's pixels
+      bool ok = true;
+      if (dt == 0) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
+      // this thread's copies left the staging area (one tile: only thread 0 copies)
+      if (NT > 1 || dt == 0) bulk_wait_read();
+      if (!role_sync_and(kBarDrain, kDrainThreads, ok)) break;
+      tc_fence_after();
+      const uint32_t tb = tmem + lane_base + (uint32_t)(s * P * NP);
+#pragma unroll
+      for (int cb = 0; cb < (kGen ? kTcMaxN : 64); cb += 32) {
+        if (cb >= tp) break;                                  // uniform across the warp
         uint32_t r0[32], r1[32];
         tmem_ld32_nowait(tb + cb, r0);
         if (P == 2) tmem_ld32_nowait(tb + NP + cb, r1);
@@ -526,11 +600,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
           if (P == 2) {
 #pragma unroll
             for (int p = 0; p < 32; ++p)
-              if (cb + p < HW) stg[dt * HW + cb + p] = from_f<T>(__uint_as_float(r0[p]) + __uint_as_float(r1[p]));
+              if (cb + p < tp) stg[dt * tp + cb + p] = from_f<T>(__uint_as_float(r0[p]) + __uint_as_float(r1[p]));
           } else {
 #pragma unroll
             for (int p = 0; p < 32; ++p)
-              if (cb + p < HW) stg[dt * HW + cb + p] = from_f<T>(__uint_as_float(r0[p]));
+              if (cb + p < tp) stg[dt * tp + cb + p] = from_f<T>(__uint_as_float(r0[p]));
           }
         }
       }
@@ -538,16 +612,29 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       mbar_arrive(&bars->d_empty[s]);
       proxy_fence_smem();
       role_sync(kBarDrain, kDrainThreads);
-      T* dst = yg + ((size_t)(b0 + i) * E + e0) * HW;
-      const uint32_t nbytes = (uint32_t)(rows * HW * sizeof(T));
-      if (((((uintptr_t)dst) | nbytes) & 15) == 0) {
-        if (dt == 0) bulk_s2g(dst, smem_u32(stg), nbytes);
-      } else {
-        for (int q = dt; q < rows * HW; q += kDrainThreads) dst[q] = stg[q];
-        role_sync(kBarDrain, kDrainThreads);
+      if (NT == 1) {
+        // the tile's rows are one contiguous range of Y: one copy
+        T* dst = yg + ((size_t)(b0 + i) * E + e0) * HW;
+        const uint32_t nbytes = (uint32_t)(rows * HW * sizeof(T));
+        if (((((uintptr_t)dst) | nbytes) & 15) == 0) {
+          if (dt == 0) bulk_s2g(dst, smem_u32(stg), nbytes);
+        } else {
+          for (int q = dt; q < rows * HW; q += kDrainThreads) dst[q] = stg[q];
+          role_sync(kBarDrain, kDrainThreads);
+        }
+      } else if (has_row) {
+        // one row segment of Y per thread
+        T* dst = yg + ((size_t)(b0 + i) * E + e0 + dt) * HW + p0;
+        const uint32_t nbytes = (uint32_t)(tp * sizeof(T));
+        const uint32_t src = smem_u32(stg) + (uint32_t)(dt * tp) * (uint32_t)sizeof(T);
+        if (((((uintptr_t)dst) | nbytes | src) & 15) == 0) {
+          bulk_s2g(dst, src, nbytes);
+        } else {
+          for (int p = 0; p < tp; ++p) dst[p] = stg[dt * tp + p];
+        }
       }
     }
-    if (dt == 0) bulk_wait_all();
+    bulk_wait_all();
   }
   tc_fence_before();
   __syncthreads();
@@ -558,24 +645,42 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
 }  // namespace
 
 struct TcShape {
-  int Kp, NP, NA, P, KMAX;
+  int Kp, NP, NT, NA, P, KMAX;
+  int direct_ok, stg_pitch;       // direct row stores possible (given an aligned Y); staging pitch otherwise
   uint32_t tmem_cols;
   size_t fixed, qbytes;           // shared memory without the X ring, bytes per ring slot
 };
 
+// pixel tiling: NT tiles of NP pixels (a multiple of 16, at most 256), the
+// last tile shorter
+void tc_tiling(int64_t HW, int* NP, int* NT, int* NA) {
+  const int64_t nt0 = (HW + kTcMaxN - 1) / kTcMaxN;
+  int64_t np = ((HW + nt0 - 1) / nt0 + 15) / 16 * 16;
+  if (np > kTcMaxN) np = kTcMaxN;
+  *NP = (int)np;
+  *NT = (int)((HW + np - 1) / np);
+  *NA = (int)((np + 63) / 64);
+}
+
 TcShape tc_shape(int64_t C, int64_t HW, int64_t k) {
   TcShape t;
   t.Kp = (int)((C + 63) / 64 * 64);
-  t.NP = (int)((HW + 15) / 16 * 16);
-  t.NA = (t.NP + 63) / 64;
-  t.P = (4 * t.NP <= 512) ? 2 : 1;
+  tc_tiling(HW, &t.NP, &t.NT, &t.NA);
+  // the drain reads 32 columns at a time, so the last read of a region whose
+  // width is not a multiple of 32 reaches 16 columns past it: allocate that
+  const int over = (t.NP % 32) ? 16 : 0;
+  t.P = (4 * t.NP + over <= 512) ? 2 : 1;
   uint32_t cols = 32;
-  while (cols < (uint32_t)(2 * t.P * t.NP)) cols <<= 1;
+  while (cols < (uint32_t)(2 * t.P * t.NP + over)) cols <<= 1;
   t.tmem_cols = cols;
   t.KMAX = k <= 16 ? 16 : k <= 32 ? 32 : 64;
   t.qbytes = (size_t)t.Kp * t.NA * 32;
-  t.fixed = 1024 + (size_t)t.Kp * 256 + tc_stage_out_bytes((int)HW, 2) + (size_t)t.Kp * 8 + (size_t)t.KMAX * 4 +
-            sizeof(TcBars);
+  // one tile: the block is the tile's rows, H*W apart; several tiles: rows
+  // of NP pixels, unless they go to Y directly (16-byte aligned rows)
+  t.direct_ok = t.NT > 1 && (HW % 8) == 0;
+  t.stg_pitch = t.NT == 1 ? (int)HW : (t.direct_ok ? 0 : t.NP);
+  t.fixed = 1024 + (size_t)t.Kp * 256 + tc_stage_out_bytes(t.stg_pitch, 2) + (size_t)t.Kp * 8 +
+            (size_t)t.KMAX * 4 + sizeof(TcBars);
   return t;
 }
 
@@ -586,11 +691,14 @@ int smem_optin_tc() {
   return smem_max;
 }
 
+size_t pool_stage_smem(int64_t C, int64_t HW);   // stage.cu
+
 int tc_supported(int dtype, int64_t C, int64_t HW, int64_t k) {
-  if (!(dtype == MOCE_BF16 || dtype == MOCE_F16) || HW < 1 || HW > kTcMaxN || k < 1 || k > 64 || C < 1 || C > 512)
+  if (!(dtype == MOCE_BF16 || dtype == MOCE_F16) || HW < 1 || HW > 65536 || k < 1 || k > 64 || C < 1 || C > 512)
     return 0;
   const TcShape t = tc_shape(C, HW, k);
-  return t.fixed + 2 * t.qbytes <= (size_t)smem_optin_tc() ? 1 : 0;
+  const size_t smem_max = (size_t)smem_optin_tc();
+  return (t.fixed + 2 * t.qbytes <= smem_max && pool_stage_smem(C, HW) <= smem_max) ? 1 : 0;
 }
 
 }  // namespace moce
@@ -602,8 +710,10 @@ extern "C" int moce_tc_supported(int dtype, int64_t C, int64_t HW, int64_t k) {
 }
 
 extern "C" size_t moce_tc_stage_bytes(int64_t B, int64_t C, int64_t HW) {
-  const int64_t NA = ((HW + 15) / 16 * 16 + 63) / 64;
-  return (size_t)B * (size_t)((C + 63) / 64 * 64) * (size_t)(NA < 1 ? 1 : NA) * 128;
+  if (HW < 1) return 0;
+  int NP, NT, NA;
+  tc_tiling(HW, &NP, &NT, &NA);
+  return (size_t)B * (size_t)NT * (size_t)((C + 63) / 64 * 64) * (size_t)NA * 128;
 }
 
 extern "C" int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
@@ -616,10 +726,16 @@ extern "C" int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C, 
   MOCE_REQUIRE(B > 0 && C >= 1 && HW >= 1 && E_r >= 1 && k >= 1 && k <= C, MOCE_ERR_INVALID,
                "moce_mix_tc: invalid shape");
   MOCE_REQUIRE(tc_supported(dtype, C, HW, k), MOCE_ERR_UNSUPPORTED,
-               "moce_mix_tc: needs bf16/fp16, H*W <= 256, C <= 512, k <= 64 within shared memory");
+               "moce_mix_tc: needs bf16/fp16, C <= 512, k <= 64 within shared memory");
   MOCE_REQUIRE(((uintptr_t)xstage & 15) == 0, MOCE_ERR_INVALID, "moce_mix_tc: xstage must be 16-byte aligned");
   MOCE_REQUIRE(B < 65536 && (E_r + 1) * HW < (int64_t)1 << 31, MOCE_ERR_UNSUPPORTED, "moce_mix_tc: shape too large");
-  const TcShape sh = tc_shape(C, HW, k);
+  TcShape sh = tc_shape(C, HW, k);
+  if (sh.direct_ok && (((uintptr_t)y) & 15) != 0) {
+    // Y not 16-byte aligned: stage the rows in shared memory instead
+    sh.direct_ok = 0;
+    sh.stg_pitch = sh.NP;
+    sh.fixed += tc_stage_out_bytes(sh.NP, 2);
+  }
   const int Kp = sh.Kp, KMAX = sh.KMAX;
   const size_t qbytes = sh.qbytes, fixed = sh.fixed;
   const int smem_max = smem_optin_tc();
@@ -631,14 +747,19 @@ extern "C" int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C, 
   if (n_bsplit < 1) n_bsplit = 1;
   if (n_bsplit > B) n_bsplit = (int)B;
   TcArgs a{xstage, y, z, idx, ln, gate_w, gate_b, T_out, tmin_tau, trange_tau,
-           (int)B, (int)C, (int)HW, (int)E_r, (int)k, Kp, n_tiles, n_bsplit, ns, sh.NP, sh.NA, sh.P, sh.tmem_cols};
+           (int)B, (int)C, (int)HW, (int)E_r, (int)k, Kp, n_tiles, n_bsplit, ns, sh.NP, sh.NA, sh.P, sh.NT,
+           sh.tmem_cols, sh.direct_ok, sh.stg_pitch};
   return dispatch_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
     if constexpr (sizeof(T) != 2) {
       return set_error(MOCE_ERR_UNSUPPORTED, "moce_mix_tc: 16-bit inputs only");
     } else {
-      void (*kern)(TcArgs) = KMAX == 16 ? mix_tc_kernel<T, 16> : KMAX == 32 ? mix_tc_kernel<T, 32>
-                                                                            : mix_tc_kernel<T, 64>;
+      const bool gen = !(sh.NP == 64 && sh.NA == 1 && sh.P == 2 && sh.NT == 1);
+      void (*kern)(TcArgs) =
+          gen ? (KMAX == 16 ? mix_tc_kernel<T, 16, true> : KMAX == 32 ? mix_tc_kernel<T, 32, true>
+                                                                      : mix_tc_kernel<T, 64, true>)
+              : (KMAX == 16 ? mix_tc_kernel<T, 16, false> : KMAX == 32 ? mix_tc_kernel<T, 32, false>
+                                                                        : mix_tc_kernel<T, 64, false>);
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return set_error(MOCE_ERR_CUDA, "moce_mix_tc: cannot reserve %zu B shared memory", smem);
       kern<<<(unsigned)(n_tiles * n_bsplit), kTcThreads, smem, (cudaStream_t)stream>>>(a);

@@ -9,11 +9,13 @@
 // flight per SM.  The per-pixel residual sums of the quarters are added up
 // by cluster rank 0 through distributed shared memory.
 //
-// Operand layout (matches the B operand of mix_tc.cu): the pixels, padded to
-// NA = ceil(round16(H*W) / 64) atoms of 64, and per sample four K-quarters of
-// Kq = Kp / 4 channels, stored [quarter][atom][Kq rows][128 bytes]; in row c
-// of atom a the 16-byte unit j holds pixels 64 a + 8 (j ^ (c & 7)) .. +7
-// (zero beyond H*W); rows C .. Kp-1 are zero.
+// Operand layout (matches the B operand of mix_tc.cu): per sample NT pixel
+// tiles of NP pixels (a multiple of 16, at most 256; the last tile shorter),
+// each padded to NA = NP / 64 rounded up atoms of 64 pixels, and four
+// K-quarters of Kq = Kp / 4 channels, stored
+// [tile][quarter][atom][Kq rows][128 bytes]; in row c of atom a of tile t the
+// 16-byte unit j holds pixels t NP + 64 a + 8 (j ^ (c & 7)) .. +7 (zero
+// beyond the tile or H*W); rows C .. Kp-1 are zero.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -26,15 +28,15 @@ namespace {
 constexpr int kStageCtas = 4;
 constexpr int kStageThreads = 256;
 
-template <typename T>
+template <typename T, bool kTiled>
 __global__ void __cluster_dims__(kStageCtas, 1, 1) __launch_bounds__(kStageThreads)
     pool_stage_kernel(const T* __restrict__ x, int C, int HW, int cc, const int32_t* __restrict__ mask,
                       const int32_t* __restrict__ meta, float* __restrict__ z, T* __restrict__ y, int E,
-                      int4* __restrict__ xstage, int Kp, int NA) {
+                      int4* __restrict__ xstage, int Kp, int NP, int NT, int NA) {
   extern __shared__ __align__(16) unsigned char s_raw[];
   T* s_x = reinterpret_cast<T*>(s_raw);                                            // cc x HW
-  float* s_res = reinterpret_cast<float*>(s_raw + (((size_t)cc * HW * sizeof(T) + 15) & ~size_t(15)));  // 64
-  int* s_ulist = reinterpret_cast<int*>(s_res + 64);                               // cc
+  float* s_res = reinterpret_cast<float*>(s_raw + (((size_t)cc * HW * sizeof(T) + 15) & ~size_t(15)));  // HW
+  int* s_ulist = reinterpret_cast<int*>(s_res + ((HW + 3) & ~3));                 // cc
   __shared__ int s_nu;
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = blockIdx.x, b = blockIdx.y;
@@ -46,7 +48,7 @@ __global__ void __cluster_dims__(kStageCtas, 1, 1) __launch_bounds__(kStageThrea
   const T* src = x + ((size_t)b * C + c0) * HW;
   const size_t n = (size_t)cn * HW;
 
-  for (int p = tid; p < 64; p += kStageThreads) s_res[p] = 0.0f;
+  for (int p = tid; p < HW; p += kStageThreads) s_res[p] = 0.0f;
   if (cn > 0) {
     // contiguous rows c0 .. c1-1: 16-byte loads, eight in flight per thread
     if ((((uintptr_t)src) | (n * sizeof(T))) % 16 == 0) {
@@ -107,21 +109,33 @@ __global__ void __cluster_dims__(kStageCtas, 1, 1) __launch_bounds__(kStageThrea
   if (n_u > 0) asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   // operand layout; the CTA holding channel C-1 also writes the zero rows
   {
-    int4* xs = xstage + (size_t)b * Kp * NA * 8;
+    int4* xs = xstage + (size_t)b * NT * Kp * NA * 8;
     const int Kq = Kp / 4;
     const int row_end = (cn > 0 && c1 == C) ? Kp : c1;
-    const int units = (row_end - c0) * NA * 8;               // 16-byte units: channel, atom, chunk
+    const int units = (row_end - c0) * NT * NA * 8;          // 16-byte units: channel, tile, atom, chunk
     for (int q = tid; q < units; q += kStageThreads) {
-      const int j = q & 7, at = (q >> 3) % NA, c = c0 + (q >> 3) / NA;
-      const int pb = at * 64 + (j ^ (c & 7)) * 8;
+      const int j = q & 7;
+      int at = 0, tl = 0, c = c0 + (q >> 3);
+      if constexpr (kTiled) {                                 // (one tile of one atom: no division)
+        int rest = q >> 3;
+        at = rest % NA;
+        rest /= NA;
+        tl = rest % NT;
+        c = c0 + rest / NT;
+      }
+      const int pend = min(HW, (tl + 1) * NP);                // end of this tile's pixels
+      const int pb = tl * NP + at * 64 + (j ^ (c & 7)) * 8;
       union {
         int4 v;
         T e[8];
       } u;
 #pragma unroll
       for (int t = 0; t < 8; ++t)
-        u.e[t] = (c < C && pb + t < HW) ? s_x[(size_t)(c - c0) * HW + pb + t] : from_f<T>(0.0f);
-      xs[(((size_t)(c / Kq) * NA + at) * Kq + (c % Kq)) * 8 + j] = u.v;
+        u.e[t] = (c < C && pb + t < pend) ? s_x[(size_t)(c - c0) * HW + pb + t] : from_f<T>(0.0f);
+      if constexpr (!kTiled)
+        xs[(size_t)c * 8 + j] = u.v;                          // [quarter][rows] == [channel rows]
+      else
+        xs[((((size_t)tl * 4 + c / Kq) * NA + at) * Kq + (c % Kq)) * 8 + j] = u.v;
     }
   }
   if (n_u > 0) {
@@ -142,6 +156,16 @@ __global__ void __cluster_dims__(kStageCtas, 1, 1) __launch_bounds__(kStageThrea
 }
 
 }  // namespace
+
+// channels per CTA: a multiple of 8, so that every chunk starts on a 16-byte
+// boundary of the sample
+int pool_stage_cc(int64_t C) { return (int)(((C + kStageCtas - 1) / kStageCtas + 7) / 8 * 8); }
+
+size_t pool_stage_smem(int64_t C, int64_t HW) {
+  const int64_t cc = pool_stage_cc(C);
+  return (((size_t)cc * HW * 2 + 15) & ~size_t(15)) + (size_t)((HW + 3) & ~3) * 4 + (size_t)cc * 4;
+}
+
 }  // namespace moce
 
 using namespace moce;
@@ -155,27 +179,36 @@ extern "C" int moce_pool_stage(const void* x, int dtype, int64_t B, int64_t C, i
   MOCE_REQUIRE(!y || (mask && meta), MOCE_ERR_INVALID, "moce_pool_stage: the residual needs mask and meta");
   MOCE_REQUIRE(dtype == MOCE_BF16 || dtype == MOCE_F16, MOCE_ERR_UNSUPPORTED, "moce_pool_stage: 16-bit inputs only");
   MOCE_REQUIRE(B > 0 && C >= 1 && HW >= 1 && E_r >= 0, MOCE_ERR_INVALID, "moce_pool_stage: invalid shape");
-  MOCE_REQUIRE(HW <= 256, MOCE_ERR_UNSUPPORTED, "moce_pool_stage: H*W must be <= 256");
+  MOCE_REQUIRE(HW <= 65536, MOCE_ERR_UNSUPPORTED, "moce_pool_stage: H*W too large");
   MOCE_REQUIRE(B < 65536 && C <= 4096, MOCE_ERR_UNSUPPORTED, "moce_pool_stage: shape too large");
-  // channels per CTA: a multiple of 8, so that every chunk starts on a
-  // 16-byte boundary of the sample
-  const int cc = (int)(((C + kStageCtas - 1) / kStageCtas + 7) / 8 * 8);
-  const size_t smem = (((size_t)cc * HW * 2 + 15) & ~size_t(15)) + 64 * 4 + (size_t)cc * 4;
+  {
+    int dev = 0, smem_max = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    MOCE_REQUIRE(pool_stage_smem(C, HW) <= (size_t)smem_max, MOCE_ERR_UNSUPPORTED,
+                 "moce_pool_stage: a quarter of the sample exceeds shared memory");
+  }
+  const int cc = pool_stage_cc(C);
+  const size_t smem = pool_stage_smem(C, HW);
   const int Kp = (int)((C + 63) / 64 * 64);
-  const int NA = (int)(((HW + 15) / 16 * 16 + 63) / 64);
+  // pixel tiling of the tensor-core mix (mix_tc.cu, tc_tiling)
+  const int64_t nt0 = (HW + 255) / 256;
+  int64_t np = ((HW + nt0 - 1) / nt0 + 15) / 16 * 16;
+  if (np > 256) np = 256;
+  const int NP = (int)np, NT = (int)((HW + np - 1) / np), NA = (int)((np + 63) / 64);
   return dispatch_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
     if constexpr (sizeof(T) != 2) {
       return set_error(MOCE_ERR_UNSUPPORTED, "moce_pool_stage: 16-bit inputs only");
     } else {
+      auto kern = (NT * NA > 1) ? pool_stage_kernel<T, true> : pool_stage_kernel<T, false>;
       if (smem > 48 * 1024 &&
-          cudaFuncSetAttribute(pool_stage_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-              cudaSuccess)
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return set_error(MOCE_ERR_CUDA, "moce_pool_stage: cannot reserve %zu B shared memory", smem);
       const dim3 grid(kStageCtas, (unsigned)B);
-      pool_stage_kernel<T><<<grid, kStageThreads, smem, (cudaStream_t)stream>>>(
+      kern<<<grid, kStageThreads, smem, (cudaStream_t)stream>>>(
           static_cast<const T*>(x), (int)C, (int)HW, cc, mask, meta, z, static_cast<T*>(y), (int)(E_r + 1),
-          reinterpret_cast<int4*>(xstage), Kp, NA);
+          reinterpret_cast<int4*>(xstage), Kp, NP, NT, NA);
       return check_launch("pool_stage_kernel");
     }
   });

@@ -40,6 +40,10 @@ def relerr(a, b):
     (2, 256, 14, 14, 300, 16, torch.bfloat16),  # 14x14: N = 208 over four pixel atoms, one accumulator
     (2, 128, 10, 10, 140, 8, torch.float16),    # HW == 100: N = 112 over two atoms, two partial accumulators
     (2, 64, 16, 16, 40, 12, torch.bfloat16),    # HW == 256: N = 256, the largest tile
+    (2, 96, 12, 12, 4, 8, torch.bfloat16),      # HW == 144 with uncovered channels (residual sums over 144 pixels)
+    (2, 128, 28, 28, 90, 16, torch.bfloat16),   # 28x28: four pixel tiles of 208 / 160, weights reused per tile
+    (1, 64, 56, 56, 40, 8, torch.float16),      # 56x56: thirteen pixel tiles of 256 / 64
+    (2, 32, 20, 21, 3, 4, torch.bfloat16),      # HW == 420: two tiles of 224 / 196, uncovered channels
 ])
 def test_tc_mix_matches_oracle(B, C, H_, W_, E, k, dtype):
     gen = torch.Generator().manual_seed(B * 100 + C + k)
