@@ -140,6 +140,19 @@ int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C,
 int moce_tc_fault(int* flag, int clear);
 
 /*
+ * Both tensor-core passes in one call: moce_pool_stage, then moce_mix_tc
+ * launched as a programmatic dependent of it (the mix's prologue overlaps
+ * pass 1; its reads of z and xstage wait for pass 1 to complete).  Same
+ * buffers and conditions as the two calls.
+ */
+int moce_forward_tc(const void* x, int dtype, int64_t B, int64_t C, int64_t HW,
+                    const int32_t* mask, const int32_t* meta,
+                    const int32_t* idx, const float* ln, int64_t E_r,
+                    int64_t k, const float* gate_w, const float* gate_b,
+                    float tmin_tau, float trange_tau, float* z, void* xstage,
+                    void* y, float* T_out, void* stream);
+
+/*
  * CUDA-core pass 2 with lanes over pixels, any dtype, H*W <= 512, k <= 64,
  * for maps of a few hundred pixels (14x14, 28x28 stages; fp32 anywhere).
  * Same inputs and outputs as moce_mix_tc with X itself in place of the

@@ -38,6 +38,8 @@ SIGNATURES = {
     "moce_pool_stage": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _p, _p]),
     "moce_mix_tc": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p, _f32, _f32, _p, _p, _p]),
     "moce_tc_fault": (_i32, [_p, _i32]),
+    "moce_forward_tc": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _p, _p, _f32, _f32, _p, _p, _p,
+                                _p, _p]),
     "moce_px_supported": (_i32, [_i32, _i64, _i64, _i64]),
     "moce_mix_px": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p, _f32, _f32, _p, _p, _p]),
     "moce_gate_temperature": (_i32, [_p, _i32, _p, _i64, _i64, _i64, _p, _i64, _i64, _p, _p, _f32, _f32,

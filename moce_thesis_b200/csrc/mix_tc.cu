@@ -226,6 +226,10 @@ __device__ __forceinline__ uint32_t pack2_16(float lo, float hi) {
   return (uint32_t)bits16(from_f<T>(lo)) | ((uint32_t)bits16(from_f<T>(hi)) << 16);
 }
 
+// Programmatic dependent launch: wait until the prerequisite grid has
+// completed and its memory is visible (returns at once without one).
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void role_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
@@ -317,6 +321,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     }
     bars->abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    // staged X comes from pass 1, which may still run when this grid is a
+    // programmatic dependent of it (moce_forward_tc); a no-op otherwise
+    grid_dep_wait();
     for (int n = 0; n < n_pre; ++n) {
       mbar_expect_tx(&bars->full_b[n], qbytes);
       bulk_g2s(smem_u32(sB) + (uint32_t)n * qbytes, xs + (size_t)(n >> 2) * sbytes + (size_t)(n & 3) * qbytes,
@@ -352,6 +359,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       }
       if constexpr (kGwReg) gwr[jj] = (j < k) ? a.gate_w[j] : 0.0f;
     }
+    grid_dep_wait();                                          // z comes from pass 1 (see above)
 #pragma unroll
     for (int u = 0; u < ZPT; ++u) {
       const int c = tid + u * kWeightThreads;
@@ -716,10 +724,39 @@ extern "C" size_t moce_tc_stage_bytes(int64_t B, int64_t C, int64_t HW) {
   return (size_t)B * (size_t)NT * (size_t)((C + 63) / 64 * 64) * (size_t)NA * 128;
 }
 
+static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
+                         const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
+                         const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out, void* stream,
+                         bool dependent);
+
 extern "C" int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
                            const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
                            const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out,
                            void* stream) {
+  return mix_tc_launch(xstage, dtype, B, C, HW, z, idx, ln, E_r, k, gate_w, gate_b, tmin_tau, trange_tau, y, T_out,
+                       stream, false);
+}
+
+extern "C" int moce_pool_stage(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
+                               const int32_t* meta, float* z, void* y, int64_t E_r, void* xstage, void* stream);
+
+extern "C" int moce_forward_tc(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
+                               const int32_t* meta, const int32_t* idx, const float* ln, int64_t E_r, int64_t k,
+                               const float* gate_w, const float* gate_b, float tmin_tau, float trange_tau, float* z,
+                               void* xstage, void* y, float* T_out, void* stream) {
+  if (B == 0) return MOCE_OK;
+  int rc = moce_pool_stage(x, dtype, B, C, HW, mask, meta, z, y, E_r, xstage, stream);
+  if (rc) return rc;
+  // pass 2 as a programmatic dependent of pass 1: its prologue (A zeroing,
+  // tensor-memory allocation, route loads) overlaps pass 1's tail
+  return mix_tc_launch(xstage, dtype, B, C, HW, z, idx, ln, E_r, k, gate_w, gate_b, tmin_tau, trange_tau, y, T_out,
+                       stream, true);
+}
+
+static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
+                         const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
+                         const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out, void* stream,
+                         bool dependent) {
   if (B == 0) return MOCE_OK;
   MOCE_REQUIRE(xstage && z && idx && ln && gate_w && gate_b && y, MOCE_ERR_INVALID,
                "moce_mix_tc: null pointer argument");
@@ -762,7 +799,17 @@ extern "C" int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C, 
                                                                         : mix_tc_kernel<T, 64, false>);
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return set_error(MOCE_ERR_CUDA, "moce_mix_tc: cannot reserve %zu B shared memory", smem);
-      kern<<<(unsigned)(n_tiles * n_bsplit), kTcThreads, smem, (cudaStream_t)stream>>>(a);
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)(n_tiles * n_bsplit));
+      cfg.blockDim = dim3(kTcThreads);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = (cudaStream_t)stream;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = dependent ? 1 : 0;
+      if (cudaLaunchKernelEx(&cfg, kern, a) != cudaSuccess) return check_launch("mix_tc_kernel");
       return check_launch("mix_tc_kernel");
     }
   });

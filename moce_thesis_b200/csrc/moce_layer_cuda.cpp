@@ -441,12 +441,10 @@ std::vector<torch::Tensor> forward_tc(torch::Tensor x, torch::Tensor idx, torch:
   auto z = f32_opts_like(x, {d.B, d.C});
   auto T = want_T ? f32_opts_like(x, {d.B, d.E_r}) : f32_opts_like(x, {0});
   auto xstage = torch::empty({(int64_t)moce_tc_stage_bytes(d.B, d.C, d.HW)}, x.options().dtype(torch::kUInt8));
-  ok(moce_pool_stage(x.data_ptr(), dtype_of(x), d.B, d.C, d.HW, mask.data_ptr<int32_t>(), meta.data_ptr<int32_t>(),
-                     z.data_ptr<float>(), y.data_ptr(), d.E_r, xstage.data_ptr(), cur_stream()));
-  ok(moce_mix_tc(xstage.data_ptr(), dtype_of(x), d.B, d.C, d.HW, z.data_ptr<float>(), idx.data_ptr<int32_t>(),
-                 ln.data_ptr<float>(), d.E_r, d.K, gate_w.data_ptr<float>(), gate_b.data_ptr<float>(),
-                 (float)tmin_tau, (float)trange_tau, y.data_ptr(), want_T ? T.data_ptr<float>() : nullptr,
-                 cur_stream()));
+  ok(moce_forward_tc(x.data_ptr(), dtype_of(x), d.B, d.C, d.HW, mask.data_ptr<int32_t>(), meta.data_ptr<int32_t>(),
+                     idx.data_ptr<int32_t>(), ln.data_ptr<float>(), d.E_r, d.K, gate_w.data_ptr<float>(),
+                     gate_b.data_ptr<float>(), (float)tmin_tau, (float)trange_tau, z.data_ptr<float>(),
+                     xstage.data_ptr(), y.data_ptr(), want_T ? T.data_ptr<float>() : nullptr, cur_stream()));
   return {y, z, T};
 }
 

@@ -40,6 +40,9 @@ __global__ void __cluster_dims__(kStageCtas, 1, 1) __launch_bounds__(kStageThrea
   __shared__ int s_nu;
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = blockIdx.x, b = blockIdx.y;
+  // a programmatic dependent (the tensor-core mix) may start its prologue
+  // once every CTA of this grid is running; it waits for this grid's results
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c0 = rank * cc;
   const int c1 = min(C, c0 + cc);

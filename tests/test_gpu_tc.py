@@ -84,3 +84,26 @@ def test_tc_mix_stage4_workload_against_scheduled_path():
     assert close(a, b, 1e-2, 1e-3), relerr(a, b)
     ref = O.forward(x[:4].float().cpu().numpy(), L.numpy(), gw.numpy(), gb.numpy(), k, 0.1, 10.0, 1.0, mode="eval")
     assert close(a[:4], ref, 1e-2, 1e-3), relerr(a[:4], ref)
+
+
+def test_forward_tc_single_call_matches_two_calls():
+    """moce_forward_tc (pass 2 as a programmatic dependent of pass 1) gives
+    the same bits as moce_pool_stage followed by moce_mix_tc."""
+    from moce_thesis_b200 import capi
+    gen = torch.Generator().manual_seed(11)
+    B, C, Hh, E, k = 6, 256, 14, 300, 16
+    x = torch.randn(B, C, Hh, Hh, generator=gen).abs().to(DEV, torch.bfloat16)
+    L = torch.randn(E - 1, C, generator=gen).to(DEV)
+    gw = (torch.rand(1, k, generator=gen) - 0.5).to(DEV)
+    gb = torch.zeros(1, device=DEV)
+    r = H.route_build(L, k, transposed=False)
+    y2, z2, T2 = H.forward_tc(x, r, gw, gb, 0.1, 9.9)
+    y1 = torch.empty_like(y2)
+    z1 = torch.empty_like(z2)
+    T1 = torch.empty_like(T2)
+    xs = torch.empty(capi.lib().moce_tc_stage_bytes(B, C, Hh * Hh), dtype=torch.uint8, device=DEV)
+    capi.call("moce_forward_tc", capi.ptr(x), capi.dtype_code(x), B, C, Hh * Hh, capi.ptr(r["mask"]),
+              capi.ptr(r["meta"]), capi.ptr(r["idx"]), capi.ptr(r["ln"]), E - 1, k, capi.ptr(gw), capi.ptr(gb),
+              0.1, 9.9, capi.ptr(z1), capi.ptr(xs), capi.ptr(y1), capi.ptr(T1), capi.stream_handle())
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2) and torch.equal(z1, z2) and torch.equal(T1, T2)
