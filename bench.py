@@ -135,6 +135,74 @@ def make_inputs(dev, dtype, seed):
     return X.to(dev, dtype), L.to(dev), gw.to(dev), gb.to(dev), X
 
 
+
+def pass_fns(mc, r, xs, ys, zs, nsets, Bs, Cs, HW, Es, Ks, gwf, gbf, tmin_tau, trange_tau, dev):
+    """The two forward passes of one workload as separate C-ABI calls over
+    rotating input sets: (pass1(i), pass2(i), (name1, name2))."""
+    import torch
+    from moce_thesis_b200 import capi
+    x0 = xs[0]
+    dcode = capi.dtype_code(x0)
+    if mc.tc_supported(x0, Ks):
+        nst = capi.lib().moce_tc_stage_bytes(Bs, Cs, HW)
+        sts = [torch.empty(nst, dtype=torch.uint8, device=dev) for _ in range(nsets)]
+
+        def pass1(i):
+            capi.call("moce_pool_stage", xs[i % nsets].data_ptr(), dcode, Bs, Cs, HW, r.mask.data_ptr(),
+                      r.meta.data_ptr(), zs[i % nsets].data_ptr(), ys[i % nsets].data_ptr(), Es - 1,
+                      sts[i % nsets].data_ptr(), capi.stream_handle())
+
+        def pass2(i):
+            capi.call("moce_mix_tc", sts[i % nsets].data_ptr(), dcode, Bs, Cs, HW, zs[i % nsets].data_ptr(),
+                      r.idx.data_ptr(), r.ln.data_ptr(), Es - 1, Ks, gwf.data_ptr(), gbf.data_ptr(), tmin_tau,
+                      trange_tau, ys[i % nsets].data_ptr(), None, capi.stream_handle())
+        return pass1, pass2, ("pass1_pool_stage", "pass2_mix_tc")
+
+    def pool(i):
+        capi.call("moce_pool_residual", xs[i % nsets].data_ptr(), dcode, Bs, Cs, HW, r.mask.data_ptr(),
+                  r.meta.data_ptr(), zs[i % nsets].data_ptr(), ys[i % nsets].data_ptr(), Es - 1, capi.stream_handle())
+
+    if mc.px_supported(x0, Ks):
+        def pass2(i):
+            capi.call("moce_mix_px", xs[i % nsets].data_ptr(), dcode, Bs, Cs, HW, zs[i % nsets].data_ptr(),
+                      r.idx.data_ptr(), r.ln.data_ptr(), Es - 1, Ks, gwf.data_ptr(), gbf.data_ptr(), tmin_tau,
+                      trange_tau, ys[i % nsets].data_ptr(), None, capi.stream_handle())
+        return pool, pass2, ("pass1_pool_residual", "pass2_mix_px")
+    ge, sc = r.schedule()
+
+    def pass2(i):
+        capi.call("moce_mix_scheduled", xs[i % nsets].data_ptr(), dcode, Bs, Cs, HW, zs[i % nsets].data_ptr(),
+                  r.ln.data_ptr(), Es - 1, Ks, ge.data_ptr(), sc.data_ptr(), gwf.data_ptr(),
+                  gbf.data_ptr(), tmin_tau, trange_tau, ys[i % nsets].data_ptr(), None, capi.stream_handle())
+    return pool, pass2, ("pass1_pool_residual", "pass2_mix_scheduled")
+
+
+def graph_time(fn, reps):
+    """ms per call of fn: `reps` calls captured in a CUDA graph and replayed
+    between two events, so host launch cost does not leak into short passes."""
+    import torch
+    st = torch.cuda.current_stream()
+    side = torch.cuda.Stream()
+    side.wait_stream(st)
+    with torch.cuda.stream(side):
+        for i in range(3):
+            fn(i)
+    st.wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(reps):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    g.replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) / reps
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -204,90 +272,33 @@ def run_ours(args):
     ms_step = ms / args.steps
     value = world * bytes_step * args.steps / (ms * 1e-3) / 1e9
 
-    # each pass timed alone through the C ABI: `reps` launches captured in a
-    # CUDA graph and replayed between two events, so that host launch cost
-    # (ctypes) does not leak into the short first pass
-    from moce_thesis_b200 import capi
-    dcode = capi.dtype_code(x0)
+    # each pass timed alone through the C ABI (CUDA-graph replay)
     zs = [torch.empty(B, C, device=dev) for _ in range(nsets)]
+    pass1, pass2, names = pass_fns(mc, r, xs, ys, zs, nsets, B, C, H * W, E, K, gwf, gbf, tmin_tau, trange_tau, dev)
     reps = max(args.steps, 20)
-
-    if use_tc:
-        nst = capi.lib().moce_tc_stage_bytes(B, C, H * W)
-        sts = [torch.empty(nst, dtype=torch.uint8, device=dev) for _ in range(nsets)]
-
-        def pass1(i):
-            capi.call("moce_pool_stage", xs[i % nsets].data_ptr(), dcode, B, C, H * W, r.mask.data_ptr(),
-                      r.meta.data_ptr(), zs[i % nsets].data_ptr(), ys[i % nsets].data_ptr(), E - 1,
-                      sts[i % nsets].data_ptr(), capi.stream_handle())
-
-        def pass2(i):
-            capi.call("moce_mix_tc", sts[i % nsets].data_ptr(), dcode, B, C, H * W, zs[i % nsets].data_ptr(),
-                      r.idx.data_ptr(), r.ln.data_ptr(), E - 1, K, gwf.data_ptr(), gbf.data_ptr(), tmin_tau,
-                      trange_tau, ys[i % nsets].data_ptr(), None, capi.stream_handle())
-    elif use_px:
-        def pass1(i):
-            capi.call("moce_pool_residual", xs[i % nsets].data_ptr(), dcode, B, C, H * W, r.mask.data_ptr(),
-                      r.meta.data_ptr(), zs[i % nsets].data_ptr(), ys[i % nsets].data_ptr(), E - 1, capi.stream_handle())
-
-        def pass2(i):
-            capi.call("moce_mix_px", xs[i % nsets].data_ptr(), dcode, B, C, H * W, zs[i % nsets].data_ptr(),
-                      r.idx.data_ptr(), r.ln.data_ptr(), E - 1, K, gwf.data_ptr(), gbf.data_ptr(), tmin_tau,
-                      trange_tau, ys[i % nsets].data_ptr(), None, capi.stream_handle())
-    else:
-        ge, sc = r.schedule()
-
-        def pass1(i):
-            capi.call("moce_pool_residual", xs[i % nsets].data_ptr(), dcode, B, C, H * W, r.mask.data_ptr(),
-                      r.meta.data_ptr(), zs[i % nsets].data_ptr(), ys[i % nsets].data_ptr(), E - 1, capi.stream_handle())
-
-        def pass2(i):
-            capi.call("moce_mix_scheduled", xs[i % nsets].data_ptr(), dcode, B, C, H * W, zs[i % nsets].data_ptr(),
-                      r.ln.data_ptr(), E - 1, K, ge.data_ptr(), sc.data_ptr(), gwf.data_ptr(),
-                      gbf.data_ptr(), tmin_tau, trange_tau, ys[i % nsets].data_ptr(), None, capi.stream_handle())
-
-    def time_loop(fn):
-        side = torch.cuda.Stream()
-        side.wait_stream(st)
-        with torch.cuda.stream(side):
-            for i in range(3):
-                fn(i)
-        st.wait_stream(side)
-        torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            for i in range(reps):
-                fn(i)
-        g.replay()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(st)
-        g.replay()
-        e1.record(st)
-        torch.cuda.synchronize()
-        del g
-        return e0.elapsed_time(e1) / reps
-
-    gate_ms = time_loop(pass1)
-    mix_ms = time_loop(pass2)
+    gate_ms = graph_time(pass1, reps)
+    mix_ms = graph_time(pass2, reps)
+    from moce_thesis_b200 import capi
     # algorithmic bytes of pass 2: its X operand in, routed Y out, z in,
     # supports (int32) and normalised logits (fp32)
     x_in = capi.lib().moce_tc_stage_bytes(B, C, H * W) if use_tc else xb
     mix_bytes = x_in + B * (E - 1) * H * W * esize + B * C * 4 + (E - 1) * K * 8
 
     # end to end through the public API: pinned host X -> layer -> host Y
+    # (MoCE.forward_host: host-to-device copies, both passes and
+    # device-to-host copies of runs of samples overlap on three streams)
     xh = x0.cpu().pin_memory()
     yh = torch.empty(B, E, H, W, dtype=dtype).pin_memory()
     with torch.no_grad():
         for _ in range(2):
-            yh.copy_(layer(xh.to(dev, non_blocking=True)), non_blocking=True)
+            layer.forward_host(xh, out=yh)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
         for _ in range(args.steps):
-            yh.copy_(layer(xh.to(dev, non_blocking=True)), non_blocking=True)
+            layer.forward_host(xh, out=yh)
         e1.record(st)
         torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
@@ -320,16 +331,14 @@ def run_ours(args):
         "config": {"workload": WORKLOAD, "global_batch": B * world, "C": C, "HW": H * W, "E": E, "k": K,
                    "parallelism": f"batch-sharded x{world}, no data-path collective",
                    "l2": f"{nsets} rotating X/Y sets ({nsets * (xb + yb) / 2**20:.0f} MiB > 126 MiB L2)"},
-        "kernels_ms": {("pass1_pool_stage" if use_tc else "pass1_pool_residual"): round(gate_ms, 5),
-                       ("pass2_mix_tc" if use_tc else "pass2_mix_px" if use_px else "pass2_mix_scheduled"):
-                           round(mix_ms, 5)},
+        "kernels_ms": {names[0]: round(gate_ms, 5), names[1]: round(mix_ms, 5)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "kernel": "mix_tc_kernel (pass 2, tcgen05)" if use_tc else
                          "mix_px kernel (pass 2, CUDA cores, lanes over pixels)" if use_px else "mix_sched_kernel (pass 2)",
                      "peak_kind": f"{peak_kind} copy bandwidth"},
         "e2e": {"value": round(e2e, 3), "unit": "GB/s", "h2d_bytes_per_step": xb, "d2h_bytes_per_step": yb,
-                "api": "moce_thesis_b200.MoCE.forward_eval, pinned host X in, host Y out"},
+                "api": "moce_thesis_b200.MoCE.forward_host, pinned host X in, host Y out"},
         "gpu_launches": 2 * args.steps,
         "clocks": clk.summary(),
     }
@@ -531,6 +540,11 @@ def run_sweep(args):
             torch.cuda.synchronize()
         ms = _max_over_ranks(e0.elapsed_time(e1), world, dev) / args.steps
         nbytes = xb + yb + (Es - 1) * Ks * 8 + Cs * 4
+        zs = [torch.empty(Bs, Cs, device=dev) for _ in range(nsets)]
+        p1, p2, names = pass_fns(mc, r, xs, ys, zs, nsets, Bs, Cs, Hs * Hs, Es, Ks, gwf, gbf,
+                                 layer.cached_temp_min_tau, layer.cached_temp_range_tau, dev)
+        reps = max(args.steps, 20)
+        kms = {names[0]: round(graph_time(p1, reps), 5), names[1]: round(graph_time(p2, reps), 5)}
         path = "tensor-core" if mc.tc_supported(x0, Ks) else "lanes-over-pixels" if mc.px_supported(x0, Ks) else (
             "scheduled" if r.schedule() is not None else "general")
         out = {"metric": "MoCE fwd HBM GB/s (% of 8 TB/s)", "value": round(world * nbytes / (ms * 1e-3) / 1e9, 2),
@@ -539,10 +553,10 @@ def run_sweep(args):
                "higher_is_better": True, "scaling": "weak", "dtype": "bf16", "data": "synthetic",
                "config": {"workload": f"ResNet-50 expand projection C={Cs} {Hs}x{Hs} E={Es} k={Ks}, N={Bs}/GPU",
                           "path": path, "l2": f"{nsets} rotating X/Y sets"},
-               "clocks": clk.summary()}
+               "kernels_ms": kms, "clocks": clk.summary()}
         if rank == 0:
             print(json.dumps(out), flush=True)
-        del xs, ys, layer, x0
+        del xs, ys, zs, layer, x0
         torch.cuda.empty_cache()
     if world > 1:
         dist.barrier()

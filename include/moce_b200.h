@@ -28,6 +28,14 @@
 extern "C" {
 #endif
 
+/* The library is built with hidden symbol visibility: only the entry points
+ * declared here are exported, so a process that loads two builds of it (or
+ * another library with the same internal names) cannot bind one build's
+ * internal calls to the other's. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
 typedef enum {
   MOCE_OK = 0,
   MOCE_ERR_INVALID = 1,      /* bad pointer, shape or dtype */
@@ -284,6 +292,10 @@ int moce_backward(const void* x, const void* dy, int dtype, int64_t B,
                   float trange_tau, const float* z, const float* T, void* dx,
                   float* dL, float* dgate_w, float* dgate_b, void* workspace,
                   size_t workspace_bytes, void* stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
 
 #ifdef __cplusplus
 }

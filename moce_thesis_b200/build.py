@@ -29,7 +29,7 @@ BINDING = os.path.join(BINDING_DIR, "moce_cuda" + EXT_SUFFIX)
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
+NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
                      "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]
 
 CU_SOURCES = ["status.cu", "route.cu", "schedule.cu", "forward.cu", "mix.cu", "stage.cu", "mix_tc.cu", "simt.cu", "backward.cu", "noalloc.cu"]

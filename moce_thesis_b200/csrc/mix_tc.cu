@@ -125,8 +125,20 @@ struct TcArgs {
   int NP, NA, P;                  // MMA N (pixel tile, a multiple of 16), 64-pixel atoms, partial accumulators
   int NT;                         // pixel tiles per sample (NP pixels each, the last one shorter)
   uint32_t tmem_cols;             // tensor-memory columns allocated (power of 2)
-  int direct;                     // tiled rows go from registers to Y (no shared staging block)
-  int stg_pitch;                  // output staging row pitch (elements), 0 when direct
+  int drain;                      // output path, one of the TcDrain values
+  int stg_pitch;                  // staging row pitch: elements (kDrainOneTile, kDrainRowsLegacy), bytes (kDrainRows)
+  int nsb;                        // staging buffers (kDrainRows)
+  uint32_t stage_bytes;           // shared memory of the output staging area
+};
+
+// How the drain moves a finished accumulator to Y.
+enum TcDrain {
+  kDrainOneTile = 0,              // one pixel tile: the tile's rows are one contiguous range of Y, staged in
+                                  // shared memory and written by one bulk copy
+  kDrainRows = 1,                 // pixel tiles of 16-byte aligned rows: 16-byte stores into rows padded by
+                                  // 16 bytes (conflict-free), one bulk copy per row, `nsb` buffers
+  kDrainDirect = 2,               // 16-byte stores from registers straight to Y (when staging does not fit)
+  kDrainRowsLegacy = 3,           // other pixel tiles: 16-bit stores into rows of NP elements
 };
 
 constexpr int kMaxSlots = 8;
@@ -184,6 +196,10 @@ __device__ __forceinline__ void bulk_s2g(void* dst, uint32_t src, uint32_t bytes
 }
 
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// every bulk group of this thread but the most recent one has read its source
+__device__ __forceinline__ void bulk_wait_read_all_but1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Named barrier over the 128 threads of one role that also ANDs a flag, so
@@ -253,10 +269,6 @@ constexpr int kWeightThreads = 256, kDrainThreads = 128;
 constexpr int kBarWeights = 1, kBarDrain = 2;
 constexpr int kWarpIssuer0 = 12, kWarpProducer = 14;
 
-__host__ __device__ constexpr size_t tc_stage_out_bytes(int HW, int esize) {
-  return ((size_t)128 * HW * esize + 15) & ~size_t(15);
-}
-
 // Roles (warp-specialized, one CTA per SM):
 //   warps 0-7   weight rows: threads 2r and 2r+1 share expert row e0 + r,
 //               each with half of its supports (a pair of adjacent lanes
@@ -286,8 +298,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   const uint32_t qbytes = sbytes / 4;                         // a quarter of the channels, all atoms
   unsigned char* sA = base;                                   // 128 x Kp : Kp * 256 B
   unsigned char* sB = sA + (size_t)Kp * 256;                  // NS quarter slots
-  T* stg = reinterpret_cast<T*>(sB + (size_t)NS * qbytes);    // 128 x (tile pixels) output block
-  float* s_z = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(stg) + tc_stage_out_bytes(a.stg_pitch, sizeof(T)));
+  T* stg = reinterpret_cast<T*>(sB + (size_t)NS * qbytes);    // output staging area
+  float* s_z = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(stg) + a.stage_bytes);
   float* s_gw = s_z + 2 * Kp;
   TcBars* bars = reinterpret_cast<TcBars*>(s_gw + KMAX);
   volatile int* abort = &bars->abort;
@@ -542,87 +554,43 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     const bool has_row = dt < rows;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     T* yg = static_cast<T*>(a.y);
-    // pixel-tiled samples with 16-byte aligned rows: the rows go straight from
-    // registers to Y with 16-byte stores (a shared staging block of rows
-    // 2 * NP bytes apart would put a warp's rows in a few banks)
-    const bool direct = kGen && a.direct != 0;
-    for (int u = 0; u < nu && direct; ++u) {
-      const int s = u & 1, i = u / NT, t = u - (u / NT) * NT;
-      const int p0 = t * NP, tp = min(NP, HW - p0);
-      bool ok = true;
-      if (dt == 0) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
-      if (!role_sync_and(kBarDrain, kDrainThreads, ok)) break;
-      tc_fence_after();
-      const uint32_t tb = tmem + lane_base + (uint32_t)(s * P * NP);
-      T* dst = yg + ((size_t)(b0 + i) * E + e0 + dt) * HW + p0;
-      for (int cb = 0; cb < tp; cb += 32) {                   // uniform across the warp
-        uint32_t r0[32], r1[32];
-        tmem_ld32_nowait(tb + cb, r0);
-        if (P == 2) tmem_ld32_nowait(tb + NP + cb, r1);
-        tmem_wait_ld();
-        if (cb + 32 >= tp) {                                  // last read of the buffer
-          tc_fence_before();
-          mbar_arrive(&bars->d_empty[s]);
-        }
-        if (has_row) {
-          float v[32];
+    const int drain = kGen ? a.drain : (int)kDrainOneTile;
+    if (drain == kDrainOneTile) {
+      // One pixel tile per sample: the tile's rows are one contiguous range of
+      // Y, staged in shared memory at a pitch of H*W elements with 16-bit
+      // stores and written by one bulk copy.  (16-byte, 8-byte or paired
+      // 4-byte staging stores, by the rows' alignment, measured slower here:
+      // 90.4 against 82.7 us at 7x7, 86 against 69 us at 14x14.)
+      for (int u = 0; u < nu; ++u) {
+        const int s = u & 1;
+        bool ok = true;
+        if (dt == 0) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
+        if (dt == 0) bulk_wait_read();                        // the previous sample's copy left the block
+        if (!role_sync_and(kBarDrain, kDrainThreads, ok)) break;
+        tc_fence_after();
+        const uint32_t tb = tmem + lane_base + (uint32_t)(s * P * NP);
 #pragma unroll
-          for (int p = 0; p < 32; ++p)
-            v[p] = (P == 2) ? __uint_as_float(r0[p]) + __uint_as_float(r1[p]) : __uint_as_float(r0[p]);
-          if (cb + 32 <= tp) {
-#pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              int4 w;
-              w.x = (int)pack2_16<T>(v[8 * g + 0], v[8 * g + 1]);
-              w.y = (int)pack2_16<T>(v[8 * g + 2], v[8 * g + 3]);
-              w.z = (int)pack2_16<T>(v[8 * g + 4], v[8 * g + 5]);
-              w.w = (int)pack2_16<T>(v[8 * g + 6], v[8 * g + 7]);
-              *reinterpret_cast<int4*>(dst + cb + 8 * g) = w;
-            }
-          } else {
+        for (int cb = 0; cb < (kGen ? kTcMaxN : 64); cb += 32) {
+          if (cb >= HW) break;                                // uniform across the warp
+          uint32_t r0[32], r1[32];
+          tmem_ld32_nowait(tb + cb, r0);
+          if (P == 2) tmem_ld32_nowait(tb + NP + cb, r1);
+          tmem_wait_ld();
+          if (has_row) {
+            float v[32];
 #pragma unroll
             for (int p = 0; p < 32; ++p)
-              if (cb + p < tp) dst[cb + p] = from_f<T>(v[p]);
+              v[p] = (P == 2) ? __uint_as_float(r0[p]) + __uint_as_float(r1[p]) : __uint_as_float(r0[p]);
+#pragma unroll
+            for (int p = 0; p < 32; ++p)
+              if (cb + p < HW) stg[dt * HW + cb + p] = from_f<T>(v[p]);
           }
         }
-      }
-    }
-    for (int u = 0; u < nu && !direct; ++u) {
-      const int s = u & 1, i = u / NT, t = u - (u / NT) * NT;
-      const int p0 = t * NP, tp = min(NP, HW - p0);           // this tile's pixels
-      bool ok = true;
-      if (dt == 0) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
-      // this thread's copies left the staging area (one tile: only thread 0 copies)
-      if (NT > 1 || dt == 0) bulk_wait_read();
-      if (!role_sync_and(kBarDrain, kDrainThreads, ok)) break;
-      tc_fence_after();
-      const uint32_t tb = tmem + lane_base + (uint32_t)(s * P * NP);
-#pragma unroll
-      for (int cb = 0; cb < (kGen ? kTcMaxN : 64); cb += 32) {
-        if (cb >= tp) break;                                  // uniform across the warp
-        uint32_t r0[32], r1[32];
-        tmem_ld32_nowait(tb + cb, r0);
-        if (P == 2) tmem_ld32_nowait(tb + NP + cb, r1);
-        tmem_wait_ld();
-        if (has_row) {
-          if (P == 2) {
-#pragma unroll
-            for (int p = 0; p < 32; ++p)
-              if (cb + p < tp) stg[dt * tp + cb + p] = from_f<T>(__uint_as_float(r0[p]) + __uint_as_float(r1[p]));
-          } else {
-#pragma unroll
-            for (int p = 0; p < 32; ++p)
-              if (cb + p < tp) stg[dt * tp + cb + p] = from_f<T>(__uint_as_float(r0[p]));
-          }
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&bars->d_empty[s]);
-      proxy_fence_smem();
-      role_sync(kBarDrain, kDrainThreads);
-      if (NT == 1) {
-        // the tile's rows are one contiguous range of Y: one copy
-        T* dst = yg + ((size_t)(b0 + i) * E + e0) * HW;
+        tc_fence_before();
+        mbar_arrive(&bars->d_empty[s]);
+        proxy_fence_smem();
+        role_sync(kBarDrain, kDrainThreads);
+        T* dst = yg + ((size_t)(b0 + u) * E + e0) * HW;
         const uint32_t nbytes = (uint32_t)(rows * HW * sizeof(T));
         if (((((uintptr_t)dst) | nbytes) & 15) == 0) {
           if (dt == 0) bulk_s2g(dst, smem_u32(stg), nbytes);
@@ -630,15 +598,134 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
           for (int q = dt; q < rows * HW; q += kDrainThreads) dst[q] = stg[q];
           role_sync(kBarDrain, kDrainThreads);
         }
-      } else if (has_row) {
-        // one row segment of Y per thread
+      }
+    } else if (drain == kDrainRows) {
+      // Pixel tiles of 16-byte aligned rows: each thread stages its row with
+      // 16-byte stores into rows 2 NP + 16 bytes apart (the 16-byte skew puts
+      // the 32 rows of a warp's store in distinct bank quads), then copies it
+      // out with one bulk copy; `nsb` buffers alternate.
+      const uint32_t pitch = (uint32_t)a.stg_pitch;
+      unsigned char* row0 = reinterpret_cast<unsigned char*>(stg) + (size_t)dt * pitch;
+      for (int u = 0; u < nu; ++u) {
+        const int s = u & 1, i = u / NT, t = u - (u / NT) * NT;
+        const int p0 = t * NP, tp = min(NP, HW - p0);       // a multiple of 8
+        unsigned char* row = row0 + (size_t)(u % a.nsb) * 128u * pitch;
+        bool ok = true;
+        if (dt == 0) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
+        // this thread's copy out of this buffer, nsb units ago, has read it
+        if (a.nsb == 2) bulk_wait_read_all_but1();
+        else bulk_wait_read();
+        if (!role_sync_and(kBarDrain, kDrainThreads, ok)) break;
+        tc_fence_after();
+        const uint32_t tb = tmem + lane_base + (uint32_t)(s * P * NP);
+        for (int cb = 0; cb < tp; cb += 32) {                 // uniform across the warp
+          uint32_t r0[32], r1[32];
+          tmem_ld32_nowait(tb + cb, r0);
+          if (P == 2) tmem_ld32_nowait(tb + NP + cb, r1);
+          tmem_wait_ld();
+          if (cb + 32 >= tp) {                                // last read of the buffer
+            tc_fence_before();
+            mbar_arrive(&bars->d_empty[s]);
+          }
+          if (has_row) {
+            float v[32];
+#pragma unroll
+            for (int p = 0; p < 32; ++p)
+              v[p] = (P == 2) ? __uint_as_float(r0[p]) + __uint_as_float(r1[p]) : __uint_as_float(r0[p]);
+#pragma unroll
+            for (int g = 0; g < 4; ++g)
+              if (cb + 8 * g < tp)
+                *reinterpret_cast<uint4*>(row + (size_t)(cb + 8 * g) * 2) =
+                    make_uint4(pack2_16<T>(v[8 * g], v[8 * g + 1]), pack2_16<T>(v[8 * g + 2], v[8 * g + 3]),
+                               pack2_16<T>(v[8 * g + 4], v[8 * g + 5]), pack2_16<T>(v[8 * g + 6], v[8 * g + 7]));
+          }
+        }
+        if (has_row) {
+          proxy_fence_smem();
+          bulk_s2g(yg + ((size_t)(b0 + i) * E + e0 + dt) * HW + p0, smem_u32(row), (uint32_t)tp * (uint32_t)sizeof(T));
+        }
+      }
+    } else if (drain == kDrainDirect) {
+      // pixel tiles of 16-byte aligned rows when no staging buffer fits:
+      // 16-byte stores from registers straight to Y
+      for (int u = 0; u < nu; ++u) {
+        const int s = u & 1, i = u / NT, t = u - (u / NT) * NT;
+        const int p0 = t * NP, tp = min(NP, HW - p0);
+        bool ok = true;
+        if (dt == 0) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
+        if (!role_sync_and(kBarDrain, kDrainThreads, ok)) break;
+        tc_fence_after();
+        const uint32_t tb = tmem + lane_base + (uint32_t)(s * P * NP);
         T* dst = yg + ((size_t)(b0 + i) * E + e0 + dt) * HW + p0;
-        const uint32_t nbytes = (uint32_t)(tp * sizeof(T));
-        const uint32_t src = smem_u32(stg) + (uint32_t)(dt * tp) * (uint32_t)sizeof(T);
-        if (((((uintptr_t)dst) | nbytes | src) & 15) == 0) {
-          bulk_s2g(dst, src, nbytes);
-        } else {
-          for (int p = 0; p < tp; ++p) dst[p] = stg[dt * tp + p];
+        for (int cb = 0; cb < tp; cb += 32) {                 // uniform across the warp
+          uint32_t r0[32], r1[32];
+          tmem_ld32_nowait(tb + cb, r0);
+          if (P == 2) tmem_ld32_nowait(tb + NP + cb, r1);
+          tmem_wait_ld();
+          if (cb + 32 >= tp) {                                // last read of the buffer
+            tc_fence_before();
+            mbar_arrive(&bars->d_empty[s]);
+          }
+          if (has_row) {
+            float v[32];
+#pragma unroll
+            for (int p = 0; p < 32; ++p)
+              v[p] = (P == 2) ? __uint_as_float(r0[p]) + __uint_as_float(r1[p]) : __uint_as_float(r0[p]);
+            if (cb + 32 <= tp) {
+#pragma unroll
+              for (int g = 0; g < 4; ++g) {
+                int4 w;
+                w.x = (int)pack2_16<T>(v[8 * g + 0], v[8 * g + 1]);
+                w.y = (int)pack2_16<T>(v[8 * g + 2], v[8 * g + 3]);
+                w.z = (int)pack2_16<T>(v[8 * g + 4], v[8 * g + 5]);
+                w.w = (int)pack2_16<T>(v[8 * g + 6], v[8 * g + 7]);
+                *reinterpret_cast<int4*>(dst + cb + 8 * g) = w;
+              }
+            } else {
+#pragma unroll
+              for (int p = 0; p < 32; ++p)
+                if (cb + p < tp) dst[cb + p] = from_f<T>(v[p]);
+            }
+          }
+        }
+      }
+    } else {
+      // other pixel tiles: 16-bit stores into rows of the tile's width, one
+      // bulk copy (or element copy) per row
+      for (int u = 0; u < nu; ++u) {
+        const int s = u & 1, i = u / NT, t = u - (u / NT) * NT;
+        const int p0 = t * NP, tp = min(NP, HW - p0);         // this tile's pixels
+        bool ok = true;
+        if (dt == 0) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
+        bulk_wait_read();                                     // this thread's copy left the staging area
+        if (!role_sync_and(kBarDrain, kDrainThreads, ok)) break;
+        tc_fence_after();
+        const uint32_t tb = tmem + lane_base + (uint32_t)(s * P * NP);
+        for (int cb = 0; cb < tp; cb += 32) {                 // uniform across the warp
+          uint32_t r0[32], r1[32];
+          tmem_ld32_nowait(tb + cb, r0);
+          if (P == 2) tmem_ld32_nowait(tb + NP + cb, r1);
+          tmem_wait_ld();
+          if (has_row) {
+#pragma unroll
+            for (int p = 0; p < 32; ++p) {
+              const float v = (P == 2) ? __uint_as_float(r0[p]) + __uint_as_float(r1[p]) : __uint_as_float(r0[p]);
+              if (cb + p < tp) stg[dt * tp + cb + p] = from_f<T>(v);
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&bars->d_empty[s]);
+        if (has_row) {
+          T* dst = yg + ((size_t)(b0 + i) * E + e0 + dt) * HW + p0;
+          const uint32_t nbytes = (uint32_t)(tp * sizeof(T));
+          const uint32_t src = smem_u32(stg) + (uint32_t)(dt * tp) * (uint32_t)sizeof(T);
+          if (((((uintptr_t)dst) | nbytes | src) & 15) == 0) {
+            proxy_fence_smem();
+            bulk_s2g(dst, src, nbytes);
+          } else {
+            for (int p = 0; p < tp; ++p) dst[p] = stg[dt * tp + p];
+          }
         }
       }
     }
@@ -654,9 +741,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
 
 struct TcShape {
   int Kp, NP, NT, NA, P, KMAX;
-  int direct_ok, stg_pitch;       // direct row stores possible (given an aligned Y); staging pitch otherwise
+  int drain, stg_pitch, nsb;      // output path (TcDrain), staging pitch, staging buffers
+  uint32_t stage_bytes;           // shared memory of the output staging area
   uint32_t tmem_cols;
   size_t fixed, qbytes;           // shared memory without the X ring, bytes per ring slot
+  int ns;                         // X quarter slots in the ring
 };
 
 // pixel tiling: NT tiles of NP pixels (a multiple of 16, at most 256), the
@@ -670,7 +759,12 @@ void tc_tiling(int64_t HW, int* NP, int* NT, int* NA) {
   *NA = (int)((np + 63) / 64);
 }
 
-TcShape tc_shape(int64_t C, int64_t HW, int64_t k) {
+int smem_optin_tc();
+
+// The kernel's shape for (C, H*W, k) and a Y that is (or is not) 16-byte
+// aligned: tiling, accumulators, output path and shared-memory plan.
+// ns == 0 when the shape does not fit shared memory.
+TcShape tc_shape(int64_t C, int64_t HW, int64_t k, bool y_aligned = true) {
   TcShape t;
   t.Kp = (int)((C + 63) / 64 * 64);
   tc_tiling(HW, &t.NP, &t.NT, &t.NA);
@@ -683,12 +777,34 @@ TcShape tc_shape(int64_t C, int64_t HW, int64_t k) {
   t.tmem_cols = cols;
   t.KMAX = k <= 16 ? 16 : k <= 32 ? 32 : 64;
   t.qbytes = (size_t)t.Kp * t.NA * 32;
-  // one tile: the block is the tile's rows, H*W apart; several tiles: rows
-  // of NP pixels, unless they go to Y directly (16-byte aligned rows)
-  t.direct_ok = t.NT > 1 && (HW % 8) == 0;
-  t.stg_pitch = t.NT == 1 ? (int)HW : (t.direct_ok ? 0 : t.NP);
-  t.fixed = 1024 + (size_t)t.Kp * 256 + tc_stage_out_bytes(t.stg_pitch, 2) + (size_t)t.Kp * 8 +
-            (size_t)t.KMAX * 4 + sizeof(TcBars);
+  const size_t base = 1024 + (size_t)t.Kp * 256 + (size_t)t.Kp * 8 + (size_t)t.KMAX * 4 + sizeof(TcBars);
+  const size_t smem_max = (size_t)smem_optin_tc();
+  auto slots = [&](size_t stage) -> int {
+    const size_t f = base + stage;
+    return f < smem_max ? (int)std::min<size_t>((size_t)kMaxSlots, (smem_max - f) / t.qbytes) : 0;
+  };
+  auto pick = [&](int drain, int pitch, int nsb, size_t stage) {
+    t.drain = drain;
+    t.stg_pitch = pitch;
+    t.nsb = nsb;
+    t.stage_bytes = (uint32_t)((stage + 15) & ~size_t(15));
+    t.fixed = base + t.stage_bytes;
+    t.ns = slots(t.stage_bytes);
+  };
+  if (t.NT == 1) {
+    // one tile: the block is the tile's rows, H*W apart
+    pick(kDrainOneTile, (int)HW, 1, (size_t)128 * HW * 2);
+  } else if (HW % 8 == 0 && y_aligned) {
+    // rows of 16-byte aligned segments: padded staging rows, two buffers if
+    // three ring slots still fit, else one with two slots, else no staging
+    const int pitch = 2 * t.NP + 16;
+    const size_t one = (size_t)128 * pitch;
+    if (slots(2 * one) >= 3) pick(kDrainRows, pitch, 2, 2 * one);
+    else if (slots(one) >= 2) pick(kDrainRows, pitch, 1, one);
+    else pick(kDrainDirect, 0, 0, 0);
+  } else {
+    pick(kDrainRowsLegacy, t.NP, 1, (size_t)128 * t.NP * 2);
+  }
   return t;
 }
 
@@ -704,9 +820,10 @@ size_t pool_stage_smem(int64_t C, int64_t HW);   // stage.cu
 int tc_supported(int dtype, int64_t C, int64_t HW, int64_t k) {
   if (!(dtype == MOCE_BF16 || dtype == MOCE_F16) || HW < 1 || HW > 65536 || k < 1 || k > 64 || C < 1 || C > 512)
     return 0;
-  const TcShape t = tc_shape(C, HW, k);
+  // the shapes of an aligned and of an unaligned Y both have to fit
   const size_t smem_max = (size_t)smem_optin_tc();
-  return (t.fixed + 2 * t.qbytes <= smem_max && pool_stage_smem(C, HW) <= smem_max) ? 1 : 0;
+  return (tc_shape(C, HW, k, true).ns >= 2 && tc_shape(C, HW, k, false).ns >= 2 &&
+          pool_stage_smem(C, HW) <= smem_max) ? 1 : 0;
 }
 
 }  // namespace moce
@@ -766,18 +883,11 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
                "moce_mix_tc: needs bf16/fp16, C <= 512, k <= 64 within shared memory");
   MOCE_REQUIRE(((uintptr_t)xstage & 15) == 0, MOCE_ERR_INVALID, "moce_mix_tc: xstage must be 16-byte aligned");
   MOCE_REQUIRE(B < 65536 && (E_r + 1) * HW < (int64_t)1 << 31, MOCE_ERR_UNSUPPORTED, "moce_mix_tc: shape too large");
-  TcShape sh = tc_shape(C, HW, k);
-  if (sh.direct_ok && (((uintptr_t)y) & 15) != 0) {
-    // Y not 16-byte aligned: stage the rows in shared memory instead
-    sh.direct_ok = 0;
-    sh.stg_pitch = sh.NP;
-    sh.fixed += tc_stage_out_bytes(sh.NP, 2);
-  }
+  const TcShape sh = tc_shape(C, HW, k, (((uintptr_t)y) & 15) == 0);
   const int Kp = sh.Kp, KMAX = sh.KMAX;
   const size_t qbytes = sh.qbytes, fixed = sh.fixed;
-  const int smem_max = smem_optin_tc();
-  const int ns = (int)std::min<size_t>((size_t)kMaxSlots, ((size_t)smem_max > fixed ? smem_max - fixed : 0) / qbytes);
-  MOCE_REQUIRE(ns >= 2, MOCE_ERR_UNSUPPORTED, "moce_mix_tc: not enough shared memory (%d B)", smem_max);
+  const int ns = sh.ns;
+  MOCE_REQUIRE(ns >= 2, MOCE_ERR_UNSUPPORTED, "moce_mix_tc: not enough shared memory (%d B)", smem_optin_tc());
   const size_t smem = fixed + (size_t)ns * qbytes;
   const int n_tiles = (int)((E_r + 127) / 128);
   int n_bsplit = num_sms() / n_tiles;
@@ -785,13 +895,13 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
   if (n_bsplit > B) n_bsplit = (int)B;
   TcArgs a{xstage, y, z, idx, ln, gate_w, gate_b, T_out, tmin_tau, trange_tau,
            (int)B, (int)C, (int)HW, (int)E_r, (int)k, Kp, n_tiles, n_bsplit, ns, sh.NP, sh.NA, sh.P, sh.NT,
-           sh.tmem_cols, sh.direct_ok, sh.stg_pitch};
+           sh.tmem_cols, sh.drain, sh.stg_pitch, sh.nsb, sh.stage_bytes};
   return dispatch_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
     if constexpr (sizeof(T) != 2) {
       return set_error(MOCE_ERR_UNSUPPORTED, "moce_mix_tc: 16-bit inputs only");
     } else {
-      const bool gen = !(sh.NP == 64 && sh.NA == 1 && sh.P == 2 && sh.NT == 1);
+      const bool gen = !(sh.NP == 64 && sh.NA == 1 && sh.P == 2 && sh.NT == 1 && sh.drain == kDrainOneTile);
       void (*kern)(TcArgs) =
           gen ? (KMAX == 16 ? mix_tc_kernel<T, 16, true> : KMAX == 32 ? mix_tc_kernel<T, 32, true>
                                                                       : mix_tc_kernel<T, 64, true>)

@@ -1,13 +1,15 @@
-// Pass 1 of the tensor-core path (16-bit inputs, H*W <= 64): one read of X
+// Pass 1 of the tensor-core path (16-bit inputs): one read of X
 // gives
 //   z[b,c]       = mean_p X[b,c,p]                     (MoCE.py:174 / 212)
 //   Y[b,E_r,p]   = mean over uncovered channels of X   (MoCE.py:191-196,
 //                  0 when every channel is covered      moce_kernel.cu:148-231)
 //   xstage[b]    = X_b in the tensor-core operand layout of the mix
-// Each sample is one cluster of kStageCtas CTAs, one channel quarter per CTA,
-// so that a sample's loads spread over several SMs and many loads are in
-// flight per SM.  The per-pixel residual sums of the quarters are added up
-// by cluster rank 0 through distributed shared memory.
+// Maps of at most 64 pixels (7x7): each sample is one cluster of kStageCtas
+// CTAs, one channel quarter per CTA, so that a sample's loads spread over
+// several SMs and many loads are in flight per SM; the per-pixel residual
+// sums of the quarters are added up by cluster rank 0 through distributed
+// shared memory.  Larger maps (14x14 and up): pool_stage_rows_kernel, a warp
+// per channel row and no shared memory (below).
 //
 // Operand layout (matches the B operand of mix_tc.cu): per sample NT pixel
 // tiles of NP pixels (a multiple of 16, at most 256; the last tile shorter),
@@ -158,13 +160,145 @@ __global__ void __cluster_dims__(kStageCtas, 1, 1) __launch_bounds__(kStageThrea
   }
 }
 
+// eight 16-bit values of one 16-byte unit, summed in order
+template <typename T>
+__device__ __forceinline__ float sum8(const int4& v) {
+  union {
+    int4 v;
+    T e[8];
+  } u;
+  u.v = v;
+  float s = 0.0f;
+#pragma unroll
+  for (int t = 0; t < 8; ++t) s += to_f(u.e[t]);
+  return s;
+}
+
+constexpr int kRowsWarps = 8;                 // channels per block of pool_stage_rows_kernel
+
+// Pixels 8u .. 8u+7 of one channel row (zero past H*W) as one 16-byte unit:
+// one 16-byte load (VEC 8: H*W % 8 == 0, X 16-byte aligned), two 8-byte
+// loads (VEC 4: H*W % 4 == 0, X 8-byte aligned) or element loads.
+template <typename T, int VEC>
+__device__ __forceinline__ int4 load_chunk(const T* __restrict__ row, int u, int HW) {
+  if constexpr (VEC == 8) {
+    return __ldg(reinterpret_cast<const int4*>(row) + u);
+  } else if constexpr (VEC == 4) {
+    const uint2* r2 = reinterpret_cast<const uint2*>(row) + 2 * u;
+    const uint2 lo = __ldg(r2);
+    const uint2 hi = (8 * u + 4 < HW) ? __ldg(r2 + 1) : make_uint2(0u, 0u);
+    return make_int4((int)lo.x, (int)lo.y, (int)hi.x, (int)hi.y);
+  } else {
+    union {
+      int4 v;
+      T e[8];
+    } w;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) w.e[t] = (8 * u + t < HW) ? row[8 * u + t] : from_f<T>(0.0f);
+    return w.v;
+  }
+}
+
+// Pass 1 for maps of more than 64 pixels.  Every 8-pixel chunk of a channel
+// row is one 16-byte unit of the operand layout, where it only moves to
+// position (chunk ^ (c & 7)) of its 128-byte row.  A warp streams one channel
+// row of one sample: chunk loads, the same units stored at their
+// operand-layout positions (a warp's 32 units fill whole 128-byte rows, so
+// stores stay coalesced), and the channel sum accumulated on the way (z,
+// MoCE.py:174 / 212).  Rows C..Kp-1 and the pixels past H*W in the last tile
+// are written as zeros.  One extra block per sample writes the residual
+// expert's row: the mean over the uncovered channels, in ascending channel
+// order (MoCE.py:191-196), or zeros.
+template <typename T, int VEC>
+__global__ void __launch_bounds__(kRowsWarps * 32)
+    pool_stage_rows_kernel(const T* __restrict__ x, int C, int HW, const int32_t* __restrict__ mask,
+                           const int32_t* __restrict__ meta, float* __restrict__ z, T* __restrict__ y, int E,
+                           int4* __restrict__ xstage, int Kp, int NP, int NT, int NA, int nblk_ch) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nv = (HW + 7) >> 3;                           // chunks of a channel row
+  if ((int)blockIdx.x == nblk_ch) {
+    if (!y) return;
+    const int n_u = (mask && meta) ? meta[0] : 0;
+    T* yr = y + ((size_t)b * E + (E - 1)) * HW;
+    const T* xb = x + (size_t)b * C * HW;
+    for (int q = threadIdx.x; q < nv; q += blockDim.x) {
+      float acc[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) acc[t] = 0.0f;
+      if (n_u > 0) {
+        for (int c = 0; c < C; ++c) {
+          if (mask[c] != 1) continue;                     // uniform across the block
+          union {
+            int4 v;
+            T e[8];
+          } w;
+          w.v = load_chunk<T, VEC>(xb + (size_t)c * HW, q, HW);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) acc[t] += to_f(w.e[t]);
+        }
+      }
+      union {
+        int4 v;
+        T e[8];
+      } o;
+#pragma unroll
+      for (int t = 0; t < 8; ++t) o.e[t] = from_f<T>(n_u > 0 ? acc[t] / (float)n_u : 0.0f);
+      if constexpr (VEC == 8) {
+        reinterpret_cast<int4*>(yr)[q] = o.v;             // Y rows 16-byte aligned (checked by the host)
+      } else {
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+          if (8 * q + t < HW) yr[8 * q + t] = o.e[t];
+      }
+    }
+    return;
+  }
+  const int c = blockIdx.x * kRowsWarps + warp;
+  if (c >= Kp) return;
+  const int Kq = Kp >> 2;
+  const int npc = NP >> 3;                                // units per pixel tile
+  const int nck = NT * npc;                               // units including the last tile's padding
+  int4* xs = xstage + (size_t)b * NT * Kp * NA * 8 + ((size_t)(c / Kq) * NA * Kq + (c % Kq)) * 8;
+  const size_t tile_units = (size_t)Kp * NA * 8;
+  const T* src = x + ((size_t)b * C + (c < C ? c : 0)) * HW;
+  const int sw = c & 7;
+  const bool real = c < C;
+  float s = 0.0f;
+  constexpr int U = 4;
+  for (int u0 = lane; u0 < nck; u0 += 32 * U) {
+    int4 v[U];
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const int u = u0 + 32 * j;
+      v[j] = make_int4(0, 0, 0, 0);
+      if (real && u < nv) v[j] = load_chunk<T, VEC>(src, u, HW);
+    }
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const int u = u0 + 32 * j;
+      if (u < nck) {
+        const int t = u / npc, pin = u - t * npc;
+        xs[(size_t)t * tile_units + (size_t)(pin >> 3) * Kq * 8 + ((pin & 7) ^ sw)] = v[j];
+        s += sum8<T>(v[j]);
+      }
+    }
+  }
+  s = warp_sum(s);
+  if (real && lane == 0) z[(size_t)b * C + c] = s * (1.0f / (float)HW);
+}
+
 }  // namespace
 
 // channels per CTA: a multiple of 8, so that every chunk starts on a 16-byte
 // boundary of the sample
 int pool_stage_cc(int64_t C) { return (int)(((C + kStageCtas - 1) / kStageCtas + 7) / 8 * 8); }
 
+// shared memory of the per-sample cluster kernel (maps of at most 64 pixels;
+// larger maps stream channel rows without shared memory)
 size_t pool_stage_smem(int64_t C, int64_t HW) {
+  if (HW > 64) return 0;
   const int64_t cc = pool_stage_cc(C);
   return (((size_t)cc * HW * 2 + 15) & ~size_t(15)) + (size_t)((HW + 3) & ~3) * 4 + (size_t)cc * 4;
 }
@@ -184,7 +318,7 @@ extern "C" int moce_pool_stage(const void* x, int dtype, int64_t B, int64_t C, i
   MOCE_REQUIRE(B > 0 && C >= 1 && HW >= 1 && E_r >= 0, MOCE_ERR_INVALID, "moce_pool_stage: invalid shape");
   MOCE_REQUIRE(HW <= 65536, MOCE_ERR_UNSUPPORTED, "moce_pool_stage: H*W too large");
   MOCE_REQUIRE(B < 65536 && C <= 4096, MOCE_ERR_UNSUPPORTED, "moce_pool_stage: shape too large");
-  {
+  if (HW <= 64) {
     int dev = 0, smem_max = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
@@ -199,10 +333,24 @@ extern "C" int moce_pool_stage(const void* x, int dtype, int64_t B, int64_t C, i
   int64_t np = ((HW + nt0 - 1) / nt0 + 15) / 16 * 16;
   if (np > 256) np = 256;
   const int NP = (int)np, NT = (int)((HW + np - 1) / np), NA = (int)((np + 63) / 64);
+  // maps of more than 64 pixels stream channel rows, smaller maps go
+  // through the per-sample cluster
+  const bool rows = HW > 64;
+  const int vec = (HW % 8 == 0 && ((uintptr_t)x & 15) == 0 && (!y || ((uintptr_t)y & 15) == 0)) ? 8
+                  : (HW % 4 == 0 && ((uintptr_t)x & 7) == 0) ? 4 : 1;
   return dispatch_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
     if constexpr (sizeof(T) != 2) {
       return set_error(MOCE_ERR_UNSUPPORTED, "moce_pool_stage: 16-bit inputs only");
+    } else if (rows) {
+      const int nblk_ch = (Kp + kRowsWarps - 1) / kRowsWarps;
+      const dim3 grid((unsigned)(nblk_ch + 1), (unsigned)B);
+      auto kern = vec == 8 ? pool_stage_rows_kernel<T, 8> : vec == 4 ? pool_stage_rows_kernel<T, 4>
+                                                                     : pool_stage_rows_kernel<T, 1>;
+      kern<<<grid, kRowsWarps * 32, 0, (cudaStream_t)stream>>>(
+          static_cast<const T*>(x), (int)C, (int)HW, mask, meta, z, static_cast<T*>(y), (int)(E_r + 1),
+          reinterpret_cast<int4*>(xstage), Kp, NP, NT, NA, nblk_ch);
+      return check_launch("pool_stage_rows_kernel");
     } else {
       auto kern = (NT * NA > 1) ? pool_stage_kernel<T, true> : pool_stage_kernel<T, false>;
       if (smem > 48 * 1024 &&

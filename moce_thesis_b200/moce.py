@@ -61,10 +61,11 @@ class _Route:
     def forward(self, x, gate_w, gate_b, tmin_tau, trange_tau, want_T=False, out=None):
         """Both forward passes; returns (y, z, T).  T is None unless wanted.
 
-        bf16/fp16 inputs with H*W <= 64 and C <= 512 run the tensor-core
-        mix; shapes with H*W <= 512 and k <= 64 whose sample fits shared
-        memory the lanes-over-pixels CUDA-core mix; other shapes the
-        scheduled CUDA-core mix (k <= 44) or the general two passes.
+        bf16/fp16 inputs with C <= 512 and k <= 64 whose tiles fit shared
+        memory run the tensor-core mix; shapes with H*W <= 512 and k <= 64
+        whose sample fits shared memory the lanes-over-pixels CUDA-core mix;
+        other shapes the scheduled CUDA-core mix (k <= 44) or the general two
+        passes.
         """
         m = native()
         k = int(self.idx.shape[1])
@@ -231,3 +232,88 @@ class MoCE(nn.Module):
         gb = self.cached_gate_bias.detach().reshape(-1).float().contiguous()
         y, _, _ = route.forward(x.contiguous(), gw, gb, self.cached_temp_min_tau, self.cached_temp_range_tau)
         return y
+
+    # ------------------------------------------------------------------
+    def forward_host(self, x, out=None, slices=8):
+        """Eval forward of a batch in host memory, with the result in host memory.
+
+        The batch is cut into ``slices`` runs of samples that flow through
+        three CUDA streams of this layer's device: the host-to-device copy of
+        run i+1, the two passes of run i and the device-to-host copy of run
+        i-1 overlap, so both PCIe directions and the GPU are busy at once
+        (the routed output is four times the input at the stage-4 shape, so
+        the device-to-host copy sets the pace).  Two device buffers per
+        direction are reused across runs and calls.
+
+        ``x``: CPU tensor [B, C, H, W], pinned for the copies to be
+        asynchronous.  ``out``: CPU tensor [B, E, H, W] of x's dtype
+        (allocated pinned when not given).  The call returns once the work
+        is queued; the current CUDA stream waits on the last copy, so
+        synchronizing that stream (or the device) completes the result, and
+        ``x`` must not change before then.
+        """
+        if self.cached_indices is None:
+            raise RuntimeError("MoCE eval cache not built. Call build_moce_cache(model) before eval.")
+        if x.is_cuda:
+            raise ValueError("forward_host: x must be a host tensor")
+        dev = self.routing_logits.device
+        if dev.type != "cuda":
+            raise RuntimeError("forward_host: the layer must be on a CUDA device")
+        B, C, H, W = x.shape
+        E = self.num_experts
+        if out is None:
+            out = torch.empty(B, E, H, W, dtype=x.dtype, pin_memory=True)
+        if B == 0:
+            return out
+        route = self._route
+        if route is None or route.idx.device != dev:
+            route = _Route(self.routing_logits, self.k, transposed=False)
+            self._route = route
+        gw = self.cached_gate_weight.detach().reshape(-1).float().contiguous()
+        gb = self.cached_gate_bias.detach().reshape(-1).float().contiguous()
+        n = max(1, min(int(slices), B))
+        run = (B + n - 1) // n
+        st = self.__dict__.get("_host_pipe")
+        key = (dev, run, C, H, W, E, x.dtype)
+        if st is None or st["key"] != key:
+            if st is not None:
+                # the old buffers return to the allocator on the current
+                # stream: order them after the side streams' last use
+                cur0 = torch.cuda.current_stream(dev)
+                cur0.wait_stream(st["h2d"])
+                cur0.wait_stream(st["d2h"])
+            with torch.cuda.device(dev):
+                st = {"key": key,
+                      "h2d": torch.cuda.Stream(dev), "d2h": torch.cuda.Stream(dev),
+                      "xb": [torch.empty(run, C, H, W, dtype=x.dtype, device=dev) for _ in range(2)],
+                      "yb": [torch.empty(run, E, H, W, dtype=x.dtype, device=dev) for _ in range(2)],
+                      "in": [torch.cuda.Event() for _ in range(2)],
+                      "done": [torch.cuda.Event() for _ in range(2)],
+                      "out": [torch.cuda.Event() for _ in range(2)],
+                      "used": [False, False]}
+            self.__dict__["_host_pipe"] = st
+        cur = torch.cuda.current_stream(dev)
+        h2d, d2h = st["h2d"], st["d2h"]
+        last = None
+        for i, b0 in enumerate(range(0, B, run)):
+            b1 = min(B, b0 + run)
+            j = i % 2
+            xb, yb = st["xb"][j][:b1 - b0], st["yb"][j][:b1 - b0]
+            if st["used"][j]:
+                h2d.wait_event(st["done"][j])              # the passes that read xb are done
+            with torch.cuda.stream(h2d):
+                xb.copy_(x[b0:b1], non_blocking=True)
+                st["in"][j].record(h2d)
+            cur.wait_event(st["in"][j])
+            if st["used"][j]:
+                cur.wait_event(st["out"][j])               # the copy that read yb is done
+            route.forward(xb, gw, gb, self.cached_temp_min_tau, self.cached_temp_range_tau, False, yb)
+            st["done"][j].record(cur)
+            d2h.wait_event(st["done"][j])
+            with torch.cuda.stream(d2h):
+                out[b0:b1].copy_(yb, non_blocking=True)
+                st["out"][j].record(d2h)
+            st["used"][j] = True
+            last = st["out"][j]
+        cur.wait_event(last)
+        return out

@@ -137,3 +137,30 @@ def test_binding_errors_match_reference_checks():
         mc.fused_moce_forward_dynamic_temp(X, idx, torch.rand(2, 3, 3, device=DEV), mask)
     with pytest.raises(RuntimeError, match="mask_int must be int32"):
         mc.fused_moce_forward_dynamic_temp(X, idx, torch.rand(2, 3, 2, device=DEV), mask.long())
+
+
+@pytest.mark.parametrize("dtype,B,C,Hh,E,k,slices", [
+    (torch.bfloat16, 37, 128, 7, 200, 16, 8),    # runs of 5 samples, the last one of 2; tensor-core path
+    (torch.float32, 9, 64, 14, 70, 8, 4),        # fp32: lanes-over-pixels path
+    (torch.bfloat16, 3, 64, 28, 40, 8, 8),       # fewer samples than runs
+])
+def test_forward_host_matches_forward_eval(dtype, B, C, Hh, E, k, slices):
+    """MoCE.forward_host (pinned host X in, host Y out, copies and passes
+    overlapped on three streams) gives the bits of forward_eval on the
+    device, on two calls in a row (buffers reused) and after a call of
+    another batch size (buffers replaced)."""
+    gen = torch.Generator().manual_seed(B + C)
+    torch.manual_seed(B)
+    m = MoCE(in_channels=C, sampling_factor=1, k=k, temp_min=0.1, temp_max=10.0)
+    m.num_experts = E
+    m.routing_logits = torch.nn.Parameter(torch.randn(E - 1, C, generator=gen))
+    m = m.to(DEV).eval()
+    m.build_eval_cache()
+    with torch.no_grad():
+        for b in (B, B, B + 1, B):
+            xh = torch.randn(b, C, Hh, Hh, generator=gen).abs().to(dtype).pin_memory()
+            ref = m(xh.to(DEV)).cpu()
+            yh = m.forward_host(xh, slices=slices)
+            torch.cuda.current_stream().synchronize()
+            assert yh.is_pinned() and yh.shape == ref.shape and yh.dtype == dtype
+            assert torch.equal(yh, ref)

@@ -44,6 +44,9 @@ def relerr(a, b):
     (2, 128, 28, 28, 90, 16, torch.bfloat16),   # 28x28: four pixel tiles of 208 / 160, weights reused per tile
     (1, 64, 56, 56, 40, 8, torch.float16),      # 56x56: thirteen pixel tiles of 256 / 64
     (2, 32, 20, 21, 3, 4, torch.bfloat16),      # HW == 420: two tiles of 224 / 196, uncovered channels
+    (1, 256, 56, 56, 140, 8, torch.bfloat16),   # 56x56 at C=256: one staging buffer of padded rows
+    (2, 64, 24, 24, 20, 8, torch.bfloat16),     # HW == 576 in 8-pixel rows with uncovered channels (residual block)
+    (3, 72, 4, 4, 100, 8, torch.float16),       # HW == 16, 16-byte staging stores of one tile
 ])
 def test_tc_mix_matches_oracle(B, C, H_, W_, E, k, dtype):
     gen = torch.Generator().manual_seed(B * 100 + C + k)
@@ -107,3 +110,40 @@ def test_forward_tc_single_call_matches_two_calls():
               0.1, 9.9, capi.ptr(z1), capi.ptr(xs), capi.ptr(y1), capi.ptr(T1), capi.stream_handle())
     torch.cuda.synchronize()
     assert torch.equal(y1, y2) and torch.equal(z1, z2) and torch.equal(T1, T2)
+
+
+@pytest.mark.parametrize("C,Hh,E,k", [(128, 28, 90, 16), (64, 7, 70, 8), (96, 14, 50, 8), (32, 56, 40, 4)])
+def test_tc_unaligned_buffers(C, Hh, E, k):
+    """X and Y that start 2 bytes past a 16-byte boundary (views one element
+    into larger buffers): pass 1 takes the per-sample cluster kernel and the
+    mix stages rows with 16-bit stores and element copies; results match the
+    oracle."""
+    from moce_thesis_b200 import capi
+    gen = torch.Generator().manual_seed(C + Hh)
+    B = 2
+    HW = Hh * Hh
+    X = torch.randn(B, C, Hh, Hh, generator=gen).abs()
+    L = torch.randn(E - 1, C, generator=gen)
+    gw = (torch.rand(1, k, generator=gen) - 0.5).to(DEV)
+    gb = torch.zeros(1, device=DEV)
+    xbuf = torch.empty(B * C * HW + 8, dtype=torch.bfloat16, device=DEV)
+    x = xbuf[1:1 + B * C * HW].view(B, C, Hh, Hh)
+    x.copy_(X.to(DEV, torch.bfloat16))
+    ybuf = torch.zeros(B * E * HW + 8, dtype=torch.bfloat16, device=DEV)
+    y = ybuf[1:1 + B * E * HW].view(B, E, Hh, Hh)
+    assert x.data_ptr() % 16 == 2 and y.data_ptr() % 16 == 2
+    r = H.route_build(L.to(DEV), k, transposed=False)
+    z = torch.empty(B, C, device=DEV)
+    T = torch.empty(B, E - 1, device=DEV)
+    xs = torch.empty(capi.lib().moce_tc_stage_bytes(B, C, HW), dtype=torch.uint8, device=DEV)
+    H.tc_fault(clear=True)
+    capi.call("moce_forward_tc", capi.ptr(x), capi.dtype_code(x), B, C, HW, capi.ptr(r["mask"]),
+              capi.ptr(r["meta"]), capi.ptr(r["idx"]), capi.ptr(r["ln"]), E - 1, k, capi.ptr(gw), capi.ptr(gb),
+              0.1, 9.9, capi.ptr(z), capi.ptr(xs), capi.ptr(y), capi.ptr(T), capi.stream_handle())
+    torch.cuda.synchronize()
+    assert H.tc_fault() == 0
+    assert ybuf[0].item() == 0 and float(ybuf[1 + B * E * HW:].abs().sum()) == 0   # nothing outside Y
+    ref = O.forward(x.float().cpu().numpy(), L.numpy(), gw.cpu().numpy(), gb.cpu().numpy(), k, 0.1, 10.0, 1.0,
+                    mode="eval")
+    got = y.float().cpu().numpy()
+    assert close(got, ref, 1e-2, 1e-3), relerr(got, ref)
