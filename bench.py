@@ -22,6 +22,8 @@ Two further workloads print their own JSON lines (not the headline):
     python bench.py --workload sweep   # per-stage sweep of ResNet-50 expand
         projections, bf16, N=256: (64, 56x56, E=256, k=8),
         (128, 28x28, 512, 16), (256, 14x14, 1024, 16), (512, 7x7, 2048, 32)
+    python bench.py --workload resnet50   # ResNet-50 + MoCE inference img/s,
+        bf16, global batch 1024 of 3x224x224 split over the GPUs
 """
 from __future__ import annotations
 
@@ -563,6 +565,63 @@ def run_sweep(args):
         dist.destroy_process_group()
 
 
+def run_resnet(args):
+    """End-to-end ResNet-50 + MoCE inference, bf16, random Kaiming init, every
+    bottleneck entrance a MoCE layer with k = C_in / 16, global batch 1024 of
+    3x224x224 N(0,1) images split over the ranks (strong scaling).  One step
+    is one forward of the local batch; img/s = global batch / max-over-ranks
+    time.  Timed with the fused MoCE -> BatchNorm -> ReLU epilogue (the
+    product path) and, for comparison, with the three ops separate."""
+    import torch
+    import torch.distributed as dist
+    world, rank, local, dev = _dist_setup()
+    from moce_thesis_b200 import resnet
+    gb = 1024
+    per = gb // world
+    kcfg = [[4, 16, 16], [16, 32, 32, 32], [32, 64, 64, 64, 64, 64], [64, 128, 128]]
+    torch.manual_seed(0)
+    model = resnet.resnet50_moce_projection(dataset="imagenet", num_classes=1000, k=kcfg)
+    model = model.to(dev, torch.bfloat16).eval()
+    resnet.build_moce_cache(model)
+    g = torch.Generator().manual_seed(rank)
+    x = torch.randn(per, 3, 224, 224, generator=g).to(dev, torch.bfloat16)
+    st = torch.cuda.current_stream()
+    res = {}
+    for fused in (True, False):
+        resnet.set_fused_epilogue(model, fused)
+        with torch.no_grad():
+            for _ in range(args.warmup):
+                model(x)
+            torch.cuda.synchronize()
+            with Clocks(local) as clk:
+                if world > 1:
+                    dist.barrier()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+                for _ in range(args.steps):
+                    model(x)
+                e1.record(st)
+                torch.cuda.synchronize()
+        ms = _max_over_ranks(e0.elapsed_time(e1), world, dev) / args.steps
+        res[fused] = (ms, clk.summary())
+    ms, clocks = res[True]
+    out = {"metric": "ResNet-50-MoCE inference img/s", "value": round(gb / (ms * 1e-3), 1), "unit": "img/s",
+           "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic N(0,1) images, seed 0 per rank; random Kaiming init",
+           "config": {"workload": "ResNet-50 + MoCE (every bottleneck entrance, k = C_in/16), ImageNet stem, "
+                                  "global batch 1024 of 3x224x224", "global_batch": gb, "per_gpu_batch": per,
+                      "parallelism": f"data-parallel x{world}, no collective in inference",
+                      "epilogue": "MoCE -> bn1 -> relu1 fused where the tensor-core path runs"},
+           "unfused": {"value": round(gb / (res[False][0] * 1e-3), 1), "ms_per_step": round(res[False][0], 3)},
+           "clocks": clocks}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -571,7 +630,7 @@ def main():
     ap.add_argument("--dtype", choices=["bf16", "fp32"], default="bf16")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["stage4", "train", "sweep"], default="stage4")
+    ap.add_argument("--workload", choices=["stage4", "train", "sweep", "resnet50"], default="stage4")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -581,6 +640,8 @@ def main():
         run_train(args)
     elif args.workload == "sweep":
         run_sweep(args)
+    elif args.workload == "resnet50":
+        run_resnet(args)
     else:
         run_ours(args)
 

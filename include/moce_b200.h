@@ -161,6 +161,26 @@ int moce_forward_tc(const void* x, int dtype, int64_t B, int64_t C, int64_t HW,
                     void* y, float* T_out, void* stream);
 
 /*
+ * moce_forward_tc with the caller's next two ops folded into the output
+ * store: every output channel e (routed experts and the residual) becomes
+ *   relu?(y[b,e,p] * out_scale[e] + out_shift[e])
+ * computed in fp32 before the one rounding to the 16-bit output type.
+ * out_scale / out_shift are fp32 [E] (E = E_r + 1): an eval-mode
+ * BatchNorm2d folded to scale = weight / sqrt(running_var + eps),
+ * shift = bias - running_mean * scale.  Replaces the MoCE -> bn1 -> relu1
+ * sequence of BottleneckWithMoCEProjection.forward (models_unified.py:155-165).
+ * T_out (when given) and z are the layer's own values, before the epilogue.
+ */
+int moce_forward_tc_ep(const void* x, int dtype, int64_t B, int64_t C,
+                       int64_t HW, const int32_t* mask, const int32_t* meta,
+                       const int32_t* idx, const float* ln, int64_t E_r,
+                       int64_t k, const float* gate_w, const float* gate_b,
+                       float tmin_tau, float trange_tau,
+                       const float* out_scale, const float* out_shift,
+                       int out_relu, float* z, void* xstage, void* y,
+                       float* T_out, void* stream);
+
+/*
  * CUDA-core pass 2 with lanes over pixels, any dtype, H*W <= 512, k <= 64,
  * for maps of a few hundred pixels (14x14, 28x28 stages; fp32 anywhere).
  * Same inputs and outputs as moce_mix_tc with X itself in place of the
@@ -172,6 +192,22 @@ int moce_forward_tc(const void* x, int dtype, int64_t B, int64_t C, int64_t HW,
  */
 int moce_px_supported(int dtype, int64_t C, int64_t HW, int64_t k);
 int moce_mix_px(const void* x, int dtype, int64_t B, int64_t C, int64_t HW,
+                const float* z, const int32_t* idx, const float* ln,
+                int64_t E_r, int64_t k, const float* gate_w,
+                const float* gate_b, float tmin_tau, float trange_tau,
+                void* y, float* T_out, void* stream);
+
+/*
+ * Pass 2 on CUDA cores for samples too large for shared memory (C >= 1024 at
+ * 14x14, 2048 at 7x7, 512 at 28x28: the deep ResNet-50 bottlenecks,
+ * models_unified.py:227-258).  Same inputs, outputs and arithmetic as
+ * moce_mix_px (replacing moce_kernel.cu:57-141 with the gate and softmax of
+ * MoCE.py:216-221), but each expert's k support rows are read from X in
+ * global memory, where a sample stays in L2 while its CTAs run.
+ * moce_gx_supported: H*W <= 1024, k <= 128, C <= 16384.
+ */
+int moce_gx_supported(int dtype, int64_t C, int64_t HW, int64_t k);
+int moce_mix_gx(const void* x, int dtype, int64_t B, int64_t C, int64_t HW,
                 const float* z, const int32_t* idx, const float* ln,
                 int64_t E_r, int64_t k, const float* gate_w,
                 const float* gate_b, float tmin_tau, float trange_tau,

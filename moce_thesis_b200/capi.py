@@ -40,8 +40,12 @@ SIGNATURES = {
     "moce_tc_fault": (_i32, [_p, _i32]),
     "moce_forward_tc": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _p, _p, _f32, _f32, _p, _p, _p,
                                 _p, _p]),
+    "moce_forward_tc_ep": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _p, _p, _f32, _f32, _p, _p, _i32,
+                                  _p, _p, _p, _p, _p]),
     "moce_px_supported": (_i32, [_i32, _i64, _i64, _i64]),
     "moce_mix_px": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p, _f32, _f32, _p, _p, _p]),
+    "moce_gx_supported": (_i32, [_i32, _i64, _i64, _i64]),
+    "moce_mix_gx": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p, _f32, _f32, _p, _p, _p]),
     "moce_gate_temperature": (_i32, [_p, _i32, _p, _i64, _i64, _i64, _p, _i64, _i64, _p, _p, _f32, _f32,
                                      _p, _p, _p]),
     "moce_mix": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p, _p]),

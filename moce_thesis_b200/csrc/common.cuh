@@ -61,6 +61,21 @@ __device__ __forceinline__ float temperature(float g, float tmin_tau, float tran
   return (t < 1e-3f) ? 1e-3f : t;
 }
 
+// Output epilogue: the caller's eval-mode BatchNorm folded to a per-channel
+// affine (scale, shift) and an optional ReLU, applied to a finished output
+// value before it is rounded and stored (models_unified.py:158-165 runs
+// MoCE -> bn1 -> relu1).  A NaN stays NaN through the ReLU, as in torch.
+struct OutEpilogue {
+  const float* scale;   // [E] or null (no epilogue)
+  const float* shift;   // [E]
+  int relu;
+};
+
+__device__ __forceinline__ float apply_epilogue(float v, float sc, float sh, int relu) {
+  const float r = fmaf(v, sc, sh);
+  return (relu && r < 0.0f) ? 0.0f : r;
+}
+
 // ---------------------------------------------------------------- host side
 
 // Records the message for moce_last_error() and returns `code`.

@@ -129,6 +129,7 @@ struct TcArgs {
   int stg_pitch;                  // staging row pitch: elements (kDrainOneTile, kDrainRowsLegacy), bytes (kDrainRows)
   int nsb;                        // staging buffers (kDrainRows)
   uint32_t stage_bytes;           // shared memory of the output staging area
+  OutEpilogue ep;                 // caller's folded BatchNorm + ReLU on the outputs (scale null: none)
 };
 
 // How the drain moves a finished accumulator to Y.
@@ -552,6 +553,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     // ===================== drain (warps 8-11): TMEM lane quarter = warp % 4
     const int dt = tid - kWeightThreads;                      // row within the tile
     const bool has_row = dt < rows;
+    // output epilogue of this thread's row (expert e0 + dt)
+    const bool hep = a.ep.scale != nullptr;
+    const float esc = (hep && has_row) ? a.ep.scale[e0 + dt] : 1.0f;
+    const float esh = (hep && has_row) ? a.ep.shift[e0 + dt] : 0.0f;
+    const int erelu = a.ep.relu;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     T* yg = static_cast<T*>(a.y);
     const int drain = kGen ? a.drain : (int)kDrainOneTile;
@@ -581,6 +587,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
 #pragma unroll
             for (int p = 0; p < 32; ++p)
               v[p] = (P == 2) ? __uint_as_float(r0[p]) + __uint_as_float(r1[p]) : __uint_as_float(r0[p]);
+            if (hep) {
+#pragma unroll
+              for (int p = 0; p < 32; ++p) v[p] = apply_epilogue(v[p], esc, esh, erelu);
+            }
 #pragma unroll
             for (int p = 0; p < 32; ++p)
               if (cb + p < HW) stg[dt * HW + cb + p] = from_f<T>(v[p]);
@@ -603,7 +613,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       // Pixel tiles of 16-byte aligned rows: each thread stages its row with
       // 16-byte stores into rows 2 NP + 16 bytes apart (the 16-byte skew puts
       // the 32 rows of a warp's store in distinct bank quads), then copies it
-      // out with one bulk copy; `nsb` buffers alternate.
+      // out with one bulk copy; `nsb` buffers alternate.  (Warp-coalesced row
+      // stores in place of the bulk copies measured 249 against 228 us at
+      // 56x56, C=64.)
       const uint32_t pitch = (uint32_t)a.stg_pitch;
       unsigned char* row0 = reinterpret_cast<unsigned char*>(stg) + (size_t)dt * pitch;
       for (int u = 0; u < nu; ++u) {
@@ -618,26 +630,62 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         if (!role_sync_and(kBarDrain, kDrainThreads, ok)) break;
         tc_fence_after();
         const uint32_t tb = tmem + lane_base + (uint32_t)(s * P * NP);
-        for (int cb = 0; cb < tp; cb += 32) {                 // uniform across the warp
-          uint32_t r0[32], r1[32];
-          tmem_ld32_nowait(tb + cb, r0);
-          if (P == 2) tmem_ld32_nowait(tb + NP + cb, r1);
-          tmem_wait_ld();
-          if (cb + 32 >= tp) {                                // last read of the buffer
-            tc_fence_before();
-            mbar_arrive(&bars->d_empty[s]);
-          }
+        // 32 columns (two partials when P == 2) into the staging row
+        auto put = [&](const uint32_t* ra, const uint32_t* rb, int cb) {
           if (has_row) {
             float v[32];
 #pragma unroll
             for (int p = 0; p < 32; ++p)
-              v[p] = (P == 2) ? __uint_as_float(r0[p]) + __uint_as_float(r1[p]) : __uint_as_float(r0[p]);
+              v[p] = (P == 2) ? __uint_as_float(ra[p]) + __uint_as_float(rb[p]) : __uint_as_float(ra[p]);
+            if (hep) {
+#pragma unroll
+              for (int p = 0; p < 32; ++p) v[p] = apply_epilogue(v[p], esc, esh, erelu);
+            }
 #pragma unroll
             for (int g = 0; g < 4; ++g)
               if (cb + 8 * g < tp)
                 *reinterpret_cast<uint4*>(row + (size_t)(cb + 8 * g) * 2) =
                     make_uint4(pack2_16<T>(v[8 * g], v[8 * g + 1]), pack2_16<T>(v[8 * g + 2], v[8 * g + 3]),
                                pack2_16<T>(v[8 * g + 4], v[8 * g + 5]), pack2_16<T>(v[8 * g + 6], v[8 * g + 7]));
+          }
+        };
+        if (P == 1) {
+          // one accumulator: two 32-column chunks in flight (r0 / r1), so
+          // each load's latency overlaps the conversion and stores of the
+          // chunk before it; the buffer is released after its last load
+          uint32_t r0[32], r1[32];
+          tmem_ld32_nowait(tb, r0);
+          tmem_wait_ld();
+          for (int cb = 0; cb < tp; cb += 64) {               // uniform across the warp
+            if (cb + 32 < tp) {
+              tmem_ld32_nowait(tb + cb + 32, r1);
+            } else {
+              tc_fence_before();
+              mbar_arrive(&bars->d_empty[s]);
+            }
+            put(r0, r0, cb);
+            if (cb + 32 >= tp) break;
+            tmem_wait_ld();
+            if (cb + 64 < tp) {
+              tmem_ld32_nowait(tb + cb + 64, r0);
+            } else {
+              tc_fence_before();
+              mbar_arrive(&bars->d_empty[s]);
+            }
+            put(r1, r1, cb + 32);
+            tmem_wait_ld();
+          }
+        } else {
+          for (int cb = 0; cb < tp; cb += 32) {               // uniform across the warp
+            uint32_t r0[32], r1[32];
+            tmem_ld32_nowait(tb + cb, r0);
+            tmem_ld32_nowait(tb + NP + cb, r1);
+            tmem_wait_ld();
+            if (cb + 32 >= tp) {                              // last read of the buffer
+              tc_fence_before();
+              mbar_arrive(&bars->d_empty[s]);
+            }
+            put(r0, r1, cb);
           }
         }
         if (has_row) {
@@ -671,6 +719,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
 #pragma unroll
             for (int p = 0; p < 32; ++p)
               v[p] = (P == 2) ? __uint_as_float(r0[p]) + __uint_as_float(r1[p]) : __uint_as_float(r0[p]);
+            if (hep) {
+#pragma unroll
+              for (int p = 0; p < 32; ++p) v[p] = apply_epilogue(v[p], esc, esh, erelu);
+            }
             if (cb + 32 <= tp) {
 #pragma unroll
               for (int g = 0; g < 4; ++g) {
@@ -709,7 +761,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
           if (has_row) {
 #pragma unroll
             for (int p = 0; p < 32; ++p) {
-              const float v = (P == 2) ? __uint_as_float(r0[p]) + __uint_as_float(r1[p]) : __uint_as_float(r0[p]);
+              float v = (P == 2) ? __uint_as_float(r0[p]) + __uint_as_float(r1[p]) : __uint_as_float(r0[p]);
+              if (hep) v = apply_epilogue(v, esc, esh, erelu);
               if (cb + p < tp) stg[dt * tp + cb + p] = from_f<T>(v);
             }
           }
@@ -748,12 +801,12 @@ struct TcShape {
   int ns;                         // X quarter slots in the ring
 };
 
-// pixel tiling: NT tiles of NP pixels (a multiple of 16, at most 256), the
+// pixel tiling: NT tiles of NP pixels (a multiple of 16, at most np_max), the
 // last tile shorter
-void tc_tiling(int64_t HW, int* NP, int* NT, int* NA) {
-  const int64_t nt0 = (HW + kTcMaxN - 1) / kTcMaxN;
+void tc_tiling(int64_t HW, int np_max, int* NP, int* NT, int* NA) {
+  const int64_t nt0 = (HW + np_max - 1) / np_max;
   int64_t np = ((HW + nt0 - 1) / nt0 + 15) / 16 * 16;
-  if (np > kTcMaxN) np = kTcMaxN;
+  if (np > np_max) np = np_max;
   *NP = (int)np;
   *NT = (int)((HW + np - 1) / np);
   *NA = (int)((np + 63) / 64);
@@ -764,10 +817,10 @@ int smem_optin_tc();
 // The kernel's shape for (C, H*W, k) and a Y that is (or is not) 16-byte
 // aligned: tiling, accumulators, output path and shared-memory plan.
 // ns == 0 when the shape does not fit shared memory.
-TcShape tc_shape(int64_t C, int64_t HW, int64_t k, bool y_aligned = true) {
+TcShape tc_shape(int64_t C, int64_t HW, int64_t k, bool y_aligned, int np_max) {
   TcShape t;
   t.Kp = (int)((C + 63) / 64 * 64);
-  tc_tiling(HW, &t.NP, &t.NT, &t.NA);
+  tc_tiling(HW, np_max, &t.NP, &t.NT, &t.NA);
   // the drain reads 32 columns at a time, so the last read of a region whose
   // width is not a multiple of 32 reaches 16 columns past it: allocate that
   const int over = (t.NP % 32) ? 16 : 0;
@@ -808,6 +861,30 @@ TcShape tc_shape(int64_t C, int64_t HW, int64_t k, bool y_aligned = true) {
   return t;
 }
 
+// The largest pixel tile (256, 128 or 64 pixels) whose kernel fits shared
+// memory with at least three (else two) ring slots, for an aligned and an
+// unaligned Y and any k <= 64; 0 if none does.  Wide C (a 128 KB weight tile at C = 512)
+// needs the smaller tiles: at 28x28, 208-pixel tiles make 64 KB ring slots.
+// The staged layout of pass 1 follows the same choice (tc_stage_tiling).
+int tc_np_max(int64_t C, int64_t HW) {
+  // first choice: three ring slots for an aligned Y (copies run ahead of the
+  // MMAs); else two
+  for (int need = 3; need >= 2; --need)
+    for (int npm = kTcMaxN; npm >= 64; npm /= 2)
+      if (tc_shape(C, HW, 64, true, npm).ns >= need && tc_shape(C, HW, 64, false, npm).ns >= 2) return npm;
+  return 0;
+}
+
+void tc_stage_tiling(int64_t C, int64_t HW, int* NP, int* NT, int* NA) {
+  int npm = tc_np_max(C, HW);
+  tc_tiling(HW, npm > 0 ? npm : kTcMaxN, NP, NT, NA);
+}
+
+TcShape tc_shape_for(int64_t C, int64_t HW, int64_t k, bool y_aligned) {
+  const int npm = tc_np_max(C, HW);
+  return tc_shape(C, HW, k, y_aligned, npm > 0 ? npm : kTcMaxN);
+}
+
 int smem_optin_tc() {
   int dev = 0, smem_max = 0;
   cudaGetDevice(&dev);
@@ -822,7 +899,7 @@ int tc_supported(int dtype, int64_t C, int64_t HW, int64_t k) {
     return 0;
   // the shapes of an aligned and of an unaligned Y both have to fit
   const size_t smem_max = (size_t)smem_optin_tc();
-  return (tc_shape(C, HW, k, true).ns >= 2 && tc_shape(C, HW, k, false).ns >= 2 &&
+  return (tc_np_max(C, HW) > 0 && tc_shape_for(C, HW, k, true).ns >= 2 && tc_shape_for(C, HW, k, false).ns >= 2 &&
           pool_stage_smem(C, HW) <= smem_max) ? 1 : 0;
 }
 
@@ -837,43 +914,63 @@ extern "C" int moce_tc_supported(int dtype, int64_t C, int64_t HW, int64_t k) {
 extern "C" size_t moce_tc_stage_bytes(int64_t B, int64_t C, int64_t HW) {
   if (HW < 1) return 0;
   int NP, NT, NA;
-  tc_tiling(HW, &NP, &NT, &NA);
+  tc_stage_tiling(C, HW, &NP, &NT, &NA);
   return (size_t)B * (size_t)NT * (size_t)((C + 63) / 64 * 64) * (size_t)NA * 128;
 }
 
 static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
                          const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
                          const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out, void* stream,
-                         bool dependent);
+                         bool dependent, OutEpilogue ep);
 
 extern "C" int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
                            const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
                            const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out,
                            void* stream) {
   return mix_tc_launch(xstage, dtype, B, C, HW, z, idx, ln, E_r, k, gate_w, gate_b, tmin_tau, trange_tau, y, T_out,
-                       stream, false);
+                       stream, false, OutEpilogue{nullptr, nullptr, 0});
 }
 
-extern "C" int moce_pool_stage(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
-                               const int32_t* meta, float* z, void* y, int64_t E_r, void* xstage, void* stream);
+namespace moce {
+int pool_stage_run(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
+                   const int32_t* meta, float* z, void* y, int64_t E_r, void* xstage, OutEpilogue ep, void* stream);
+}
+
+static int forward_tc_run(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
+                          const int32_t* meta, const int32_t* idx, const float* ln, int64_t E_r, int64_t k,
+                          const float* gate_w, const float* gate_b, float tmin_tau, float trange_tau, float* z,
+                          void* xstage, void* y, float* T_out, OutEpilogue ep, void* stream) {
+  if (B == 0) return MOCE_OK;
+  int rc = pool_stage_run(x, dtype, B, C, HW, mask, meta, z, y, E_r, xstage, ep, stream);
+  if (rc) return rc;
+  // pass 2 as a programmatic dependent of pass 1: its prologue (A zeroing,
+  // tensor-memory allocation, route loads) overlaps pass 1's tail
+  return mix_tc_launch(xstage, dtype, B, C, HW, z, idx, ln, E_r, k, gate_w, gate_b, tmin_tau, trange_tau, y, T_out,
+                       stream, true, ep);
+}
 
 extern "C" int moce_forward_tc(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
                                const int32_t* meta, const int32_t* idx, const float* ln, int64_t E_r, int64_t k,
                                const float* gate_w, const float* gate_b, float tmin_tau, float trange_tau, float* z,
                                void* xstage, void* y, float* T_out, void* stream) {
-  if (B == 0) return MOCE_OK;
-  int rc = moce_pool_stage(x, dtype, B, C, HW, mask, meta, z, y, E_r, xstage, stream);
-  if (rc) return rc;
-  // pass 2 as a programmatic dependent of pass 1: its prologue (A zeroing,
-  // tensor-memory allocation, route loads) overlaps pass 1's tail
-  return mix_tc_launch(xstage, dtype, B, C, HW, z, idx, ln, E_r, k, gate_w, gate_b, tmin_tau, trange_tau, y, T_out,
-                       stream, true);
+  return forward_tc_run(x, dtype, B, C, HW, mask, meta, idx, ln, E_r, k, gate_w, gate_b, tmin_tau, trange_tau, z,
+                        xstage, y, T_out, OutEpilogue{nullptr, nullptr, 0}, stream);
+}
+
+extern "C" int moce_forward_tc_ep(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
+                                  const int32_t* meta, const int32_t* idx, const float* ln, int64_t E_r, int64_t k,
+                                  const float* gate_w, const float* gate_b, float tmin_tau, float trange_tau,
+                                  const float* out_scale, const float* out_shift, int out_relu, float* z,
+                                  void* xstage, void* y, float* T_out, void* stream) {
+  MOCE_REQUIRE(out_scale && out_shift, MOCE_ERR_INVALID, "moce_forward_tc_ep: null scale or shift");
+  return forward_tc_run(x, dtype, B, C, HW, mask, meta, idx, ln, E_r, k, gate_w, gate_b, tmin_tau, trange_tau, z,
+                        xstage, y, T_out, OutEpilogue{out_scale, out_shift, out_relu ? 1 : 0}, stream);
 }
 
 static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
                          const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
                          const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out, void* stream,
-                         bool dependent) {
+                         bool dependent, OutEpilogue ep) {
   if (B == 0) return MOCE_OK;
   MOCE_REQUIRE(xstage && z && idx && ln && gate_w && gate_b && y, MOCE_ERR_INVALID,
                "moce_mix_tc: null pointer argument");
@@ -883,7 +980,7 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
                "moce_mix_tc: needs bf16/fp16, C <= 512, k <= 64 within shared memory");
   MOCE_REQUIRE(((uintptr_t)xstage & 15) == 0, MOCE_ERR_INVALID, "moce_mix_tc: xstage must be 16-byte aligned");
   MOCE_REQUIRE(B < 65536 && (E_r + 1) * HW < (int64_t)1 << 31, MOCE_ERR_UNSUPPORTED, "moce_mix_tc: shape too large");
-  const TcShape sh = tc_shape(C, HW, k, (((uintptr_t)y) & 15) == 0);
+  const TcShape sh = tc_shape_for(C, HW, k, (((uintptr_t)y) & 15) == 0);
   const int Kp = sh.Kp, KMAX = sh.KMAX;
   const size_t qbytes = sh.qbytes, fixed = sh.fixed;
   const int ns = sh.ns;
@@ -895,7 +992,7 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
   if (n_bsplit > B) n_bsplit = (int)B;
   TcArgs a{xstage, y, z, idx, ln, gate_w, gate_b, T_out, tmin_tau, trange_tau,
            (int)B, (int)C, (int)HW, (int)E_r, (int)k, Kp, n_tiles, n_bsplit, ns, sh.NP, sh.NA, sh.P, sh.NT,
-           sh.tmem_cols, sh.drain, sh.stg_pitch, sh.nsb, sh.stage_bytes};
+           sh.tmem_cols, sh.drain, sh.stg_pitch, sh.nsb, sh.stage_bytes, ep};
   return dispatch_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
     if constexpr (sizeof(T) != 2) {

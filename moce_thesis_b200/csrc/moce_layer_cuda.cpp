@@ -448,6 +448,39 @@ std::vector<torch::Tensor> forward_tc(torch::Tensor x, torch::Tensor idx, torch:
   return {y, z, T};
 }
 
+// the tensor-core forward with the caller's eval BatchNorm (folded to a
+// per-channel scale / shift over the E outputs) and ReLU applied in the store
+torch::Tensor forward_tc_ep(torch::Tensor x, torch::Tensor idx, torch::Tensor ln, torch::Tensor mask,
+                            torch::Tensor meta, torch::Tensor gate_w, torch::Tensor gate_b, double tmin_tau,
+                            double trange_tau, torch::Tensor out_scale, torch::Tensor out_shift, bool relu,
+                            c10::optional<torch::Tensor> out_opt) {
+  for (auto* t : {&x, &idx, &ln, &mask, &meta, &gate_w, &gate_b, &out_scale, &out_shift}) {
+    CHECK_INPUT(*t);
+  }
+  TORCH_CHECK(idx.scalar_type() == torch::kInt32 && ln.scalar_type() == torch::kFloat32, "idx int32, ln float32");
+  const c10::cuda::CUDAGuard guard(x.device());
+  Dims d = dims(x, idx);
+  TORCH_CHECK(out_scale.scalar_type() == torch::kFloat32 && out_shift.scalar_type() == torch::kFloat32 &&
+                  out_scale.numel() == d.E_r + 1 && out_shift.numel() == d.E_r + 1,
+              "out_scale / out_shift must be float32 [E]");
+  torch::Tensor y;
+  if (out_opt.has_value()) {
+    y = *out_opt;
+    CHECK_INPUT(y);
+    TORCH_CHECK(y.scalar_type() == x.scalar_type() && y.numel() == d.B * (d.E_r + 1) * d.HW, "out mismatch");
+  } else {
+    y = torch::empty({d.B, d.E_r + 1, d.H, d.W}, x.options());
+  }
+  auto z = f32_opts_like(x, {d.B, d.C});
+  auto xstage = torch::empty({(int64_t)moce_tc_stage_bytes(d.B, d.C, d.HW)}, x.options().dtype(torch::kUInt8));
+  ok(moce_forward_tc_ep(x.data_ptr(), dtype_of(x), d.B, d.C, d.HW, mask.data_ptr<int32_t>(),
+                        meta.data_ptr<int32_t>(), idx.data_ptr<int32_t>(), ln.data_ptr<float>(), d.E_r, d.K,
+                        gate_w.data_ptr<float>(), gate_b.data_ptr<float>(), (float)tmin_tau, (float)trange_tau,
+                        out_scale.data_ptr<float>(), out_shift.data_ptr<float>(), relu ? 1 : 0, z.data_ptr<float>(),
+                        xstage.data_ptr(), y.data_ptr(), nullptr, cur_stream()));
+  return y;
+}
+
 bool px_supported(torch::Tensor x, int64_t k) {
   if (x.dim() != 4) return false;
   return moce_px_supported(dtype_of(x), x.size(1), x.size(2) * x.size(3), k) != 0;
@@ -483,6 +516,41 @@ std::vector<torch::Tensor> forward_px(torch::Tensor x, torch::Tensor idx, torch:
   return {y, z, T};
 }
 
+bool gx_supported(torch::Tensor x, int64_t k) {
+  if (x.dim() != 4) return false;
+  return moce_gx_supported(dtype_of(x), x.size(1), x.size(2) * x.size(3), k) != 0;
+}
+
+// pass 1 (pool + residual) and the CUDA-core pass 2 reading X from global memory
+std::vector<torch::Tensor> forward_gx(torch::Tensor x, torch::Tensor idx, torch::Tensor ln, torch::Tensor mask,
+                                      torch::Tensor meta, torch::Tensor gate_w, torch::Tensor gate_b,
+                                      double tmin_tau, double trange_tau, bool want_T,
+                                      c10::optional<torch::Tensor> out_opt) {
+  for (auto* t : {&x, &idx, &ln, &mask, &meta, &gate_w, &gate_b}) {
+    CHECK_INPUT(*t);
+  }
+  TORCH_CHECK(idx.scalar_type() == torch::kInt32 && ln.scalar_type() == torch::kFloat32, "idx int32, ln float32");
+  const c10::cuda::CUDAGuard guard(x.device());
+  Dims d = dims(x, idx);
+  torch::Tensor y;
+  if (out_opt.has_value()) {
+    y = *out_opt;
+    CHECK_INPUT(y);
+    TORCH_CHECK(y.scalar_type() == x.scalar_type() && y.numel() == d.B * (d.E_r + 1) * d.HW, "out mismatch");
+  } else {
+    y = torch::empty({d.B, d.E_r + 1, d.H, d.W}, x.options());
+  }
+  auto z = f32_opts_like(x, {d.B, d.C});
+  auto T = want_T ? f32_opts_like(x, {d.B, d.E_r}) : f32_opts_like(x, {0});
+  ok(moce_pool_residual(x.data_ptr(), dtype_of(x), d.B, d.C, d.HW, mask.data_ptr<int32_t>(),
+                        meta.data_ptr<int32_t>(), z.data_ptr<float>(), y.data_ptr(), d.E_r, cur_stream()));
+  ok(moce_mix_gx(x.data_ptr(), dtype_of(x), d.B, d.C, d.HW, z.data_ptr<float>(), idx.data_ptr<int32_t>(),
+                 ln.data_ptr<float>(), d.E_r, d.K, gate_w.data_ptr<float>(), gate_b.data_ptr<float>(),
+                 (float)tmin_tau, (float)trange_tau, y.data_ptr(), want_T ? T.data_ptr<float>() : nullptr,
+                 cur_stream()));
+  return {y, z, T};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -512,9 +580,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("meta"), py::arg("group_expert"), py::arg("sched"), py::arg("gate_w"), py::arg("gate_b"),
         py::arg("tmin_tau"), py::arg("trange_tau"), py::arg("want_T") = false, py::arg("out") = py::none());
   m.def("tc_supported", &tc_supported, "Whether the tensor-core mix takes this input");
+  m.def("forward_tc_ep", &forward_tc_ep,
+        "Tensor-core forward with a folded BatchNorm (scale, shift per output channel) and ReLU on the outputs",
+        py::arg("x"), py::arg("idx"), py::arg("ln"), py::arg("mask"), py::arg("meta"), py::arg("gate_w"),
+        py::arg("gate_b"), py::arg("tmin_tau"), py::arg("trange_tau"), py::arg("out_scale"), py::arg("out_shift"),
+        py::arg("relu"), py::arg("out") = py::none());
   m.def("forward_tc", &forward_tc, "Pool + residual, then the tensor-core mix: (y, z, T)", py::arg("x"),
         py::arg("idx"), py::arg("ln"), py::arg("mask"), py::arg("meta"), py::arg("gate_w"), py::arg("gate_b"),
         py::arg("tmin_tau"), py::arg("trange_tau"), py::arg("want_T") = false, py::arg("out") = py::none());
+  m.def("gx_supported", &gx_supported, "Whether the global-memory CUDA-core mix takes this input");
+  m.def("forward_gx", &forward_gx, "Pool + residual, then the CUDA-core mix reading X from global memory: (y, z, T)",
+        py::arg("x"), py::arg("idx"), py::arg("ln"), py::arg("mask"), py::arg("meta"), py::arg("gate_w"),
+        py::arg("gate_b"), py::arg("tmin_tau"), py::arg("trange_tau"), py::arg("want_T") = false,
+        py::arg("out") = py::none());
   m.def("px_supported", &px_supported, "Whether the lanes-over-pixels CUDA-core mix takes this input");
   m.def("forward_px", &forward_px, "Pool + residual, then the lanes-over-pixels CUDA-core mix: (y, z, T)",
         py::arg("x"), py::arg("idx"), py::arg("ln"), py::arg("mask"), py::arg("meta"), py::arg("gate_w"),

@@ -33,6 +33,7 @@ struct PxArgs {
   float tmin_tau, trange_tau;
   int B, C, HW, HWp, E_r, k;
   int vec_out;                    // Y rows allow 4-element vector stores
+  int vec_in;                     // X rows allow 4-element vector loads (global-memory kernel)
 };
 
 // grid (n_echunks, B); kPxThreads threads; warp per expert.
@@ -245,6 +246,108 @@ __global__ void __launch_bounds__(kPxThreads, 1) mix_px_grouped_kernel(PxArgs a)
   }
 }
 
+
+// Pass 2 on CUDA cores for samples that do not fit shared memory (C of 1024
+// and more at 14x14, 2048 at 7x7, 512 at 28x28): the same warp per expert
+// and lanes over pixels as mix_px_kernel, but each support row is read from
+// global memory, where the CTAs of one sample (consecutive blocks) keep X_b
+// resident in L2 and L1 while they walk its experts.  Up to KL x 32 = 128
+// supports per expert (lane i holds supports i, i + 32, ...) and NSLAB x 128
+// pixels per row; rows with H*W % 4 == 0 are read as 4-element vectors.
+template <typename T, int NSLAB, int KL>
+__global__ void __launch_bounds__(kPxThreads, 1) mix_gx_kernel(PxArgs a) {
+  extern __shared__ __align__(16) unsigned char s_raw[];
+  const int C = a.C, HW = a.HW, k = a.k, E_r = a.E_r;
+  float* s_z = reinterpret_cast<float*>(s_raw);                                        // C
+  float* s_gw = s_z + C;                                                               // k
+  const int b = blockIdx.y, ch = blockIdx.x, nch = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const T* xb = static_cast<const T*>(a.x) + (size_t)b * C * HW;
+  for (int c = threadIdx.x; c < C; c += kPxThreads) s_z[c] = a.z[(size_t)b * C + c];
+  for (int i = threadIdx.x; i < k; i += kPxThreads) s_gw[i] = a.gate_w[i];
+  __syncthreads();
+  const float bias = a.gate_b[0];
+  const int per = (E_r + nch - 1) / nch;
+  const int e0 = ch * per, e1 = min(E_r, e0 + per);
+  const int E = E_r + 1;
+  const bool vin = a.vec_in != 0;
+  T* yg = static_cast<T*>(a.y);
+  for (int e = e0 + warp; e < e1; e += kPxWarps) {
+    int c_l[KL];
+    float u_l[KL];
+#pragma unroll
+    for (int q = 0; q < KL; ++q) {
+      const int i = lane + 32 * q;
+      c_l[q] = i < k ? a.idx[(size_t)e * k + i] : 0;
+      u_l[q] = i < k ? a.ln[(size_t)e * k + i] : -INFINITY;
+    }
+    float gp = 0.0f;
+#pragma unroll
+    for (int q = 0; q < KL; ++q)
+      if (lane + 32 * q < k) gp += s_gw[lane + 32 * q] * s_z[c_l[q]];
+    const float g = warp_sum(gp) + bias;
+    const float t = temperature(g, a.tmin_tau, a.trange_tau, nullptr);
+    if (a.T_out && lane == 0) a.T_out[(size_t)b * E_r + e] = t;
+    float m = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < KL; ++q) {
+      if (lane + 32 * q < k) u_l[q] = u_l[q] / t;
+      m = nan_max(m, u_l[q]);
+    }
+    m = warp_max(m);
+    float a_l[KL], sum = 0.0f;
+#pragma unroll
+    for (int q = 0; q < KL; ++q) {
+      a_l[q] = (lane + 32 * q < k) ? expf(u_l[q] - m) : 0.0f;
+      sum += a_l[q];
+    }
+    sum = warp_sum(sum);
+#pragma unroll
+    for (int q = 0; q < KL; ++q) a_l[q] /= sum;
+
+    float acc[NSLAB][4];
+#pragma unroll
+    for (int sl = 0; sl < NSLAB; ++sl)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[sl][j] = 0.0f;
+#pragma unroll
+    for (int q = 0; q < KL; ++q) {
+      const int nq = min(32, k - 32 * q);
+#pragma unroll 4
+      for (int j = 0; j < nq; ++j) {
+        const int c = __shfl_sync(kFull, c_l[q], j);
+        const float w = __shfl_sync(kFull, a_l[q], j);
+        const T* row = xb + (size_t)c * HW;
+#pragma unroll
+        for (int sl = 0; sl < NSLAB; ++sl) {
+          const int p = 128 * sl + 4 * lane;
+          float f[4];
+          if (vin && p + 3 < HW) {
+            ld4<T>(row + p, f);
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) f[jj] = (p + jj < HW) ? to_f(row[p + jj]) : 0.0f;
+          }
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) acc[sl][jj] = fmaf(w, f[jj], acc[sl][jj]);
+        }
+      }
+    }
+    T* yr = yg + ((size_t)b * E + e) * HW;
+#pragma unroll
+    for (int sl = 0; sl < NSLAB; ++sl) {
+      const int p = 128 * sl + 4 * lane;
+      if (p + 3 < HW && a.vec_out) {
+        st4<T>(yr + p, acc[sl]);
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj)
+          if (p + jj < HW) yr[p + jj] = from_f<T>(acc[sl][jj]);
+      }
+    }
+  }
+}
+
 }  // namespace
 
 size_t px_smem_bytes(int64_t C, int64_t HW, int64_t k, size_t esize) {
@@ -258,6 +361,10 @@ int px_supported(int dtype, int64_t C, int64_t HW, int64_t k) {
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   return px_smem_bytes(C, HW, k, dtype_size(dtype)) <= (size_t)smem_max ? 1 : 0;
+}
+
+int gx_supported(int dtype, int64_t C, int64_t HW, int64_t k) {
+  return (dtype_ok(dtype) && HW >= 1 && HW <= 1024 && k >= 1 && k <= 128 && C >= 1 && C <= 16384) ? 1 : 0;
 }
 
 }  // namespace moce
@@ -296,7 +403,7 @@ extern "C" int moce_mix_px(const void* x, int dtype, int64_t B, int64_t C, int64
   if (grouped && per > 32 * kPxWarps) nch = (E_r + 32 * kPxWarps - 1) / (32 * kPxWarps);
   const int vec = (HW % 4 == 0) && (((uintptr_t)y) % 16 == 0);
   PxArgs a{x, y, z, idx, ln, gate_w, gate_b, T_out, tmin_tau, trange_tau,
-           (int)B, (int)C, (int)HW, HWp, (int)E_r, (int)k, vec};
+           (int)B, (int)C, (int)HW, HWp, (int)E_r, (int)k, vec, 0};
   return dispatch_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
     void (*kern)(PxArgs) = nullptr;
@@ -317,5 +424,57 @@ extern "C" int moce_mix_px(const void* x, int dtype, int64_t B, int64_t C, int64
       return set_error(MOCE_ERR_CUDA, "moce_mix_px: cannot reserve %zu B shared memory", smem);
     kern<<<dim3((unsigned)nch, (unsigned)B), kPxThreads, smem, (cudaStream_t)stream>>>(a);
     return check_launch("mix_px_kernel");
+  });
+}
+
+
+extern "C" int moce_gx_supported(int dtype, int64_t C, int64_t HW, int64_t k) { return gx_supported(dtype, C, HW, k); }
+
+extern "C" int moce_mix_gx(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
+                           const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
+                           const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out,
+                           void* stream) {
+  if (B == 0) return MOCE_OK;  // an empty batch is a no-op
+  MOCE_REQUIRE(x && z && idx && ln && gate_w && gate_b && y, MOCE_ERR_INVALID, "moce_mix_gx: null pointer argument");
+  MOCE_REQUIRE(dtype_ok(dtype), MOCE_ERR_INVALID, "moce_mix_gx: unknown dtype %d", dtype);
+  MOCE_REQUIRE(B > 0 && C >= 1 && HW >= 1 && E_r >= 1 && k >= 1 && k <= C, MOCE_ERR_INVALID,
+               "moce_mix_gx: invalid shape");
+  MOCE_REQUIRE(B < 65536 && (E_r + 1) * HW < (int64_t)1 << 31 && C * HW < (int64_t)1 << 31, MOCE_ERR_UNSUPPORTED,
+               "moce_mix_gx: shape too large");
+  MOCE_REQUIRE(gx_supported(dtype, C, HW, k), MOCE_ERR_UNSUPPORTED,
+               "moce_mix_gx: needs H*W <= 1024, k <= 128 and C <= 16384");
+  const size_t esize = dtype_size(dtype);
+  const size_t smem = (size_t)C * 4 + (size_t)k * 4;
+  const int nslab = (int)((HW + 127) / 128);
+  // expert chunks per sample: enough CTAs to cover the SMs four times over
+  int64_t nch = (4LL * num_sms() + B - 1) / B;
+  const int64_t max_ch = (E_r + kPxWarps - 1) / kPxWarps;
+  if (nch > max_ch) nch = max_ch;
+  if (nch < 1) nch = 1;
+  const int vout = (HW % 4 == 0) && (((uintptr_t)y) % 16 == 0);
+  const int vin = (HW % 4 == 0) && (((uintptr_t)x) % (4 * esize) == 0);
+  PxArgs a{x, y, z, idx, ln, gate_w, gate_b, T_out, tmin_tau, trange_tau,
+           (int)B, (int)C, (int)HW, (int)HW, (int)E_r, (int)k, vout, vin};
+  return dispatch_dtype(dtype, [&](auto tag) {
+    using T = decltype(tag);
+    void (*kern)(PxArgs) = nullptr;
+    const int ns = nslab <= 1 ? 1 : nslab <= 2 ? 2 : nslab <= 4 ? 4 : 8;
+#define MOCE_GX_PICK(NS)                                                                          \
+  case NS:                                                                                        \
+    kern = k <= 32 ? mix_gx_kernel<T, NS, 1> : k <= 64 ? mix_gx_kernel<T, NS, 2> : mix_gx_kernel<T, NS, 4>; \
+    break;
+    switch (ns) {
+      MOCE_GX_PICK(1)
+      MOCE_GX_PICK(2)
+      MOCE_GX_PICK(4)
+      MOCE_GX_PICK(8)
+      default: return set_error(MOCE_ERR_UNSUPPORTED, "moce_mix_gx: H*W=%lld", (long long)HW);
+    }
+#undef MOCE_GX_PICK
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return set_error(MOCE_ERR_CUDA, "moce_mix_gx: cannot reserve %zu B shared memory", smem);
+    kern<<<dim3((unsigned)nch, (unsigned)B), kPxThreads, smem, (cudaStream_t)stream>>>(a);
+    return check_launch("mix_gx_kernel");
   });
 }

@@ -34,7 +34,7 @@ template <typename T, bool kTiled>
 __global__ void __cluster_dims__(kStageCtas, 1, 1) __launch_bounds__(kStageThreads)
     pool_stage_kernel(const T* __restrict__ x, int C, int HW, int cc, const int32_t* __restrict__ mask,
                       const int32_t* __restrict__ meta, float* __restrict__ z, T* __restrict__ y, int E,
-                      int4* __restrict__ xstage, int Kp, int NP, int NT, int NA) {
+                      int4* __restrict__ xstage, int Kp, int NP, int NT, int NA, OutEpilogue ep) {
   extern __shared__ __align__(16) unsigned char s_raw[];
   T* s_x = reinterpret_cast<T*>(s_raw);                                            // cc x HW
   float* s_res = reinterpret_cast<float*>(s_raw + (((size_t)cc * HW * sizeof(T) + 15) & ~size_t(15)));  // HW
@@ -143,6 +143,8 @@ __global__ void __cluster_dims__(kStageCtas, 1, 1) __launch_bounds__(kStageThrea
         xs[((((size_t)tl * 4 + c / Kq) * NA + at) * Kq + (c % Kq)) * 8 + j] = u.v;
     }
   }
+  // residual row, with the output epilogue of channel E-1 when one is given
+  const float esc = ep.scale ? ep.scale[E - 1] : 1.0f, esh = ep.scale ? ep.shift[E - 1] : 0.0f;
   if (n_u > 0) {
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
     if (rank == 0 && y) {
@@ -150,13 +152,15 @@ __global__ void __cluster_dims__(kStageCtas, 1, 1) __launch_bounds__(kStageThrea
       for (int p = tid; p < HW; p += kStageThreads) {
         float r = 0.0f;
         for (int q = 0; q < kStageCtas; ++q) r += cluster.map_shared_rank(s_res, q)[p];
-        yr[p] = from_f<T>(r / (float)n_u);
+        r = r / (float)n_u;
+        yr[p] = from_f<T>(ep.scale ? apply_epilogue(r, esc, esh, ep.relu) : r);
       }
     }
     cluster.sync();                                 // peers' shared memory stays until rank 0 has read it
   } else if (rank == 0 && y) {
     T* yr = y + ((size_t)b * E + (E - 1)) * HW;
-    for (int p = tid; p < HW; p += kStageThreads) yr[p] = from_f<T>(0.0f);
+    const T zv = from_f<T>(ep.scale ? apply_epilogue(0.0f, esc, esh, ep.relu) : 0.0f);
+    for (int p = tid; p < HW; p += kStageThreads) yr[p] = zv;
   }
 }
 
@@ -213,7 +217,8 @@ template <typename T, int VEC>
 __global__ void __launch_bounds__(kRowsWarps * 32)
     pool_stage_rows_kernel(const T* __restrict__ x, int C, int HW, const int32_t* __restrict__ mask,
                            const int32_t* __restrict__ meta, float* __restrict__ z, T* __restrict__ y, int E,
-                           int4* __restrict__ xstage, int Kp, int NP, int NT, int NA, int nblk_ch) {
+                           int4* __restrict__ xstage, int Kp, int NP, int NT, int NA, int nblk_ch,
+                           OutEpilogue ep) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int b = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -243,8 +248,12 @@ __global__ void __launch_bounds__(kRowsWarps * 32)
         int4 v;
         T e[8];
       } o;
+      const float esc = ep.scale ? ep.scale[E - 1] : 1.0f, esh = ep.scale ? ep.shift[E - 1] : 0.0f;
 #pragma unroll
-      for (int t = 0; t < 8; ++t) o.e[t] = from_f<T>(n_u > 0 ? acc[t] / (float)n_u : 0.0f);
+      for (int t = 0; t < 8; ++t) {
+        const float r = n_u > 0 ? acc[t] / (float)n_u : 0.0f;
+        o.e[t] = from_f<T>(ep.scale ? apply_epilogue(r, esc, esh, ep.relu) : r);
+      }
       if constexpr (VEC == 8) {
         reinterpret_cast<int4*>(yr)[q] = o.v;             // Y rows 16-byte aligned (checked by the host)
       } else {
@@ -307,8 +316,22 @@ size_t pool_stage_smem(int64_t C, int64_t HW) {
 
 using namespace moce;
 
+namespace moce {
+void tc_stage_tiling(int64_t C, int64_t HW, int* NP, int* NT, int* NA);   // mix_tc.cu
+int pool_stage_run(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
+                   const int32_t* meta, float* z, void* y, int64_t E_r, void* xstage, OutEpilogue ep, void* stream);
+}
+
 extern "C" int moce_pool_stage(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
                                const int32_t* meta, float* z, void* y, int64_t E_r, void* xstage, void* stream) {
+  return pool_stage_run(x, dtype, B, C, HW, mask, meta, z, y, E_r, xstage, OutEpilogue{nullptr, nullptr, 0},
+                        stream);
+}
+
+// pass 1 with an optional output epilogue on the residual row
+int moce::pool_stage_run(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
+                         const int32_t* meta, float* z, void* y, int64_t E_r, void* xstage, OutEpilogue ep,
+                         void* stream) {
   if (B == 0) return MOCE_OK;  // an empty batch is a no-op
   MOCE_REQUIRE(x && z && xstage, MOCE_ERR_INVALID, "moce_pool_stage: null pointer argument");
   MOCE_REQUIRE(((uintptr_t)xstage & 15) == 0, MOCE_ERR_INVALID,
@@ -328,11 +351,9 @@ extern "C" int moce_pool_stage(const void* x, int dtype, int64_t B, int64_t C, i
   const int cc = pool_stage_cc(C);
   const size_t smem = pool_stage_smem(C, HW);
   const int Kp = (int)((C + 63) / 64 * 64);
-  // pixel tiling of the tensor-core mix (mix_tc.cu, tc_tiling)
-  const int64_t nt0 = (HW + 255) / 256;
-  int64_t np = ((HW + nt0 - 1) / nt0 + 15) / 16 * 16;
-  if (np > 256) np = 256;
-  const int NP = (int)np, NT = (int)((HW + np - 1) / np), NA = (int)((np + 63) / 64);
+  // pixel tiling of the tensor-core mix
+  int NP, NT, NA;
+  tc_stage_tiling(C, HW, &NP, &NT, &NA);
   // maps of more than 64 pixels stream channel rows, smaller maps go
   // through the per-sample cluster
   const bool rows = HW > 64;
@@ -349,7 +370,7 @@ extern "C" int moce_pool_stage(const void* x, int dtype, int64_t B, int64_t C, i
                                                                      : pool_stage_rows_kernel<T, 1>;
       kern<<<grid, kRowsWarps * 32, 0, (cudaStream_t)stream>>>(
           static_cast<const T*>(x), (int)C, (int)HW, mask, meta, z, static_cast<T*>(y), (int)(E_r + 1),
-          reinterpret_cast<int4*>(xstage), Kp, NP, NT, NA, nblk_ch);
+          reinterpret_cast<int4*>(xstage), Kp, NP, NT, NA, nblk_ch, ep);
       return check_launch("pool_stage_rows_kernel");
     } else {
       auto kern = (NT * NA > 1) ? pool_stage_kernel<T, true> : pool_stage_kernel<T, false>;
@@ -359,7 +380,7 @@ extern "C" int moce_pool_stage(const void* x, int dtype, int64_t B, int64_t C, i
       const dim3 grid(kStageCtas, (unsigned)B);
       kern<<<grid, kStageThreads, smem, (cudaStream_t)stream>>>(
           static_cast<const T*>(x), (int)C, (int)HW, cc, mask, meta, z, static_cast<T*>(y), (int)(E_r + 1),
-          reinterpret_cast<int4*>(xstage), Kp, NP, NT, NA);
+          reinterpret_cast<int4*>(xstage), Kp, NP, NT, NA, ep);
       return check_launch("pool_stage_kernel");
     }
   });

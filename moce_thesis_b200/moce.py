@@ -64,8 +64,9 @@ class _Route:
         bf16/fp16 inputs with C <= 512 and k <= 64 whose tiles fit shared
         memory run the tensor-core mix; shapes with H*W <= 512 and k <= 64
         whose sample fits shared memory the lanes-over-pixels CUDA-core mix;
-        other shapes the scheduled CUDA-core mix (k <= 44) or the general two
-        passes.
+        shapes with H*W <= 1024 and k <= 128 the same mix reading X from
+        global memory; other shapes the scheduled CUDA-core mix (k <= 44) or
+        the general two passes.
         """
         m = native()
         k = int(self.idx.shape[1])
@@ -75,6 +76,10 @@ class _Route:
             return y, z, (T if want_T else None)
         if m.px_supported(x, k):
             y, z, T = m.forward_px(x, self.idx, self.ln, self.mask, self.meta, gate_w, gate_b, float(tmin_tau),
+                                   float(trange_tau), bool(want_T), out)
+            return y, z, (T if want_T else None)
+        if m.gx_supported(x, k):
+            y, z, T = m.forward_gx(x, self.idx, self.ln, self.mask, self.meta, gate_w, gate_b, float(tmin_tau),
                                    float(trange_tau), bool(want_T), out)
             return y, z, (T if want_T else None)
         if self.schedule() is not None:
@@ -232,6 +237,40 @@ class MoCE(nn.Module):
         gb = self.cached_gate_bias.detach().reshape(-1).float().contiguous()
         y, _, _ = route.forward(x.contiguous(), gw, gb, self.cached_temp_min_tau, self.cached_temp_range_tau)
         return y
+
+    # ------------------------------------------------------------------
+    def forward_eval_bn_relu(self, x, bn, relu=True):
+        """``relu(bn(forward_eval(x)))`` for an eval-mode ``BatchNorm2d`` over
+        the layer's E outputs: the sequence MoCE -> bn1 -> relu1 of
+        ``BottleneckWithMoCEProjection.forward`` (models_unified.py:155-165).
+
+        On the tensor-core path the BatchNorm, folded to a per-channel
+        scale / shift, and the ReLU are applied to each output in the mix's
+        store (one pass over Y instead of three).  Other inputs, or a
+        BatchNorm in training mode, run forward_eval and then the torch ops.
+        """
+        if self.cached_indices is None:
+            raise RuntimeError("MoCE eval cache not built. Call build_moce_cache(model) before eval.")
+        m = native()
+        use_bn_stats = (not bn.training) and bn.running_mean is not None and bn.running_var is not None
+        if not (use_bn_stats and m.tc_supported(x, self.k)):
+            y = bn(self.forward_eval(x))
+            return F.relu(y) if relu else y
+        route = self._route
+        if route is None or route.idx.device != x.device:
+            route = _Route(self.routing_logits, self.k, transposed=False)
+            self._route = route
+        with torch.no_grad():
+            inv = torch.rsqrt(bn.running_var.float() + float(bn.eps))
+            scale = inv if bn.weight is None else bn.weight.float() * inv
+            shift = -bn.running_mean.float() * scale
+            if bn.bias is not None:
+                shift = shift + bn.bias.float()
+        gw = self.cached_gate_weight.detach().reshape(-1).float().contiguous()
+        gb = self.cached_gate_bias.detach().reshape(-1).float().contiguous()
+        return m.forward_tc_ep(x.contiguous(), route.idx, route.ln, route.mask, route.meta, gw, gb,
+                               float(self.cached_temp_min_tau), float(self.cached_temp_range_tau),
+                               scale.contiguous(), shift.contiguous(), bool(relu))
 
     # ------------------------------------------------------------------
     def forward_host(self, x, out=None, slices=8):

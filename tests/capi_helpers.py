@@ -115,6 +115,25 @@ def forward_px(x, r, gate_w, gate_b, tmin_tau, trange_tau, want_T=True):
     return y, z, T
 
 
+def gx_supported(x, k):
+    C, HW = x.shape[1], x.shape[2] * x.shape[3]
+    return bool(capi.lib().moce_gx_supported(dtype_code(x), C, HW, k))
+
+
+def forward_gx(x, r, gate_w, gate_b, tmin_tau, trange_tau, want_T=True):
+    """CUDA-core path reading X from global memory: pass 1 (pool + residual), then the mix."""
+    B, C, H, W = x.shape
+    E_r, k = r["idx"].shape
+    y = torch.empty(B, E_r + 1, H, W, dtype=x.dtype, device=x.device)
+    z = torch.empty(B, C, dtype=torch.float32, device=x.device)
+    T = torch.empty(B, E_r, dtype=torch.float32, device=x.device) if want_T else None
+    call("moce_pool_residual", ptr(x), dtype_code(x), B, C, H * W, ptr(r["mask"]), ptr(r["meta"]), ptr(z), ptr(y),
+         E_r, stream_handle())
+    call("moce_mix_gx", ptr(x), dtype_code(x), B, C, H * W, ptr(z), ptr(r["idx"]), ptr(r["ln"]), E_r, k,
+         ptr(gate_w), ptr(gate_b), tmin_tau, trange_tau, ptr(y), ptr(T), stream_handle())
+    return y, z, T
+
+
 def tc_fault(clear=True):
     import ctypes
     flag = ctypes.c_int(0)
@@ -128,6 +147,9 @@ def forward(x, L, gate_w, gate_b, k, tmin, tmax, tau, route=None, path="general"
     r = route or route_build(L, k, transposed=False)
     if path == "tc":
         y, z, T = forward_tc(x, r, gate_w, gate_b, tmin * tau, (tmax - tmin) * tau)
+        return y, dict(r, z=z, T=T)
+    if path == "gx":
+        y, z, T = forward_gx(x, r, gate_w, gate_b, tmin * tau, (tmax - tmin) * tau)
         return y, dict(r, z=z, T=T)
     if path == "px":
         y, z, T = forward_px(x, r, gate_w, gate_b, tmin * tau, (tmax - tmin) * tau)

@@ -164,3 +164,30 @@ def test_forward_host_matches_forward_eval(dtype, B, C, Hh, E, k, slices):
             torch.cuda.current_stream().synchronize()
             assert yh.is_pinned() and yh.shape == ref.shape and yh.dtype == dtype
             assert torch.equal(yh, ref)
+
+
+@pytest.mark.parametrize("dtype,C,Hh,E,k", [
+    (torch.bfloat16, 128, 14, 64, 8),    # tensor-core path: epilogue in the kernels
+    (torch.float32, 64, 7, 40, 8),       # fp32: forward_eval, then torch BatchNorm and ReLU
+])
+def test_forward_eval_bn_relu(dtype, C, Hh, E, k):
+    """MoCE.forward_eval_bn_relu equals relu(bn(forward_eval(x))) for an
+    eval-mode BatchNorm2d (bf16 / fp32 tolerances)."""
+    gen = torch.Generator().manual_seed(C)
+    torch.manual_seed(C)
+    m = MoCE(in_channels=C, sampling_factor=1, k=k, temp_min=0.1, temp_max=10.0)
+    m.num_experts = E
+    m.routing_logits = torch.nn.Parameter(torch.randn(E - 1, C, generator=gen))
+    m = m.to(DEV).eval()
+    m.build_eval_cache()
+    bn = torch.nn.BatchNorm2d(E).to(DEV).eval()
+    with torch.no_grad():
+        bn.weight.copy_(torch.rand(E, generator=gen) + 0.5)
+        bn.bias.copy_(torch.randn(E, generator=gen) * 0.3)
+        bn.running_mean.copy_(torch.randn(E, generator=gen) * 0.1)
+        bn.running_var.copy_(torch.rand(E, generator=gen) + 0.5)
+        x = torch.randn(4, C, Hh, Hh, generator=gen).abs().to(DEV, dtype)
+        ref = torch.relu(bn(m(x).float())).cpu().numpy()
+        got = m.forward_eval_bn_relu(x, bn).float().cpu().numpy()
+    tol = (1e-2, 1e-3) if dtype != torch.float32 else (1e-5, 1e-6)
+    assert close(got, ref, *tol), maxrel(got, ref)

@@ -44,7 +44,8 @@ def relerr(a, b):
     (2, 128, 28, 28, 90, 16, torch.bfloat16),   # 28x28: four pixel tiles of 208 / 160, weights reused per tile
     (1, 64, 56, 56, 40, 8, torch.float16),      # 56x56: thirteen pixel tiles of 256 / 64
     (2, 32, 20, 21, 3, 4, torch.bfloat16),      # HW == 420: two tiles of 224 / 196, uncovered channels
-    (1, 256, 56, 56, 140, 8, torch.bfloat16),   # 56x56 at C=256: one staging buffer of padded rows
+    (1, 256, 56, 56, 140, 8, torch.bfloat16),   # 56x56 at C=256: 128-pixel tiles (three ring slots)
+    (2, 512, 28, 28, 130, 32, torch.bfloat16),  # 28x28 at C=512: 64-pixel tiles (a 208-pixel ring slot would not fit)
     (2, 64, 24, 24, 20, 8, torch.bfloat16),     # HW == 576 in 8-pixel rows with uncovered channels (residual block)
     (3, 72, 4, 4, 100, 8, torch.float16),       # HW == 16, 16-byte staging stores of one tile
 ])
@@ -147,3 +148,51 @@ def test_tc_unaligned_buffers(C, Hh, E, k):
                     mode="eval")
     got = y.float().cpu().numpy()
     assert close(got, ref, 1e-2, 1e-3), relerr(got, ref)
+
+
+@pytest.mark.parametrize("C,Hh,E,k,relu", [
+    (512, 7, 300, 32, True),     # 7x7 one tile, two partial accumulators
+    (256, 14, 140, 16, True),    # 14x14 one tile, one accumulator
+    (128, 28, 90, 16, False),    # 28x28 pixel tiles through padded staging rows, no ReLU
+    (96, 12, 4, 8, True),        # uncovered channels: the residual row goes through the epilogue too
+])
+def test_forward_tc_ep_matches_bn_relu(C, Hh, E, k, relu):
+    """moce_forward_tc_ep (BatchNorm folded to scale / shift and ReLU applied
+    in the output store) against forward_tc followed by torch's eval
+    BatchNorm and ReLU on the same inputs (bf16 tolerance)."""
+    from moce_thesis_b200 import capi
+    gen = torch.Generator().manual_seed(C + k)
+    B = 3
+    x = torch.randn(B, C, Hh, Hh, generator=gen).abs().to(DEV, torch.bfloat16)
+    L = torch.randn(E - 1, C, generator=gen).to(DEV)
+    gw = (torch.rand(1, k, generator=gen) - 0.5).to(DEV)
+    gb = torch.zeros(1, device=DEV)
+    bn = torch.nn.BatchNorm2d(E).to(DEV).eval()
+    with torch.no_grad():
+        bn.weight.copy_(torch.rand(E, generator=gen) * 2 - 0.5)
+        bn.bias.copy_(torch.randn(E, generator=gen) * 0.2)
+        bn.running_mean.copy_(torch.randn(E, generator=gen) * 0.1)
+        bn.running_var.copy_(torch.rand(E, generator=gen) + 0.5)
+    r = H.route_build(L, k, transposed=False)
+    y0, z0, _ = H.forward_tc(x, r, gw, gb, 0.1, 9.9)
+    with torch.no_grad():
+        ref = bn(y0.float())
+        ref = torch.relu(ref) if relu else ref
+        inv = torch.rsqrt(bn.running_var + bn.eps)
+        scale = (bn.weight * inv).contiguous()
+        shift = (bn.bias - bn.running_mean * bn.weight * inv).contiguous()
+    y = torch.empty_like(y0)
+    z = torch.empty_like(z0)
+    xs = torch.empty(capi.lib().moce_tc_stage_bytes(B, C, Hh * Hh), dtype=torch.uint8, device=DEV)
+    H.tc_fault(clear=True)
+    capi.call("moce_forward_tc_ep", capi.ptr(x), capi.dtype_code(x), B, C, Hh * Hh, capi.ptr(r["mask"]),
+              capi.ptr(r["meta"]), capi.ptr(r["idx"]), capi.ptr(r["ln"]), E - 1, k, capi.ptr(gw), capi.ptr(gb),
+              0.1, 9.9, capi.ptr(scale), capi.ptr(shift), 1 if relu else 0, capi.ptr(z), capi.ptr(xs), capi.ptr(y),
+              None, capi.stream_handle())
+    torch.cuda.synchronize()
+    assert H.tc_fault() == 0
+    assert torch.equal(z, z0)
+    got, want = y.float().cpu().numpy(), ref.cpu().numpy()
+    assert close(got, want, 1e-2, 1e-3), relerr(got, want)
+    if relu:
+        assert float(y.float().min()) >= 0.0
