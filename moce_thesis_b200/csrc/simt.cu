@@ -13,6 +13,8 @@
 // i + 32 for k <= 64); the gate Linear(k,1) on z[S_e], the temperature, and
 // the softmax of ln / T are warp reductions; then the k weighted rows are
 // summed pixel by pixel in support order and the row of Y is stored directly.
+#include <cooperative_groups.h>
+
 #include "px.cuh"
 
 namespace moce {
@@ -34,23 +36,38 @@ struct PxArgs {
   int B, C, HW, HWp, E_r, k;
   int vec_out;                    // Y rows allow 4-element vector stores
   int vec_in;                     // X rows allow 4-element vector loads (global-memory kernel)
+  int csplit;                     // channels staged per CTA (C, or ceil(C/2) in a CTA pair)
 };
 
-// grid (n_echunks, B); kPxThreads threads; warp per expert.
-template <typename T, int NSLAB, int KL>
+// grid (n_echunks, B); kPxThreads threads; warp per expert.  CL == 2: the
+// two CTAs of a cluster (consecutive expert chunks of one sample) each stage
+// half of X_b's channels, and a support row of the other half is read from
+// the peer's shared memory (distributed shared memory), so samples of up to
+// twice the shared memory of one CTA (C = 1024 at 14x14) stay on chip.
+template <typename T, int NSLAB, int KL, int CL>
 __global__ void __launch_bounds__(kPxThreads, 1) mix_px_kernel(PxArgs a) {
   extern __shared__ __align__(16) unsigned char s_raw[];
   const int C = a.C, HW = a.HW, HWp = a.HWp, k = a.k, E_r = a.E_r;
-  T* s_x = reinterpret_cast<T*>(s_raw);                                                // C x HWp
-  float* s_z = reinterpret_cast<float*>(s_raw + (((size_t)C * HWp * sizeof(T) + 15) & ~size_t(15)));  // C
+  const int Ch = (CL == 1) ? C : a.csplit;                                             // channels per CTA
+  int rank = 0;
+  if constexpr (CL > 1) rank = (int)cooperative_groups::this_cluster().block_rank();
+  const int cs0 = rank * Ch, chn = min(C, cs0 + Ch) - cs0;                             // staged here
+  T* s_x = reinterpret_cast<T*>(s_raw);                                                // Ch x HWp
+  float* s_z = reinterpret_cast<float*>(s_raw + (((size_t)Ch * HWp * sizeof(T) + 15) & ~size_t(15)));  // C
   float* s_gw = s_z + C;                                                               // k
   const int b = blockIdx.y, ch = blockIdx.x, nch = gridDim.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const T* xg = static_cast<const T*>(a.x);
-  px_stage_rows<T>(s_x, xg + (size_t)b * C * HW, C, HW, HWp);
+  px_stage_rows<T>(s_x, xg + ((size_t)b * C + cs0) * HW, chn, HW, HWp);
   for (int c = threadIdx.x; c < C; c += kPxThreads) s_z[c] = a.z[(size_t)b * C + c];
   for (int i = threadIdx.x; i < k; i += kPxThreads) s_gw[i] = a.gate_w[i];
   __syncthreads();
+  const T* s_peer = nullptr;
+  if constexpr (CL > 1) {
+    auto cluster = cooperative_groups::this_cluster();
+    cluster.sync();                                     // both halves staged
+    s_peer = cluster.map_shared_rank(s_x, rank ^ 1);
+  }
   const float bias = a.gate_b[0];
   const int per = (E_r + nch - 1) / nch;
   const int e0 = ch * per, e1 = min(E_r, e0 + per);
@@ -118,15 +135,23 @@ __global__ void __launch_bounds__(kPxThreads, 1) mix_px_kernel(PxArgs a) {
       for (int j = 0; j < nq; ++j) {
         const int c = __shfl_sync(kFull, c_l[q], j);
         const float w = __shfl_sync(kFull, a_l[q], j);
-        const T* row = s_x + (size_t)c * HWp + 4 * lane;
+        auto mix_row = [&](const T* row) {
 #pragma unroll
-        for (int sl = 0; sl < NSLAB; ++sl) {
-          if (128 * sl + 4 * lane < HW) {
-            float f[4];
-            ld4<T>(row + 128 * sl, f);
+          for (int sl = 0; sl < NSLAB; ++sl) {
+            if (128 * sl + 4 * lane < HW) {
+              float f[4];
+              ld4<T>(row + 128 * sl, f);
 #pragma unroll
-            for (int jj = 0; jj < 4; ++jj) acc[sl][jj] = fmaf(w, f[jj], acc[sl][jj]);
+              for (int jj = 0; jj < 4; ++jj) acc[sl][jj] = fmaf(w, f[jj], acc[sl][jj]);
+            }
           }
+        };
+        if constexpr (CL == 1) {
+          mix_row(s_x + (size_t)c * HWp + 4 * lane);
+        } else {
+          // the row's owner is uniform across the warp (one support at a time)
+          if (c >= cs0 && c < cs0 + chn) mix_row(s_x + (size_t)(c - cs0) * HWp + 4 * lane);
+          else mix_row(s_peer + (size_t)(c - (rank ^ 1) * Ch) * HWp + 4 * lane);
         }
       }
     }
@@ -143,6 +168,8 @@ __global__ void __launch_bounds__(kPxThreads, 1) mix_px_kernel(PxArgs a) {
       }
     }
   }
+  // the peer reads this CTA's rows until it is done
+  if constexpr (CL > 1) cooperative_groups::this_cluster().sync();
 }
 
 // k <= 32: the weights of 32 experts are computed at once with lanes over
@@ -355,12 +382,31 @@ size_t px_smem_bytes(int64_t C, int64_t HW, int64_t k, size_t esize) {
   return (((size_t)C * HWp * esize + 15) & ~size_t(15)) + (size_t)C * 4 + (size_t)k * 4;
 }
 
-int px_supported(int dtype, int64_t C, int64_t HW, int64_t k) {
-  if (!dtype_ok(dtype) || HW < 1 || HW > 512 || k < 1 || k > 64) return 0;
+// shared memory of one CTA staging Ch of the sample's C channels
+static size_t px_smem_split(int64_t C, int64_t Ch, int64_t HW, int64_t k, size_t esize) {
+  const int64_t HWp = (HW + 3) / 4 * 4;
+  return (((size_t)Ch * HWp * esize + 15) & ~size_t(15)) + (size_t)C * 4 + (size_t)k * 4;
+}
+
+static int px_smem_max() {
   int dev = 0, smem_max = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-  return px_smem_bytes(C, HW, k, dtype_size(dtype)) <= (size_t)smem_max ? 1 : 0;
+  return smem_max;
+}
+
+// CTAs per cluster that hold one sample: 1 if X_b fits one CTA's shared
+// memory, 2 if half of it does, 0 otherwise
+static int px_cluster(int dtype, int64_t C, int64_t HW, int64_t k) {
+  const size_t es = dtype_size(dtype), mx = (size_t)px_smem_max();
+  if (px_smem_split(C, C, HW, k, es) <= mx) return 1;
+  if (px_smem_split(C, (C + 1) / 2, HW, k, es) <= mx) return 2;
+  return 0;
+}
+
+int px_supported(int dtype, int64_t C, int64_t HW, int64_t k) {
+  if (!dtype_ok(dtype) || HW < 1 || HW > 512 || k < 1 || k > 128) return 0;
+  return px_cluster(dtype, C, HW, k) > 0 ? 1 : 0;
 }
 
 int gx_supported(int dtype, int64_t C, int64_t HW, int64_t k) {
@@ -385,10 +431,12 @@ extern "C" int moce_mix_px(const void* x, int dtype, int64_t B, int64_t C, int64
   MOCE_REQUIRE(B < 65536 && (E_r + 1) * HW < (int64_t)1 << 31 && C * HW < (int64_t)1 << 31, MOCE_ERR_UNSUPPORTED,
                "moce_mix_px: shape too large");
   MOCE_REQUIRE(px_supported(dtype, C, HW, k), MOCE_ERR_UNSUPPORTED,
-               "moce_mix_px: needs H*W <= 512, k <= 64 and X_b within shared memory");
+               "moce_mix_px: needs H*W <= 512, k <= 128 and X_b within the shared memory of two CTAs");
   const size_t esize = dtype_size(dtype);
   const int HWp = (int)((HW + 3) / 4 * 4);
-  const size_t smem = px_smem_bytes(C, HW, k, esize);
+  const int CL = px_cluster(dtype, C, HW, k);
+  const int64_t Ch = CL == 1 ? C : (C + 1) / 2;
+  const size_t smem = px_smem_split(C, Ch, HW, k, esize);
   const int nslab = (int)((HW + 127) / 128);
   // CTAs per sample so that the grid covers the SMs several times over
   const int per_sm = smem <= 110 * 1024 ? 2 : 1;
@@ -396,21 +444,23 @@ extern "C" int moce_mix_px(const void* x, int dtype, int64_t B, int64_t C, int64
   const int64_t max_ch = (E_r + kPxWarps - 1) / kPxWarps;
   if (nch > max_ch) nch = max_ch;
   if (nch < 1) nch = 1;
+  if (CL == 2) nch = (nch + 1) / 2 * 2;                   // whole CTA pairs
   // grouped weights (k <= 16) pay off with at least 8 experts per warp; a
   // group holds at most 32
   const int64_t per = (E_r + nch - 1) / nch;
-  const bool grouped = k <= 16 && per >= 8 * kPxWarps;
+  const bool grouped = CL == 1 && k <= 16 && per >= 8 * kPxWarps;
   if (grouped && per > 32 * kPxWarps) nch = (E_r + 32 * kPxWarps - 1) / (32 * kPxWarps);
   const int vec = (HW % 4 == 0) && (((uintptr_t)y) % 16 == 0);
   PxArgs a{x, y, z, idx, ln, gate_w, gate_b, T_out, tmin_tau, trange_tau,
-           (int)B, (int)C, (int)HW, HWp, (int)E_r, (int)k, vec, 0};
+           (int)B, (int)C, (int)HW, HWp, (int)E_r, (int)k, vec, 0, (int)Ch};
   return dispatch_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
     void (*kern)(PxArgs) = nullptr;
+#define MOCE_PX_KL(NS, CLN) (k <= 32 ? mix_px_kernel<T, NS, 1, CLN> : k <= 64 ? mix_px_kernel<T, NS, 2, CLN> \
+                                                                          : mix_px_kernel<T, NS, 4, CLN>)
 #define MOCE_PX_PICK(NS)                                                                          \
   case NS:                                                                                        \
-    kern = grouped ? mix_px_grouped_kernel<T, NS, 16>                                             \
-           : k <= 32 ? mix_px_kernel<T, NS, 1> : mix_px_kernel<T, NS, 2>;                         \
+    kern = grouped ? mix_px_grouped_kernel<T, NS, 16> : CL == 2 ? MOCE_PX_KL(NS, 2) : MOCE_PX_KL(NS, 1); \
     break;
     switch (nslab) {
       MOCE_PX_PICK(1)
@@ -420,9 +470,22 @@ extern "C" int moce_mix_px(const void* x, int dtype, int64_t B, int64_t C, int64
       default: return set_error(MOCE_ERR_UNSUPPORTED, "moce_mix_px: H*W=%lld", (long long)HW);
     }
 #undef MOCE_PX_PICK
+#undef MOCE_PX_KL
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return set_error(MOCE_ERR_CUDA, "moce_mix_px: cannot reserve %zu B shared memory", smem);
-    kern<<<dim3((unsigned)nch, (unsigned)B), kPxThreads, smem, (cudaStream_t)stream>>>(a);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)nch, (unsigned)B);
+    cfg.blockDim = dim3(kPxThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)CL;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = CL > 1 ? 1 : 0;
+    if (cudaLaunchKernelEx(&cfg, kern, a) != cudaSuccess) return check_launch("mix_px_kernel");
     return check_launch("mix_px_kernel");
   });
 }
@@ -454,7 +517,7 @@ extern "C" int moce_mix_gx(const void* x, int dtype, int64_t B, int64_t C, int64
   const int vout = (HW % 4 == 0) && (((uintptr_t)y) % 16 == 0);
   const int vin = (HW % 4 == 0) && (((uintptr_t)x) % (4 * esize) == 0);
   PxArgs a{x, y, z, idx, ln, gate_w, gate_b, T_out, tmin_tau, trange_tau,
-           (int)B, (int)C, (int)HW, (int)HW, (int)E_r, (int)k, vout, vin};
+           (int)B, (int)C, (int)HW, (int)HW, (int)E_r, (int)k, vout, vin, (int)C};
   return dispatch_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
     void (*kern)(PxArgs) = nullptr;

@@ -36,6 +36,9 @@ def relerr(a, b):
     (2, 37, 9, 9, 12, 5, torch.float32),         # odd C, HW = 81, uncovered channels (residual)
     (3, 256, 14, 14, 64, 16, torch.bfloat16),
     (2, 128, 11, 13, 40, 64, torch.float16),     # HW = 143, k = 64
+    (2, 2048, 7, 7, 60, 128, torch.bfloat16),    # k = 128 (four supports per lane), 221 KB sample in one CTA
+    (2, 1024, 14, 14, 100, 64, torch.bfloat16),  # 401 KB sample: two CTAs of a cluster hold one half each
+    (3, 600, 13, 13, 70, 100, torch.float32),    # fp32 split over a CTA pair, odd C and H*W, k = 100
 ])
 def test_px_mix_matches_oracle(B, C, H_, W_, E, k, dtype):
     gen = torch.Generator().manual_seed(B * 100 + C + k)
