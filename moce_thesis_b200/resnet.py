@@ -169,3 +169,4 @@ def set_fused_epilogue(model, on=True):
     for module in model.modules():
         if isinstance(module, BottleneckWithMoCEProjection):
             module.fuse_epilogue = bool(on)
+

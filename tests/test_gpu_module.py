@@ -191,3 +191,32 @@ def test_forward_eval_bn_relu(dtype, C, Hh, E, k):
         got = m.forward_eval_bn_relu(x, bn).float().cpu().numpy()
     tol = (1e-2, 1e-3) if dtype != torch.float32 else (1e-5, 1e-6)
     assert close(got, ref, *tol), maxrel(got, ref)
+
+
+def test_resnet_inference_paths_agree():
+    """ResNet-50 + MoCE on a small batch: with MoCE -> bn1 -> relu1 fused in
+    the MoCE kernels the logits equal the reference-order eval output within
+    bf16 tolerance (relative to the largest logit)."""
+    from moce_thesis_b200 import resnet
+    torch.manual_seed(0)
+    kcfg = [[4, 16, 16], [16, 32, 32, 32], [32, 64, 64, 64, 64, 64], [64, 128, 128]]
+    m = resnet.resnet50_moce_projection(dataset="imagenet", num_classes=1000, k=kcfg).to(DEV, torch.bfloat16).eval()
+    # BatchNorms with non-trivial statistics, so that the epilogue is exercised
+    g = torch.Generator().manual_seed(1)
+    with torch.no_grad():
+        for mod in m.modules():
+            if isinstance(mod, torch.nn.BatchNorm2d):
+                n = mod.num_features
+                mod.weight.copy_(torch.rand(n, generator=g) * 0.5 + 0.75)
+                mod.bias.copy_(torch.randn(n, generator=g) * 0.05)
+                mod.running_mean.copy_(torch.randn(n, generator=g) * 0.05)
+                mod.running_var.copy_(torch.rand(n, generator=g) * 0.5 + 0.75)
+    resnet.build_moce_cache(m)
+    x = torch.randn(4, 3, 224, 224, generator=g).to(DEV, torch.bfloat16)
+    with torch.no_grad():
+        resnet.set_fused_epilogue(m, False)
+        ref = m(x).float()
+        resnet.set_fused_epilogue(m, True)
+        fused = m(x).float()
+    scale = ref.abs().max().item()
+    assert (fused - ref).abs().max().item() <= 5e-2 * scale

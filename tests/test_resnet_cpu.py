@@ -40,3 +40,4 @@ def test_moce_layers_and_k_config():
     assert (layers[-1].in_channels, layers[-1].num_experts, layers[-1].k) == (2048, 512, 128)
     with pytest.raises(ValueError):
         resnet.normalize_k_config([[8]], [3, 4, 6, 3])
+
