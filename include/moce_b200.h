@@ -115,16 +115,18 @@ int moce_mix_scheduled(const void* x, int dtype, int64_t B, int64_t C,
                        void* y, float* T_out, void* stream);
 
 /*
- * Tensor-core fast path, for bf16 / fp16 inputs with H*W <= 256, C <= 512 and
- * k <= 64 whose operands fit the shared memory of one CTA (the 7x7 stage-4
- * and 14x14 stage-3 maps); moce_tc_supported returns 1 for those.
+ * Tensor-core fast path, for bf16 / fp16 inputs with C <= 512 and k <= 64
+ * (any H*W) whose operands fit the shared memory of one CTA (the ResNet-50
+ * maps from 56x56 to 7x7); moce_tc_supported returns 1 for those.
  *
  * moce_pool_stage: pass 1 as moce_pool_residual, plus a copy of X in the
- * tensor-core operand layout: per sample, Kp = C rounded up to 64 channel
- * rows in four K-quarters, the pixels padded to NA = ceil(round16(H*W) / 64)
- * atoms of 64; stored [quarter][atom][Kp/4 rows][128 bytes], each row's
- * 16-byte units swizzled by (channel mod 8).  moce_tc_stage_bytes gives its
- * size.
+ * tensor-core operand layout: per sample, NT pixel tiles of NP pixels (NP a
+ * multiple of 16 of at most 256, 128 or 64, chosen from C and H*W so that
+ * pass 2 fits shared memory; the last tile shorter), each with Kp = C
+ * rounded up to 64 channel rows in four K-quarters and NA = ceil(NP / 64)
+ * atoms of 64 pixels; stored [tile][quarter][atom][Kp/4 rows][128 bytes],
+ * each row's 16-byte units swizzled by (channel mod 8).  moce_tc_stage_bytes
+ * gives its size.
  *
  * moce_mix_tc: pass 2.  Same outputs as moce_mix_scheduled; the routed
  * experts are computed per sample as a dense product of the 128-expert weight
