@@ -287,7 +287,9 @@ constexpr int kWarpIssuer0 = 12, kWarpProducer = 14;
 // Tensor memory: 2 accumulator buffers x 2 partials x 64 columns.
 // kGen: N, atoms, partials and tiles from the arguments; otherwise the 7x7
 // stage-4 case (N = 64, one atom, two partials, one tile) as constants.
-template <typename T, int KMAX, bool kGen>
+// kEp: the output epilogue is applied (a separate instantiation: even an
+// untaken epilogue branch cost the tiled drain 14 %).
+template <typename T, int KMAX, bool kGen, bool kEp>
 __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   extern __shared__ unsigned char s_dyn[];
   // 1024-byte aligned operand base, offset from s_dyn so that every pointer
@@ -554,7 +556,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     const int dt = tid - kWeightThreads;                      // row within the tile
     const bool has_row = dt < rows;
     // output epilogue of this thread's row (expert e0 + dt)
-    const bool hep = a.ep.scale != nullptr;
+    constexpr bool hep = kEp;
     const float esc = (hep && has_row) ? a.ep.scale[e0 + dt] : 1.0f;
     const float esh = (hep && has_row) ? a.ep.shift[e0 + dt] : 0.0f;
     const int erelu = a.ep.relu;
@@ -587,7 +589,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
 #pragma unroll
             for (int p = 0; p < 32; ++p)
               v[p] = (P == 2) ? __uint_as_float(r0[p]) + __uint_as_float(r1[p]) : __uint_as_float(r0[p]);
-            if (hep) {
+            if constexpr (hep) {
 #pragma unroll
               for (int p = 0; p < 32; ++p) v[p] = apply_epilogue(v[p], esc, esh, erelu);
             }
@@ -637,7 +639,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
 #pragma unroll
             for (int p = 0; p < 32; ++p)
               v[p] = (P == 2) ? __uint_as_float(ra[p]) + __uint_as_float(rb[p]) : __uint_as_float(ra[p]);
-            if (hep) {
+            if constexpr (hep) {
 #pragma unroll
               for (int p = 0; p < 32; ++p) v[p] = apply_epilogue(v[p], esc, esh, erelu);
             }
@@ -719,7 +721,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
 #pragma unroll
             for (int p = 0; p < 32; ++p)
               v[p] = (P == 2) ? __uint_as_float(r0[p]) + __uint_as_float(r1[p]) : __uint_as_float(r0[p]);
-            if (hep) {
+            if constexpr (hep) {
 #pragma unroll
               for (int p = 0; p < 32; ++p) v[p] = apply_epilogue(v[p], esc, esh, erelu);
             }
@@ -762,7 +764,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
 #pragma unroll
             for (int p = 0; p < 32; ++p) {
               float v = (P == 2) ? __uint_as_float(r0[p]) + __uint_as_float(r1[p]) : __uint_as_float(r0[p]);
-              if (hep) v = apply_epilogue(v, esc, esh, erelu);
+              if constexpr (hep) v = apply_epilogue(v, esc, esh, erelu);
               if (cb + p < tp) stg[dt * tp + cb + p] = from_f<T>(v);
             }
           }
@@ -999,11 +1001,12 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
       return set_error(MOCE_ERR_UNSUPPORTED, "moce_mix_tc: 16-bit inputs only");
     } else {
       const bool gen = !(sh.NP == 64 && sh.NA == 1 && sh.P == 2 && sh.NT == 1 && sh.drain == kDrainOneTile);
-      void (*kern)(TcArgs) =
-          gen ? (KMAX == 16 ? mix_tc_kernel<T, 16, true> : KMAX == 32 ? mix_tc_kernel<T, 32, true>
-                                                                      : mix_tc_kernel<T, 64, true>)
-              : (KMAX == 16 ? mix_tc_kernel<T, 16, false> : KMAX == 32 ? mix_tc_kernel<T, 32, false>
-                                                                        : mix_tc_kernel<T, 64, false>);
+      const bool epi = ep.scale != nullptr;
+#define MOCE_TC_KMAX(G, EP)                                                                         \
+  (KMAX == 16 ? mix_tc_kernel<T, 16, G, EP> : KMAX == 32 ? mix_tc_kernel<T, 32, G, EP> : mix_tc_kernel<T, 64, G, EP>)
+      void (*kern)(TcArgs) = gen ? (epi ? MOCE_TC_KMAX(true, true) : MOCE_TC_KMAX(true, false))
+                                 : (epi ? MOCE_TC_KMAX(false, true) : MOCE_TC_KMAX(false, false));
+#undef MOCE_TC_KMAX
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return set_error(MOCE_ERR_CUDA, "moce_mix_tc: cannot reserve %zu B shared memory", smem);
       cudaLaunchConfig_t cfg = {};
