@@ -289,8 +289,15 @@ constexpr int kWarpIssuer0 = 12, kWarpProducer = 14;
 // stage-4 case (N = 64, one atom, two partials, one tile) as constants.
 // kEp: the output epilogue is applied (a separate instantiation: even an
 // untaken epilogue branch cost the tiled drain 14 %).
-template <typename T, int KMAX, bool kGen, bool kEp>
+// kW1 (pixel-tiled maps with padded staging rows, k <= 16): one weight
+// thread per row (warps 0-3; the weights change once per sample, every NT
+// tiles) and eight drain warps (4-11), two per tensor-memory lane quarter,
+// each taking one half of a tile's 32-column chunks: the drain of a
+// 128 x 256 tile, not the MMAs, sets the pace of these maps.
+template <typename T, int KMAX, bool kGen, bool kEp, bool kW1>
 __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
+  constexpr int WT = kW1 ? 128 : kWeightThreads;              // weight threads
+  constexpr int DT = kW1 ? 256 : kDrainThreads;               // drain threads
   extern __shared__ unsigned char s_dyn[];
   // 1024-byte aligned operand base, offset from s_dyn so that every pointer
   // below stays in the shared address space (LDS/STS, not generic accesses)
@@ -328,10 +335,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       mbar_init(&bars->slot_free[s], 1);
     }
     for (int h = 0; h < 2; ++h) {
-      mbar_init(&bars->a_full[h], kWeightThreads);
+      mbar_init(&bars->a_full[h], WT);
       mbar_init(&bars->a_free[h], 1);
       mbar_init(&bars->d_full[h], P);
-      mbar_init(&bars->d_empty[h], kDrainThreads);
+      mbar_init(&bars->d_empty[h], DT);
       mbar_init(&bars->fin[h], 1);
     }
     bars->abort = 0;
@@ -346,10 +353,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     }
   }
   // weight rows: threads 2r and 2r+1 share expert row e0 + r, each with KH
-  // of its supports
-  constexpr int KH = KMAX / 2;
-  const int row = tid >> 1, part = tid & 1;
-  const bool w_row = tid < kWeightThreads && row < rows;
+  // of its supports (kW1: thread r alone, with all of them)
+  constexpr int KH = kW1 ? KMAX : KMAX / 2;
+  const int row = kW1 ? tid : tid >> 1, part = kW1 ? 0 : tid & 1;
+  const bool w_row = tid < WT && row < rows;
   uint32_t chp[KH];                                           // channel << 17 | byte offset in A
   float ln2[KH];
   float mx2 = -INFINITY;
@@ -357,9 +364,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   // read from shared memory per sample
   constexpr bool kGwReg = KMAX <= 32;
   float gwr[kGwReg ? KH : 1];
-  constexpr int ZPT = 2;                                      // z values per weight thread (C <= 512)
+  constexpr int ZPT = 512 / WT;                               // z values per weight thread (C <= 512)
   float zr[ZPT];
-  if (tid < kWeightThreads) {
+  if (tid < WT) {
 #pragma unroll
     for (int jj = 0; jj < KH; ++jj) {
       const int j = part * KH + jj;
@@ -377,7 +384,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     grid_dep_wait();                                          // z comes from pass 1 (see above)
 #pragma unroll
     for (int u = 0; u < ZPT; ++u) {
-      const int c = tid + u * kWeightThreads;
+      const int c = tid + u * WT;
       zr[u] = (nb > 0 && c < C) ? a.z[(size_t)b0 * C + c] : 0.0f;
     }
   }
@@ -480,7 +487,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       umma_commit(&bars->fin[hi]);
       mbar_wait(&bars->fin[hi], 0);
     }
-  } else if (tid < kWeightThreads) {
+  } else if (tid < WT) {
     // ===================== weight rows (pairs of threads per row)
     const int e = e0 + row;
     const bool has_row = w_row;
@@ -490,7 +497,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     // softmax sum and the two half writes (k <= 32); for k <= 64 they are
     // recomputed per half to stay within the register budget
     constexpr bool kKeepW = KMAX <= 32;
-    mx2 = nan_max(mx2, __shfl_xor_sync(kFull, mx2, 1));
+    if constexpr (!kW1) mx2 = nan_max(mx2, __shfl_xor_sync(kFull, mx2, 1));
     const float bias = a.gate_b[0];
     bool ok = true;
     for (int i = 0; i < nb && ok; ++i) {
@@ -498,12 +505,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       float* szb = s_z + (i & 1) * Kp;
 #pragma unroll
       for (int u = 0; u < ZPT; ++u)
-        if (tid + u * kWeightThreads < C) szb[tid + u * kWeightThreads] = zr[u];
-      role_sync(kBarWeights, kWeightThreads);
+        if (tid + u * WT < C) szb[tid + u * WT] = zr[u];
+      role_sync(kBarWeights, WT);
       if (i + 1 < nb) {
 #pragma unroll
         for (int u = 0; u < ZPT; ++u) {
-          const int c = tid + u * kWeightThreads;
+          const int c = tid + u * WT;
           if (c < C) zr[u] = a.z[(size_t)(b + 1) * C + c];
         }
       }
@@ -511,7 +518,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
 #pragma unroll
       for (int jj = 0; jj < KH; ++jj)
         if (part * KH + jj < k && has_row) gp += (kGwReg ? gwr[jj] : s_gw[part * KH + jj]) * szb[chp[jj] >> 17];
-      const float g = bias + gp + __shfl_xor_sync(kFull, gp, 1);
+      const float g = bias + gp + (kW1 ? 0.0f : __shfl_xor_sync(kFull, gp, 1));
       const float t = temperature(g, a.tmin_tau, a.trange_tau, nullptr);
       if (a.T_out && has_row && part == 0) a.T_out[(size_t)b * E_r + e] = t;
       const float it = 1.0f / t;
@@ -524,13 +531,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         if constexpr (kKeepW) wv[jj] = ev;
         zp += ev;
       }
-      const float iz = 1.0f / (zp + __shfl_xor_sync(kFull, zp, 1));
+      const float iz = 1.0f / (zp + (kW1 ? 0.0f : __shfl_xor_sync(kFull, zp, 1)));
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         // the previous sample's MMAs have released this half of A
         bool w_ok = true;
         if (i >= 1 && tid == 0) w_ok = mbar_wait_abort(&bars->a_free[h], (i - 1) & 1, abort);
-        if (i >= 1) w_ok = role_sync_and(kBarWeights, kWeightThreads, w_ok);
+        if (i >= 1) w_ok = role_sync_and(kBarWeights, WT, w_ok);
         if (!w_ok) {
           ok = false;
           break;
@@ -551,9 +558,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         mbar_arrive(&bars->a_full[h]);
       }
     }
-  } else if (tid < kWeightThreads + kDrainThreads) {
-    // ===================== drain (warps 8-11): TMEM lane quarter = warp % 4
-    const int dt = tid - kWeightThreads;                      // row within the tile
+  } else if (tid < WT + DT) {
+    // ===================== drain (warps 8-11; kW1: 4-11): TMEM lane quarter = warp % 4
+    const int dt = (warp & 3) * 32 + lane;                    // row within the tile
+    const int dhalf = kW1 ? (warp - 4) >> 2 : 0;              // kW1: which half of the tile's chunks
+    const bool dlead = tid == WT;                             // waits for the accumulator
     const bool has_row = dt < rows;
     // output epilogue of this thread's row (expert e0 + dt)
     constexpr bool hep = kEp;
@@ -562,7 +571,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     const int erelu = a.ep.relu;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     T* yg = static_cast<T*>(a.y);
-    const int drain = kGen ? a.drain : (int)kDrainOneTile;
+    const int drain = kW1 ? (int)kDrainRows : kGen ? a.drain : (int)kDrainOneTile;
     if (drain == kDrainOneTile) {
       // One pixel tile per sample: the tile's rows are one contiguous range of
       // Y, staged in shared memory at a pitch of H*W elements with 16-bit
@@ -572,9 +581,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       for (int u = 0; u < nu; ++u) {
         const int s = u & 1;
         bool ok = true;
-        if (dt == 0) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
+        if (dlead) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
         if (dt == 0) bulk_wait_read();                        // the previous sample's copy left the block
-        if (!role_sync_and(kBarDrain, kDrainThreads, ok)) break;
+        if (!role_sync_and(kBarDrain, DT, ok)) break;
         tc_fence_after();
         const uint32_t tb = tmem + lane_base + (uint32_t)(s * P * NP);
 #pragma unroll
@@ -601,14 +610,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         tc_fence_before();
         mbar_arrive(&bars->d_empty[s]);
         proxy_fence_smem();
-        role_sync(kBarDrain, kDrainThreads);
+        role_sync(kBarDrain, DT);
         T* dst = yg + ((size_t)(b0 + u) * E + e0) * HW;
         const uint32_t nbytes = (uint32_t)(rows * HW * sizeof(T));
         if (((((uintptr_t)dst) | nbytes) & 15) == 0) {
           if (dt == 0) bulk_s2g(dst, smem_u32(stg), nbytes);
         } else {
-          for (int q = dt; q < rows * HW; q += kDrainThreads) dst[q] = stg[q];
-          role_sync(kBarDrain, kDrainThreads);
+          for (int q = dt; q < rows * HW; q += DT) dst[q] = stg[q];
+          role_sync(kBarDrain, DT);
         }
       }
     } else if (drain == kDrainRows) {
@@ -625,11 +634,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         const int p0 = t * NP, tp = min(NP, HW - p0);       // a multiple of 8
         unsigned char* row = row0 + (size_t)(u % a.nsb) * 128u * pitch;
         bool ok = true;
-        if (dt == 0) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
+        if (dlead) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
         // this thread's copy out of this buffer, nsb units ago, has read it
         if (a.nsb == 2) bulk_wait_read_all_but1();
         else bulk_wait_read();
-        if (!role_sync_and(kBarDrain, kDrainThreads, ok)) break;
+        if (!role_sync_and(kBarDrain, DT, ok)) break;
         tc_fence_after();
         const uint32_t tb = tmem + lane_base + (uint32_t)(s * P * NP);
         // 32 columns (two partials when P == 2) into the staging row
@@ -651,24 +660,35 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
                                pack2_16<T>(v[8 * g + 4], v[8 * g + 5]), pack2_16<T>(v[8 * g + 6], v[8 * g + 7]));
           }
         };
-        if (P == 1) {
+        // this thread's columns: the whole tile, or (kW1) one half of its
+        // 32-column chunks (the halves start on 32-column boundaries)
+        int c_lo = 0, c_hi = tp;
+        if constexpr (kW1) {
+          const int mid = min(tp, ((tp + 31) / 32 + 1) / 2 * 32);
+          c_lo = dhalf ? mid : 0;
+          c_hi = dhalf ? tp : mid;
+        }
+        if (c_lo >= c_hi) {                                   // nothing to read (uniform across the warp)
+          tc_fence_before();
+          mbar_arrive(&bars->d_empty[s]);
+        } else if (P == 1) {
           // one accumulator: two 32-column chunks in flight (r0 / r1), so
           // each load's latency overlaps the conversion and stores of the
           // chunk before it; the buffer is released after its last load
           uint32_t r0[32], r1[32];
-          tmem_ld32_nowait(tb, r0);
+          tmem_ld32_nowait(tb + c_lo, r0);
           tmem_wait_ld();
-          for (int cb = 0; cb < tp; cb += 64) {               // uniform across the warp
-            if (cb + 32 < tp) {
+          for (int cb = c_lo; cb < c_hi; cb += 64) {          // uniform across the warp
+            if (cb + 32 < c_hi) {
               tmem_ld32_nowait(tb + cb + 32, r1);
             } else {
               tc_fence_before();
               mbar_arrive(&bars->d_empty[s]);
             }
             put(r0, r0, cb);
-            if (cb + 32 >= tp) break;
+            if (cb + 32 >= c_hi) break;
             tmem_wait_ld();
-            if (cb + 64 < tp) {
+            if (cb + 64 < c_hi) {
               tmem_ld32_nowait(tb + cb + 64, r0);
             } else {
               tc_fence_before();
@@ -678,21 +698,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
             tmem_wait_ld();
           }
         } else {
-          for (int cb = 0; cb < tp; cb += 32) {               // uniform across the warp
+          for (int cb = c_lo; cb < c_hi; cb += 32) {          // uniform across the warp
             uint32_t r0[32], r1[32];
             tmem_ld32_nowait(tb + cb, r0);
             tmem_ld32_nowait(tb + NP + cb, r1);
             tmem_wait_ld();
-            if (cb + 32 >= tp) {                              // last read of the buffer
+            if (cb + 32 >= c_hi) {                            // last read of the buffer
               tc_fence_before();
               mbar_arrive(&bars->d_empty[s]);
             }
             put(r0, r1, cb);
           }
         }
-        if (has_row) {
+        if (has_row && c_hi > c_lo) {
           proxy_fence_smem();
-          bulk_s2g(yg + ((size_t)(b0 + i) * E + e0 + dt) * HW + p0, smem_u32(row), (uint32_t)tp * (uint32_t)sizeof(T));
+          bulk_s2g(yg + ((size_t)(b0 + i) * E + e0 + dt) * HW + p0 + c_lo, smem_u32(row + (size_t)c_lo * 2),
+                   (uint32_t)(c_hi - c_lo) * (uint32_t)sizeof(T));
         }
       }
     } else if (drain == kDrainDirect) {
@@ -702,8 +723,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         const int s = u & 1, i = u / NT, t = u - (u / NT) * NT;
         const int p0 = t * NP, tp = min(NP, HW - p0);
         bool ok = true;
-        if (dt == 0) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
-        if (!role_sync_and(kBarDrain, kDrainThreads, ok)) break;
+        if (dlead) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
+        if (!role_sync_and(kBarDrain, DT, ok)) break;
         tc_fence_after();
         const uint32_t tb = tmem + lane_base + (uint32_t)(s * P * NP);
         T* dst = yg + ((size_t)(b0 + i) * E + e0 + dt) * HW + p0;
@@ -750,9 +771,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         const int s = u & 1, i = u / NT, t = u - (u / NT) * NT;
         const int p0 = t * NP, tp = min(NP, HW - p0);         // this tile's pixels
         bool ok = true;
-        if (dt == 0) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
+        if (dlead) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
         bulk_wait_read();                                     // this thread's copy left the staging area
-        if (!role_sync_and(kBarDrain, kDrainThreads, ok)) break;
+        if (!role_sync_and(kBarDrain, DT, ok)) break;
         tc_fence_after();
         const uint32_t tb = tmem + lane_base + (uint32_t)(s * P * NP);
         for (int cb = 0; cb < tp; cb += 32) {                 // uniform across the warp
@@ -1003,9 +1024,14 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
       const bool gen = !(sh.NP == 64 && sh.NA == 1 && sh.P == 2 && sh.NT == 1 && sh.drain == kDrainOneTile);
       const bool epi = ep.scale != nullptr;
 #define MOCE_TC_KMAX(G, EP)                                                                         \
-  (KMAX == 16 ? mix_tc_kernel<T, 16, G, EP> : KMAX == 32 ? mix_tc_kernel<T, 32, G, EP> : mix_tc_kernel<T, 64, G, EP>)
-      void (*kern)(TcArgs) = gen ? (epi ? MOCE_TC_KMAX(true, true) : MOCE_TC_KMAX(true, false))
-                                 : (epi ? MOCE_TC_KMAX(false, true) : MOCE_TC_KMAX(false, false));
+  (KMAX == 16 ? mix_tc_kernel<T, 16, G, EP, false>                                                 \
+              : KMAX == 32 ? mix_tc_kernel<T, 32, G, EP, false> : mix_tc_kernel<T, 64, G, EP, false>)
+      // pixel-tiled maps with padded staging rows and k <= 16: one weight
+      // thread per row and eight drain warps
+      const bool w1 = gen && sh.drain == kDrainRows && KMAX == 16;
+      void (*kern)(TcArgs) = w1 ? (epi ? mix_tc_kernel<T, 16, true, true, true> : mix_tc_kernel<T, 16, true, false, true>)
+                             : gen ? (epi ? MOCE_TC_KMAX(true, true) : MOCE_TC_KMAX(true, false))
+                                   : (epi ? MOCE_TC_KMAX(false, true) : MOCE_TC_KMAX(false, false));
 #undef MOCE_TC_KMAX
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return set_error(MOCE_ERR_CUDA, "moce_mix_tc: cannot reserve %zu B shared memory", smem);
