@@ -177,6 +177,102 @@ __global__ void __launch_bounds__(px_threads(NSLAB), 1) mix_px_kernel(PxArgs a) 
   if constexpr (CL > 1) cooperative_groups::this_cluster().sync();
 }
 
+// Maps of at most 64 pixels (7x7): a warp mixes two experts at once, one per
+// half-warp (16 lanes x 4 pixels), so 26 of 32 lanes carry pixels at 7x7
+// instead of 13.  Lane i of a half holds supports i, i + 16, ... (KL16 of
+// them, k <= 16 KL16); the gate, temperature and softmax reduce over the 16
+// lanes of the half, and each support's channel and weight reach the half by
+// a width-16 shuffle.  X_b in one CTA's shared memory, as mix_px_kernel.
+template <typename T, int KL16>
+__global__ void __launch_bounds__(px_threads(1), 1) mix_px_half_kernel(PxArgs a) {
+  constexpr int kPxThreads = px_threads(1), kPxWarps = kPxThreads / 32;
+  extern __shared__ __align__(16) unsigned char s_raw[];
+  const int C = a.C, HW = a.HW, HWp = a.HWp, k = a.k, E_r = a.E_r;
+  T* s_x = reinterpret_cast<T*>(s_raw);                                                // C x HWp
+  float* s_z = reinterpret_cast<float*>(s_raw + (((size_t)C * HWp * sizeof(T) + 15) & ~size_t(15)));  // C
+  float* s_gw = s_z + C;                                                               // k
+  const int b = blockIdx.y, ch = blockIdx.x, nch = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hl = lane & 15, hsel = lane >> 4;
+  const T* xg = static_cast<const T*>(a.x);
+  px_stage_rows<T>(s_x, xg + (size_t)b * C * HW, C, HW, HWp);
+  for (int c = threadIdx.x; c < C; c += kPxThreads) s_z[c] = a.z[(size_t)b * C + c];
+  for (int i = threadIdx.x; i < k; i += kPxThreads) s_gw[i] = a.gate_w[i];
+  __syncthreads();
+  const float bias = a.gate_b[0];
+  const int per = (E_r + nch - 1) / nch;
+  const int e0 = ch * per, e1 = min(E_r, e0 + per);
+  const int E = E_r + 1;
+  T* yg = static_cast<T*>(a.y);
+  for (int eb = e0 + 2 * warp; eb < e1; eb += 2 * kPxWarps) {       // uniform across the warp
+    const int e = eb + hsel;
+    const bool ve = e < e1;                                         // uniform across the half
+    int c_l[KL16];
+    float u_l[KL16];
+#pragma unroll
+    for (int q = 0; q < KL16; ++q) {
+      const int i = hl + 16 * q;
+      const bool v = ve && i < k;
+      c_l[q] = v ? a.idx[(size_t)e * k + i] : 0;
+      u_l[q] = v ? a.ln[(size_t)e * k + i] : -INFINITY;
+    }
+    float gp = 0.0f;
+#pragma unroll
+    for (int q = 0; q < KL16; ++q)
+      if (hl + 16 * q < k) gp += s_gw[hl + 16 * q] * s_z[c_l[q]];
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) gp += __shfl_xor_sync(kFull, gp, o);
+    const float g = gp + bias;
+    const float t = temperature(g, a.tmin_tau, a.trange_tau, nullptr);
+    if (a.T_out && ve && hl == 0) a.T_out[(size_t)b * E_r + e] = t;
+    float m = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < KL16; ++q) {
+      if (hl + 16 * q < k) u_l[q] = u_l[q] / t;
+      m = nan_max(m, u_l[q]);
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) m = nan_max(m, __shfl_xor_sync(kFull, m, o));
+    float a_l[KL16], sum = 0.0f;
+#pragma unroll
+    for (int q = 0; q < KL16; ++q) {
+      a_l[q] = (hl + 16 * q < k) ? expf(u_l[q] - m) : 0.0f;
+      sum += a_l[q];
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(kFull, sum, o);
+#pragma unroll
+    for (int q = 0; q < KL16; ++q) a_l[q] /= sum;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const int p = 4 * hl;
+#pragma unroll
+    for (int q = 0; q < KL16; ++q) {
+      const int nq = min(16, k - 16 * q);
+#pragma unroll 4
+      for (int j = 0; j < nq; ++j) {
+        const int c = __shfl_sync(kFull, c_l[q], j, 16);
+        const float w = __shfl_sync(kFull, a_l[q], j, 16);
+        if (p < HW) {
+          float f[4];
+          ld4<T>(s_x + (size_t)c * HWp + p, f);
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) acc[jj] = fmaf(w, f[jj], acc[jj]);
+        }
+      }
+    }
+    if (ve) {
+      T* yr = yg + ((size_t)b * E + e) * HW;
+      if (p + 3 < HW && a.vec_out) {
+        st4<T>(yr + p, acc);
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj)
+          if (p + jj < HW) yr[p + jj] = from_f<T>(acc[jj]);
+      }
+    }
+  }
+}
+
 // k <= 32: the weights of 32 experts are computed at once with lanes over
 // experts (each lane runs its expert's gate, temperature and softmax alone,
 // no warp reductions), then the warp walks those experts with lanes over
@@ -470,7 +566,12 @@ extern "C" int moce_mix_px(const void* x, int dtype, int64_t B, int64_t C, int64
   case NS:                                                                                        \
     kern = grouped ? mix_px_grouped_kernel<T, NS, 16> : CL == 2 ? MOCE_PX_KL(NS, 2) : MOCE_PX_KL(NS, 1); \
     break;
-    switch (nslab) {
+    // maps of at most 64 pixels: two experts per warp (half-warps)
+    const bool half = CL == 1 && HW <= 64 && !grouped;
+    if (half)
+      kern = k <= 16 ? mix_px_half_kernel<T, 1> : k <= 32 ? mix_px_half_kernel<T, 2>
+             : k <= 64 ? mix_px_half_kernel<T, 4> : mix_px_half_kernel<T, 8>;
+    else switch (nslab) {
       MOCE_PX_PICK(1)
       MOCE_PX_PICK(2)
       MOCE_PX_PICK(3)
