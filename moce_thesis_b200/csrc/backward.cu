@@ -357,8 +357,9 @@ __global__ void __launch_bounds__(kPxThreadsB, 1) bwd_px_route_kernel(
 // in shared memory (dY read from HBM once); warp per input channel, lane per
 // pixel, the channel's transposed list gathered in list order as in
 // bwd_dx_kernel.
+constexpr int kDxThreads = 1024;          // 32 warps (56 registers a thread): more channel rows in flight
 template <typename T>
-__global__ void __launch_bounds__(kPxThreadsB, 1) bwd_px_dx_kernel(
+__global__ void __launch_bounds__(kDxThreads, 1) bwd_px_dx_kernel(
     const T* __restrict__ dy, int C, int HW, int E_r, int k, const int32_t* __restrict__ mask,
     const int32_t* __restrict__ meta, const int32_t* __restrict__ toff, const int32_t* __restrict__ tslot,
     const float* __restrict__ gate_w, BwdWs ws, T* __restrict__ dx) {
@@ -368,7 +369,7 @@ __global__ void __launch_bounds__(kPxThreadsB, 1) bwd_px_dx_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = E_r + 1;
   const T* dyb = dy + (size_t)b * E * HW;
-  for (int q = threadIdx.x; q < E * 32; q += kPxThreadsB) {
+  for (int q = threadIdx.x; q < E * 32; q += kDxThreads) {
     const int p = p0 + (q & 31);
     s_dy[q] = (p < HW) ? to_f(dyb[(size_t)(q >> 5) * HW + p]) : 0.0f;
   }
@@ -406,7 +407,7 @@ __global__ void __launch_bounds__(kPxThreadsB, 1) bwd_px_dx_kernel(
     // advance to the next chunk and prefetch it
     int c2 = c, sc2 = sc + 32;
     if (sc2 >= s1) {
-      c2 = c + kPxWarpsB;
+      c2 = c + (kDxThreads / 32);
       sc2 = (c2 < C) ? toff[c2] : 0;
     }
     if (c2 < C) fetch(c2, sc2, e_n, a_n, g_n);
@@ -606,7 +607,7 @@ extern "C" int moce_backward(const void* x, const void* dy, int dtype, int64_t B
       if (cudaFuncSetAttribute(bwd_px_dx_kernel<Tt>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_dx) !=
           cudaSuccess)
         return set_error(MOCE_ERR_CUDA, "moce_backward: dx smem %zu", smem_dx);
-      bwd_px_dx_kernel<Tt><<<dim3((unsigned)((HW + 31) / 32), (unsigned)B), kPxThreadsB, smem_dx, st>>>(
+      bwd_px_dx_kernel<Tt><<<dim3((unsigned)((HW + 31) / 32), (unsigned)B), kDxThreads, smem_dx, st>>>(
           static_cast<const Tt*>(dy), (int)C, (int)HW, (int)E_r, (int)k, mask, meta, toff, tslot, gate_w, ws,
           static_cast<Tt*>(dx));
     } else {
