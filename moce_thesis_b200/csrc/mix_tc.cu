@@ -571,7 +571,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     const int erelu = a.ep.relu;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     T* yg = static_cast<T*>(a.y);
-    const int drain = kW1 ? (int)kDrainRows : kGen ? a.drain : (int)kDrainOneTile;
+    const int drain = kGen ? a.drain : (int)kDrainOneTile;  // kW1: one tile or padded rows (host)
     if (drain == kDrainOneTile) {
       // One pixel tile per sample: the tile's rows are one contiguous range of
       // Y, staged in shared memory at a pitch of H*W elements with 16-bit
@@ -582,13 +582,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         const int s = u & 1;
         bool ok = true;
         if (dlead) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
-        if (dt == 0) bulk_wait_read();                        // the previous sample's copy left the block
+        if (dlead) bulk_wait_read();                          // the previous sample's copy left the block
         if (!role_sync_and(kBarDrain, DT, ok)) break;
         tc_fence_after();
         const uint32_t tb = tmem + lane_base + (uint32_t)(s * P * NP);
+        // this thread's columns: the whole row, or (kW1) one half of its
+        // 32-column chunks
+        int c_lo = 0, c_hi = HW;
+        if constexpr (kW1) {
+          const int mid = min(HW, ((HW + 31) / 32 + 1) / 2 * 32);
+          c_lo = dhalf ? mid : 0;
+          c_hi = dhalf ? HW : mid;
+        }
 #pragma unroll
         for (int cb = 0; cb < (kGen ? kTcMaxN : 64); cb += 32) {
-          if (cb >= HW) break;                                // uniform across the warp
+          if (cb >= c_hi) break;                              // uniform across the warp
+          if (cb < c_lo) continue;
           uint32_t r0[32], r1[32];
           tmem_ld32_nowait(tb + cb, r0);
           if (P == 2) tmem_ld32_nowait(tb + NP + cb, r1);
@@ -614,9 +623,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         T* dst = yg + ((size_t)(b0 + u) * E + e0) * HW;
         const uint32_t nbytes = (uint32_t)(rows * HW * sizeof(T));
         if (((((uintptr_t)dst) | nbytes) & 15) == 0) {
-          if (dt == 0) bulk_s2g(dst, smem_u32(stg), nbytes);
+          if (dlead) bulk_s2g(dst, smem_u32(stg), nbytes);
         } else {
-          for (int q = dt; q < rows * HW; q += DT) dst[q] = stg[q];
+          for (int q = tid - WT; q < rows * HW; q += DT) dst[q] = stg[q];
           role_sync(kBarDrain, DT);
         }
       }
@@ -1027,7 +1036,9 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
   (KMAX == 16 ? mix_tc_kernel<T, 16, G, EP, false>                                                 \
               : KMAX == 32 ? mix_tc_kernel<T, 32, G, EP, false> : mix_tc_kernel<T, 64, G, EP, false>)
       // pixel-tiled maps with padded staging rows and k <= 16: one weight
-      // thread per row and eight drain warps
+      // thread per row and eight drain warps (with one tile per sample the
+      // weights are rewritten every unit and the split measured slower:
+      // 74.7 against 68.6 us at 14x14)
       const bool w1 = gen && sh.drain == kDrainRows && KMAX == 16;
       void (*kern)(TcArgs) = w1 ? (epi ? mix_tc_kernel<T, 16, true, true, true> : mix_tc_kernel<T, 16, true, false, true>)
                              : gen ? (epi ? MOCE_TC_KMAX(true, true) : MOCE_TC_KMAX(true, false))
