@@ -71,9 +71,13 @@ def test_allreduce_averages_across_two_ranks():
 def _failing_worker(rank, world, port, q):
     from datetime import timedelta
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=3))
+    # rendezvous with room for slow process start-up (a cold container pages
+    # torch in for tens of seconds); the step that fails runs in a group
+    # whose collectives time out after 3 s
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    short = dist.new_group(list(range(world)), timeout=timedelta(seconds=3))
     t = torch.ones(4)
-    dist.all_reduce(t)               # one completed step: connections are up
+    dist.all_reduce(t, group=short)  # one completed step: connections are up
     if rank == 1:
         # leaves between steps, before its collective: the host-side failure
         q.put((rank, "left"))
@@ -82,7 +86,7 @@ def _failing_worker(rank, world, port, q):
         os._exit(0)
     try:
         t = torch.ones(4)
-        dist.all_reduce(t)
+        dist.all_reduce(t, group=short)
         q.put((rank, "completed"))
     except Exception as exc:  # the peer never joins: the collective must error out
         q.put((rank, "error:" + type(exc).__name__))
