@@ -29,7 +29,8 @@ def _worker(rank, world, port, q):
     from moce_thesis_b200 import MoCE
     from moce_thesis_b200.dist import allreduce_moce_grads
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
+    # generous: on a cold container a spawned rank may take tens of seconds to import torch
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
     torch.manual_seed(0)
     net = torch.nn.Sequential(MoCE(in_channels=16, sampling_factor=2, k=4), MoCE(in_channels=8, sampling_factor=2, k=2))
     for i, p in enumerate(net.parameters()):

@@ -220,3 +220,32 @@ def test_resnet_inference_paths_agree():
         fused = m(x).float()
     scale = ref.abs().max().item()
     assert (fused - ref).abs().max().item() <= 5e-2 * scale
+
+
+def test_resnet_forward_replays_as_cuda_graph():
+    """The eval forward of ResNet-50 + MoCE (tensor-core, lanes-over-pixels
+    and CTA-pair kernels, the fused epilogue) captured once as a CUDA graph
+    and replayed gives the eager output bit for bit."""
+    from moce_thesis_b200 import resnet
+    torch.manual_seed(0)
+    kcfg = [[4, 16, 16], [16, 32, 32, 32], [32, 64, 64, 64, 64, 64], [64, 128, 128]]
+    m = resnet.resnet50_moce_projection(dataset="imagenet", num_classes=1000, k=kcfg).to(DEV, torch.bfloat16).eval()
+    resnet.build_moce_cache(m)
+    x = torch.randn(4, 3, 224, 224, generator=torch.Generator().manual_seed(2)).to(DEV, torch.bfloat16)
+    with torch.no_grad():
+        want = m(x).clone()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            m(x)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            out = m(x)
+        for _ in range(2):
+            g.replay()
+        torch.cuda.synchronize()
+        got = out.clone()
+        del g
+    assert torch.equal(got, want)
