@@ -48,6 +48,8 @@ def relerr(a, b):
     (2, 512, 28, 28, 130, 32, torch.bfloat16),  # 28x28 at C=512: 64-pixel tiles (a 208-pixel ring slot would not fit)
     (2, 64, 24, 24, 20, 8, torch.bfloat16),     # HW == 576 in 8-pixel rows with uncovered channels (residual block)
     (3, 72, 4, 4, 100, 8, torch.float16),       # HW == 16, 16-byte staging stores of one tile
+    (59, 512, 7, 7, 601, 32, torch.bfloat16),   # 5 expert tiles (the last of 88 rows), samples split 29 ways
+    (59, 192, 6, 6, 601, 16, torch.float16),    # the same through the general one-tile kernel (N = 48)
 ])
 def test_tc_mix_matches_oracle(B, C, H_, W_, E, k, dtype):
     gen = torch.Generator().manual_seed(B * 100 + C + k)
@@ -150,19 +152,19 @@ def test_tc_unaligned_buffers(C, Hh, E, k):
     assert close(got, ref, 1e-2, 1e-3), relerr(got, ref)
 
 
-@pytest.mark.parametrize("C,Hh,E,k,relu", [
-    (512, 7, 300, 32, True),     # 7x7 one tile, two partial accumulators
-    (256, 14, 140, 16, True),    # 14x14 one tile, one accumulator
-    (128, 28, 90, 16, False),    # 28x28 pixel tiles through padded staging rows, no ReLU
-    (96, 12, 4, 8, True),        # uncovered channels: the residual row goes through the epilogue too
+@pytest.mark.parametrize("C,Hh,E,k,relu,B", [
+    (512, 7, 300, 32, True, 3),     # 7x7 one tile, two partial accumulators
+    (256, 14, 140, 16, True, 3),    # 14x14 one tile, one accumulator
+    (128, 28, 90, 16, False, 3),    # 28x28 pixel tiles through padded staging rows, no ReLU
+    (96, 12, 4, 8, True, 3),        # uncovered channels: the residual row goes through the epilogue too
+    (512, 7, 601, 32, True, 59),    # 5 expert tiles, the last of 88 rows, 2-3 samples per block
 ])
-def test_forward_tc_ep_matches_bn_relu(C, Hh, E, k, relu):
+def test_forward_tc_ep_matches_bn_relu(C, Hh, E, k, relu, B):
     """moce_forward_tc_ep (BatchNorm folded to scale / shift and ReLU applied
     in the output store) against forward_tc followed by torch's eval
     BatchNorm and ReLU on the same inputs (bf16 tolerance)."""
     from moce_thesis_b200 import capi
     gen = torch.Generator().manual_seed(C + k)
-    B = 3
     x = torch.randn(B, C, Hh, Hh, generator=gen).abs().to(DEV, torch.bfloat16)
     L = torch.randn(E - 1, C, generator=gen).to(DEV)
     gw = (torch.rand(1, k, generator=gen) - 0.5).to(DEV)
