@@ -13,7 +13,15 @@ per second, whole job; also reported as % of 8 TB/s.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--dtype bf16|fp32]
     python bench.py --impl reference ...   # the CPU oracle port, host cores
 
-Two further workloads print their own JSON lines (not the headline):
+The default line also carries, measured in the same run at the same GPU
+count: "fp32" (the same layer in fp32, the reference's own precision),
+"resnet50" (ResNet-50 + MoCE inference img/s, global batch 1024 split over
+the GPUs, strong scaling) and "train" (the training step below, with the NCCL
+all-reduce of the L and gate gradients when N > 1); --no-extra skips them.
+"cpu_baseline" is the oracle port of the reference layer on every host core
+(rank 0, one GPU only).
+
+Further workloads print their own JSON lines (not the headline):
 
     python bench.py --workload train   # fp32 training step of one layer:
         N=512/GPU, C_in=256, 14x14, E=1024, k=16, forward + aux loss +
@@ -280,11 +288,12 @@ def run_ours(args):
     reps = max(args.steps, 20)
     gate_ms = graph_time(pass1, reps)
     mix_ms = graph_time(pass2, reps)
-    from moce_thesis_b200 import capi
-    # algorithmic bytes of pass 2: its X operand in, routed Y out, z in,
-    # supports (int32) and normalised logits (fp32)
-    x_in = capi.lib().moce_tc_stage_bytes(B, C, H * W) if use_tc else xb
-    mix_bytes = x_in + B * (E - 1) * H * W * esize + B * C * 4 + (E - 1) * K * 8
+    # algorithmic bytes of pass 2: X in (unpadded, once), routed Y out, z in,
+    # supports (int32) and normalised logits (fp32); the staged copy pass 1
+    # writes for the tensor cores is padding and layout, not algorithmic bytes
+    mix_bytes = xb + B * (E - 1) * H * W * esize + B * C * 4 + (E - 1) * K * 8
+    from moce_thesis_b200 import check_faults
+    check_faults()          # a bounded wait that ran out fails the record
 
     # end to end through the public API: pinned host X -> layer -> host Y
     # (MoCE.forward_host: host-to-device copies, both passes and
@@ -344,8 +353,20 @@ def run_ours(args):
         "gpu_launches": 2 * args.steps,
         "clocks": clk.summary(),
     }
+    check_faults()
+    del xs, ys, zs, x0, xh, yh, layer, r, pass1, pass2, step
+    torch.cuda.empty_cache()
+    if not args.no_extra:
+        # the same layer in the reference's precision, the ResNet-50 + MoCE
+        # img/s half of the metric, and the training step with its
+        # all-reduce: each at this run's GPU count
+        if args.dtype != "fp32":
+            out["fp32"] = layer_fp32(args, world, dev)
+        out["resnet50"] = resnet_measure(args, world, rank, local, dev, steps=min(args.steps, 10))
+        out["train"] = train_measure(args, world, rank, local, dev, steps=min(args.steps, 10))
+        check_faults()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_baseline(args.dtype, Xcpu, L.cpu(), gw.cpu(), gb.cpu())
+        out["cpu_baseline"] = cpu_baseline_pool(args.dtype, seconds=12.0)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -353,23 +374,100 @@ def run_ours(args):
         print(json.dumps(out), flush=True)
 
 
-def cpu_baseline(dtype, X, L, gw, gb, sample=8):
-    """The numpy oracle on a bounded sample of the workload (host cores)."""
-    import numpy as np
-    from oracle import moce_oracle as O
+def layer_fp32(args, world, dev):
+    """The stage-4 layer in fp32 (the reference's own precision): device time
+    of both passes over rotating input sets, max over ranks."""
+    import torch
+    from moce_thesis_b200 import MoCE, native
+    mc = native()
+    x0, L, gw, gb, _ = make_inputs(dev, torch.float32, seed=1100 + int(os.environ.get("RANK", "0")))
+    layer = MoCE(in_channels=C, sampling_factor=1, k=K, temp_min=TMIN, temp_max=TMAX).to(dev)
+    layer.num_experts = E
+    layer.routing_logits = torch.nn.Parameter(L.clone())
+    with torch.no_grad():
+        layer.gate.weight.copy_(gw)
+        layer.gate.bias.copy_(gb)
+    layer.eval()
+    layer.build_eval_cache()
+    r = layer._route
+    gwf = layer.cached_gate_weight.detach().reshape(-1).float().contiguous()
+    gbf = layer.cached_gate_bias.detach().reshape(-1).float().contiguous()
+    tmin_tau, trange_tau = layer.cached_temp_min_tau, layer.cached_temp_range_tau
+    nbytes, xb, yb = algo_bytes(B, 4)
+    nsets = max(2, int(3 * L2_BYTES // (xb + yb)) + 1)
+    xs = [x0] + [(x0 * (1.0 + 0.001 * i)).contiguous() for i in range(1, nsets)]
+    ys = [torch.empty(B, E, H, W, device=dev, dtype=torch.float32) for _ in range(nsets)]
+    steps = min(args.steps, 20)
+
+    def step(i):
+        r.forward(xs[i % nsets], gwf, gbf, tmin_tau, trange_tau, False, ys[i % nsets])
+
+    ms = _timed_steps(step, args.warmup, steps, world, dev)
+    zs = [torch.empty(B, C, device=dev) for _ in range(nsets)]
+    p1, p2, names = pass_fns(mc, r, xs, ys, zs, nsets, B, C, H * W, E, K, gwf, gbf, tmin_tau, trange_tau, dev)
+    kms = {names[0]: round(graph_time(p1, 20), 5), names[1]: round(graph_time(p2, 20), 5)}
+    out = {"value": round(world * nbytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 5),
+           "steps": steps, "dtype": "fp32", "kernels_ms": kms,
+           "pct_of_8tbs": round(100.0 * nbytes / (ms * 1e-3) / 1e9 / NOMINAL_HBM_GBS, 2),
+           "config": f"{WORKLOAD}, fp32 in and out, {nsets} rotating X/Y sets"}
+    del xs, ys, zs, layer, r
+    torch.cuda.empty_cache()
+    return out
+
+
+def _timed_steps(step, warmup, steps, world, dev):
+    """ms per step: `warmup` untimed calls, then `steps` calls between two
+    events on the current stream, with a barrier and a synchronize on both
+    sides; max over ranks."""
+    import torch
+    import torch.distributed as dist
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(st)
+    for i in range(steps):
+        step(i)
+    e1.record(st)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    return _max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
+
+
+def cpu_baseline_pool(dtype, seconds=12.0, per_task=4):
+    """The numpy oracle port of the reference layer on every host core (a
+    spawn-started process pool, one BLAS thread per process, four images per
+    task), repeated over a bounded sample of the workload's images (one
+    task per core) for about `seconds`."""
+    import multiprocessing as mp
+    import torch
+    cores = os.cpu_count() or 1
+    _, L, gw, gb, X = make_inputs("cpu", torch.float32, seed=1000)
+    sample = max(per_task, min(B, per_task * cores))
+    jobs = [X[i:i + per_task].numpy() for i in range(0, sample, per_task)]
+    for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[var] = "1"
+    with mp.get_context("spawn").Pool(cores, initializer=_ref_init,
+                                      initargs=((L.numpy(), gw.numpy(), gb.numpy()),)) as pool:
+        pool.map(_ref_chunk, jobs)                      # warm-up: imports, first touch
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            pool.map(_ref_chunk, jobs)
+            reps += 1
+            if time.perf_counter() - t0 > seconds:
+                break
+        dt = (time.perf_counter() - t0) / reps
     esize = 2 if dtype == "bf16" else 4
-    Xs = X[:sample].numpy()
-    t0 = time.perf_counter()
-    reps = 0
-    while True:
-        O.forward(Xs, L.numpy(), gw.numpy(), gb.numpy(), K, TMIN, TMAX, TAU, mode="eval", dtype=np.float32)
-        reps += 1
-        if time.perf_counter() - t0 > 5.0:
-            break
-    dt = (time.perf_counter() - t0) / reps
     nb, _, _ = algo_bytes(sample, esize)
-    return {"value": round(nb / dt / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
-            "sample": f"{sample} of {B} images, {reps} forward(s), float32 numpy oracle, bytes counted at {dtype}",
+    return {"value": round(nb / dt / 1e9, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"{sample} of {B} images per pass, {reps} passes in {seconds:.0f} s, float32 numpy oracle "
+                      f"over {cores} processes ({per_task} images per task), bytes counted at {dtype}",
             "ms_per_sample_batch": round(dt * 1e3, 2)}
 
 
@@ -433,7 +531,45 @@ def run_reference(args):
                                    f"task over {cores} processes"},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if torch.cuda.is_available():
+        out["reference_gpu"] = reference_gpu_measure(args)
     print(json.dumps(out), flush=True)
+
+
+def reference_gpu_measure(args):
+    """The reference's own GPU path on this box: MoCE.forward_eval's ATen
+    steps (pool, gate, temperature, materialised softmax weights) and its
+    K2/K4 kernels, built unmodified from the reference sources for sm_100a
+    (oracle/build_ref.py), on the stage-4 workload in fp32 (the reference's
+    precision) and with bf16 in and out (the reference upcasts).  Device time
+    over rotating inputs larger than L2; same bytes as the headline."""
+    import torch
+    from oracle import build_ref, ref_gpu
+    if not os.path.exists(build_ref.TARGET):
+        return {"unavailable": "reference extension not built (oracle/build_ref.py)"}
+    mod = build_ref.load()
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    res = {"path": "MoCE.forward_eval (MoCE.py:204-230): ATen pool/gate/softmax + reference kernels K2/K4 "
+                   "(moce_kernel.cu:1079-1153), built from source for sm_100a with the reference's flags"}
+    for name, dtype, esize in (("fp32", torch.float32, 4), ("bf16", torch.bfloat16, 2)):
+        x0, L, gw, gb, _ = make_inputs(dev, dtype, seed=1000)
+        idx, ln, mask = ref_gpu.cache(L, K)
+        nbytes, xb, yb = algo_bytes(B, esize)
+        nsets = max(2, int(3 * L2_BYTES // (xb + yb)) + 1)
+        xs = [x0] + [(x0 * (1.0 + 0.001 * i)).contiguous() for i in range(1, nsets)]
+        steps = min(args.steps, 20)
+
+        def step(i):
+            ref_gpu.forward_eval(mod, xs[i % nsets], idx, ln, gw, gb, mask, TMIN, TMAX, TAU)
+
+        with torch.no_grad():
+            ms = _timed_steps(step, args.warmup, steps, 1, dev)
+        res[name] = {"value": round(nbytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
+                     "steps": steps}
+        del xs
+        torch.cuda.empty_cache()
+    return res
 
 
 def _dist_setup():
@@ -460,11 +596,12 @@ def _max_over_ranks(ms, world, dev):
     return ms
 
 
-def run_train(args):
-    """fp32 training step of one MoCE layer (ResNet-101 stage-3 shape)."""
+def train_measure(args, world, rank, local, dev, steps):
+    """fp32 training step of one MoCE layer (ResNet-101 stage-3 shape):
+    forward, auxiliary loss, backward (dX, dL, dgate) and, with more than one
+    rank, the NCCL all-reduce of the L and gate gradients.  Returns the
+    measurement as a dict (ms per step is the max over ranks)."""
     import torch
-    import torch.distributed as dist
-    world, rank, local, dev = _dist_setup()
     from moce_thesis_b200 import MoCE
     from moce_thesis_b200.dist import allreduce_moce_grads
     Bt, Ct, Ht, Wt, Et, Kt = 512, 256, 14, 14, 1024, 16
@@ -479,7 +616,7 @@ def run_train(args):
     x.requires_grad_(True)
     one = torch.ones((), device=dev)
 
-    def step():
+    def step(_i):
         for prm in layer.parameters():
             prm.grad = None
         x.grad = None
@@ -488,32 +625,29 @@ def run_train(args):
         if world > 1:
             allreduce_moce_grads(layer)
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    st = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0.record(st)
-        for _ in range(args.steps):
-            step()
-        e1.record(st)
-        torch.cuda.synchronize()
-    ms = _max_over_ranks(e0.elapsed_time(e1), world, dev) / args.steps
+        ms = _timed_steps(step, args.warmup, steps, world, dev)
     xb, yb = Bt * Ct * Ht * Wt * 4, Bt * Et * Ht * Wt * 4
     nbytes = (xb + yb) + (yb + xb + xb)          # forward X+Y, backward dY+X+dX
     out = {"metric": "MoCE training step HBM GB/s", "value": round(world * nbytes / (ms * 1e-3) / 1e9, 2),
-           "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+           "unit": "GB/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
            "dtype": "fp32", "data": "synthetic (seeded half-normal X, N(0,1) dY and logits)",
            "config": {"workload": "MoCE layer training step: N=512/GPU C=256 14x14 E=1024 k=16, fwd + aux + bwd",
                       "global_batch": Bt * world,
-                      "parallelism": f"batch-sharded x{world}, L/gate grads all-reduced (NCCL)" if world > 1
-                      else "single GPU"},
+                      "parallelism": f"batch-sharded x{world}, L/gate grads all-reduced (NCCL) every step"
+                      if world > 1 else "single GPU"},
            "clocks": clk.summary()}
+    del x, dy, layer
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_train(args):
+    """fp32 training step of one MoCE layer; prints its own JSON line."""
+    import torch.distributed as dist
+    world, rank, local, dev = _dist_setup()
+    out = train_measure(args, world, rank, local, dev, args.steps)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -592,21 +726,20 @@ def run_sweep(args):
         dist.destroy_process_group()
 
 
-def run_resnet(args):
+def resnet_measure(args, world, rank, local, dev, steps, global_batch=1024, eager=True, unfused=True):
     """End-to-end ResNet-50 + MoCE inference, bf16, random Kaiming init, every
-    bottleneck entrance a MoCE layer with k = C_in / 16, global batch 1024 of
+    bottleneck entrance a MoCE layer with k = C_in / 16, a global batch of
     3x224x224 N(0,1) images split over the ranks (strong scaling).  One step
     is one forward of the local batch; img/s = global batch / max-over-ranks
-    time.  The headline value is the fused path (MoCE -> bn1 -> relu1 in the
-    MoCE kernels) with the whole forward captured once as a CUDA graph and
+    time.  The value is the fused path (MoCE -> bn1 -> relu1 in the MoCE
+    kernels) with the whole forward captured once as a CUDA graph and
     replayed per step; the same path launched eagerly and the reference's
-    eval order (MoCE, then BatchNorm and ReLU as torch ops) are reported
-    beside it, on the same weights."""
+    eval order (MoCE, then BatchNorm and ReLU as torch ops) are measured
+    beside it on the same weights when asked."""
     import torch
     import torch.distributed as dist
-    world, rank, local, dev = _dist_setup()
     from moce_thesis_b200 import resnet
-    gb = 1024
+    gb = global_batch
     per = gb // world
     kcfg = [[4, 16, 16], [16, 32, 32, 32], [32, 64, 64, 64, 64, 64], [64, 128, 128]]
     torch.manual_seed(0)
@@ -644,41 +777,60 @@ def run_resnet(args):
                     dist.barrier()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(st)
-                for _ in range(args.steps):
+                for _ in range(steps):
                     fwd()
                 e1.record(st)
                 torch.cuda.synchronize()
             del g
-        return _max_over_ranks(e0.elapsed_time(e1), world, dev) / args.steps, clk.summary()
+        return _max_over_ranks(e0.elapsed_time(e1), world, dev) / steps, clk.summary()
 
     # MoCE -> bn1 -> relu1 fused in the MoCE kernels (the product path, the
     # headline value), then the reference's eval sequence (MoCE, then
     # BatchNorm and ReLU as torch ops) on the same weights
     resnet.set_fused_epilogue(model, True)
     ms, clocks = timed(graph=True)
-    ms_eager, _ = timed()
-    resnet.set_fused_epilogue(model, False)
-    ms_plain, _ = timed()
-    resnet.set_fused_epilogue(model, True)
     out = {"metric": "ResNet-50-MoCE inference img/s", "value": round(gb / (ms * 1e-3), 1), "unit": "img/s",
-           "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+           "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-           "data": "synthetic N(0,1) images, seed 0 per rank; random Kaiming init",
+           "data": "synthetic N(0,1) images, seed = rank; random Kaiming init",
            "config": {"workload": "ResNet-50 + MoCE (every bottleneck entrance, k = C_in/16), ImageNet stem, "
-                                  "global batch 1024 of 3x224x224", "global_batch": gb, "per_gpu_batch": per,
+                                  f"global batch {gb} of 3x224x224", "global_batch": gb, "per_gpu_batch": per,
                       "parallelism": f"data-parallel x{world}, no collective in inference",
                       "inference": "MoCE -> bn1 -> relu1 in the MoCE kernels; other layers torch / cuDNN, NCHW; "
                                    "the forward replayed as one CUDA graph"},
-           "eager": {"value": round(gb / (ms_eager * 1e-3), 1), "ms_per_step": round(ms_eager, 3),
-                     "note": "same path, launched op by op instead of one CUDA graph"},
-           "unfused": {"value": round(gb / (ms_plain * 1e-3), 1), "ms_per_step": round(ms_plain, 3),
-                       "note": "reference eval order, eager"},
            "clocks": clocks}
+    if eager:
+        ms_eager, _ = timed()
+        out["eager"] = {"value": round(gb / (ms_eager * 1e-3), 1), "ms_per_step": round(ms_eager, 3),
+                        "note": "same path, launched op by op instead of one CUDA graph"}
+    if unfused:
+        resnet.set_fused_epilogue(model, False)
+        ms_plain, _ = timed()
+        resnet.set_fused_epilogue(model, True)
+        out["unfused"] = {"value": round(gb / (ms_plain * 1e-3), 1), "ms_per_step": round(ms_plain, 3),
+                          "note": "reference eval order, eager"}
+    del model, x
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_resnet(args):
+    """ResNet-50 + MoCE inference img/s; prints its own JSON line."""
+    import torch.distributed as dist
+    world, rank, local, dev = _dist_setup()
+    out = resnet_measure(args, world, rank, local, dev, args.steps, global_batch=args.resnet_batch)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(out), flush=True)
+
+
+def _set_batch(b):
+    """Images per GPU of the stage-4 layer (default 256; larger only for
+    profiling captures whose routed output must exceed L2)."""
+    global B
+    B = int(b)
 
 
 def main():
@@ -690,9 +842,14 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["stage4", "train", "sweep", "resnet50"], default="stage4")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="headline line only: skip the fp32, ResNet-50 and training sub-measurements")
+    ap.add_argument("--resnet-batch", type=int, default=1024, help="global batch of --workload resnet50")
+    ap.add_argument("--batch", type=int, default=256, help="images per GPU of the stage-4 layer (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    _set_batch(args.batch)
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "train":

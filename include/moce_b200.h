@@ -133,8 +133,17 @@ int moce_mix_scheduled(const void* x, int dtype, int64_t B, int64_t C,
  * tile (zero off the supports) with the staged X (bulk copies into shared
  * memory, tcgen05.mma with the accumulator in tensor memory).  Weights are
  * rounded to the input's 16-bit type before the product (fp32 accumulation).
- * Waits inside the kernel are bounded; moce_tc_fault reads (and optionally
- * clears) the flag a wait that ran out sets.
+ *
+ * Waits inside the kernel are bounded in time.  If a wait of one role of the
+ * kernel on another runs out (about one second by default), the kernel sets a
+ * device flag and abandons the launch, so part of y is left unwritten.  The
+ * copies and MMAs already in flight complete, the kernel returns, and the
+ * CUDA context stays usable.  moce_tc_fault reads (and optionally clears)
+ * that flag.  It synchronises with the device, so check it after a batch of
+ * calls, not after each one.  moce_tc_wait_limit_ns(ns) sets the bound, in
+ * nanoseconds, for launches made after it when ns > 0, and returns the bound
+ * that was in effect; ns <= 0 only queries.  (No reference counterpart: the
+ * reference kernels have no waits.)
  */
 int moce_tc_supported(int dtype, int64_t C, int64_t HW, int64_t k);
 size_t moce_tc_stage_bytes(int64_t B, int64_t C, int64_t HW);
@@ -148,6 +157,7 @@ int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C,
                 const float* gate_b, float tmin_tau, float trange_tau,
                 void* y, float* T_out, void* stream);
 int moce_tc_fault(int* flag, int clear);
+int64_t moce_tc_wait_limit_ns(int64_t ns);
 
 /*
  * Both tensor-core passes in one call: moce_pool_stage, then moce_mix_tc
@@ -292,10 +302,12 @@ int moce_gate_route(const void* x, int dtype, const float* pooled,
  * (4 MiB), which every GPU that loads the library holds until exit.  Shapes
  * needing more (moce_gate_route_workspace_bytes) fail with
  * MOCE_ERR_UNSUPPORTED.  The first call on a device looks up the array's
- * device address (cudaGetSymbolAddress) with that device current; make that
- * first call before any stream capture.  All calls share the array: calls
- * that overlap on the GPU race and must be serialised by the caller.  It
- * never calls cudaMalloc or cudaFree.
+ * device address (cudaGetSymbolAddress) with that device current and keeps
+ * it for the life of the process; make that first call before any stream
+ * capture.  Calls across a cudaDeviceReset of that device are not supported
+ * (the kept address belongs to the context the reset destroyed).  All calls
+ * share the array: calls that overlap on the GPU race and must be serialised
+ * by the caller.  It never calls cudaMalloc or cudaFree.
  */
 size_t moce_noalloc_scratch_bytes(void);
 int moce_gate_route_noalloc(const void* x, int dtype, const float* pooled,

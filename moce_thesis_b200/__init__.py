@@ -6,6 +6,6 @@ The package holds the CUDA kernels and C ABI (``csrc/``, built into
 nn.Module surface (Elianiluk/MoCE_thesis ``MoCE.py``) routed through those
 kernels in both eval and train mode.
 """
-from .moce import MoCE, MoCEFunction, native  # noqa: F401
+from .moce import MoCE, MoCEFunction, check_faults, native  # noqa: F401
 
-__all__ = ["MoCE", "MoCEFunction", "native"]
+__all__ = ["MoCE", "MoCEFunction", "check_faults", "native"]

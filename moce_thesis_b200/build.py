@@ -5,7 +5,8 @@
 * ``moce_fixed/moce_cuda<EXT_SUFFIX>`` -- the PyTorch binding (reference
   module path ``moce_fixed.moce_cuda``), linked against the library above.
 
-Run ``python -m moce_thesis_b200.build`` (or ``python setup.py build_ext``).
+Run ``python -m moce_thesis_b200.build``, or ``python setup.py build_ext``
+(``setup.py`` at the repository root drives the same two steps).
 Objects go to ``_build/``; nothing is written outside the repository.
 """
 from __future__ import annotations

@@ -25,10 +25,13 @@
 // accumulator), A rewritten per K-half as soon as the previous sample's MMAs
 // release it, and the staged-X copies running several quarters ahead.
 //
-// Every wait is bounded: a wait that runs out sets g_tc_fault, the roles
-// leave their loops together, copies and MMAs in flight complete, and the
-// kernel returns after releasing its tensor memory.
+// Every wait is bounded in time (%globaltimer): a wait on another role that
+// runs out (TcArgs::wait_ns, about one second unless the caller sets it with
+// moce_tc_wait_limit_ns) sets g_tc_fault, the roles leave their loops
+// together, the copies and MMAs already in flight complete (waits bounded by
+// kOwnWaitNs), and the kernel returns after releasing its tensor memory.
 #include <algorithm>
+#include <atomic>
 
 #include "common.cuh"
 
@@ -39,7 +42,10 @@ __device__ int g_tc_fault = 0;
 namespace {
 
 constexpr int kTcMaxN = 256;              // pixels per MMA (N), padded to 16
-constexpr long long kSpinLimit = 1ll << 28;
+// bound of a wait for this thread's own copies or MMAs already in flight,
+// which the hardware completes by itself
+constexpr uint64_t kOwnWaitNs = 2000000000ull;
+constexpr long long kDefaultWaitNs = 1ll << 30;   // about 1.07 s
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -68,21 +74,35 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
 
-// Bounded parity wait; returns false if the limit ran out.
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(a), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Wait for this thread's own copies or MMAs in flight (bounded by
+// kOwnWaitNs); returns false if the bound ran out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t a = smem_u32(bar);
-  for (long long it = 0; it < kSpinLimit; ++it) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
+  if (mbar_try(a, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try(a, parity)) return true;
+    if (global_ns() - t0 > kOwnWaitNs) return false;
   }
-  return false;
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -125,6 +145,7 @@ struct TcArgs {
   int NP, NA, P;                  // MMA N (pixel tile, a multiple of 16), 64-pixel atoms, partial accumulators
   int NT;                         // pixel tiles per sample (NP pixels each, the last one shorter)
   uint32_t tmem_cols;             // tensor-memory columns allocated (power of 2)
+  unsigned long long wait_ns;     // bound of a wait on another role
   int drain;                      // output path, one of the TcDrain values
   int stg_pitch;                  // staging row pitch: elements (kDrainOneTile, kDrainRowsLegacy), bytes (kDrainRows)
   int nsb;                        // staging buffers (kDrainRows)
@@ -164,20 +185,19 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
-// Bounded wait that also gives up when another role has aborted.
-__device__ __forceinline__ bool mbar_wait_abort(uint64_t* bar, uint32_t parity, volatile int* abort) {
+// Wait on another role, bounded by limit_ns; also gives up when another role
+// has aborted.  A wait that runs out raises the CTA's abort flag and
+// g_tc_fault.
+__device__ __forceinline__ bool mbar_wait_abort(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                uint64_t limit_ns) {
   const uint32_t a = smem_u32(bar);
-  for (long long it = 0; it < kSpinLimit; ++it) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if ((it & 1023) == 1023 && *abort) return false;
+  if (mbar_try(a, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try(a, parity)) return true;
+    if (*abort) return false;
+    if (global_ns() - t0 > limit_ns) break;
   }
   *abort = 1;
   atomicExch(&g_tc_fault, 1);
@@ -313,6 +333,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   float* s_gw = s_z + 2 * Kp;
   TcBars* bars = reinterpret_cast<TcBars*>(s_gw + KMAX);
   volatile int* abort = &bars->abort;
+  const uint64_t wlim = a.wait_ns;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x % a.n_tiles, bsplit = blockIdx.x / a.n_tiles;
@@ -409,14 +430,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       int n = n_pre;
       for (; n < total; ++n) {
         const int slot = n % NS, use = n / NS;
-        if (use >= 1 && !mbar_wait_abort(&bars->slot_free[slot], (use - 1) & 1, abort)) break;
+        if (use >= 1 && !mbar_wait_abort(&bars->slot_free[slot], (use - 1) & 1, abort, wlim)) break;
         mbar_expect_tx(&bars->full_b[slot], qbytes);
         bulk_g2s(aB + (uint32_t)slot * qbytes, xs + (size_t)(n >> 2) * sbytes + (size_t)(n & 3) * qbytes, qbytes,
                  &bars->full_b[slot]);
       }
       // copies still in flight land before the block can exit (no-op on the
       // normal path: the issuers consumed every slot)
-      for (int m = (n > NS ? n - NS : 0); m < n; ++m) mbar_wait(&bars->full_b[m % NS], (m / NS) & 1);
+      for (int m = (n > NS ? n - NS : 0); m < n; ++m)
+        if (!mbar_wait(&bars->full_b[m % NS], (m / NS) & 1)) atomicExch(&g_tc_fault, 1);
     }
   } else if (warp == kWarpIssuer0 || warp == kWarpIssuer0 + 1) {
     // ===================== MMA issuers.  P == 2: issuer h takes K-half h
@@ -437,16 +459,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       for (int i = 0; i < nb && run; ++i) {
         // one tile per sample: the accumulator buffer first, as it frees
         // earlier than the next weights
-        if (NT == 1 && i >= 2 && !mbar_wait_abort(&bars->d_empty[i & 1], ((i - 2) >> 1) & 1, abort)) break;
+        if (NT == 1 && i >= 2 && !mbar_wait_abort(&bars->d_empty[i & 1], ((i - 2) >> 1) & 1, abort, wlim)) break;
         // this sample's weights (A), both halves of this issuer
         for (int h = h0; h < h1 && run; ++h)
-          if (!mbar_wait_abort(&bars->a_full[h], i & 1, abort)) run = false;
+          if (!mbar_wait_abort(&bars->a_full[h], i & 1, abort, wlim)) run = false;
         if (!run) break;
         tc_fence_after();
         for (int t = 0; t < NT && run; ++t) {
           const int u = i * NT + t, s = u & 1;
           if (NT > 1 && u >= 2) {
-            if (!mbar_wait_abort(&bars->d_empty[s], ((u - 2) >> 1) & 1, abort)) {
+            if (!mbar_wait_abort(&bars->d_empty[s], ((u - 2) >> 1) & 1, abort, wlim)) {
               run = false;
               break;
             }
@@ -456,7 +478,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
             const uint32_t d = tmem + (uint32_t)(s * P * NP + (P == 2 ? h : 0) * NP);
             for (int qq = 0; qq < 2; ++qq) {
               const int q = 2 * h + qq, n = 4 * u + q, slot = n % NS;
-              if (!mbar_wait_abort(&bars->full_b[slot], (n / NS) & 1, abort)) {
+              if (!mbar_wait_abort(&bars->full_b[slot], (n / NS) & 1, abort, wlim)) {
                 run = false;
                 break;
               }
@@ -485,7 +507,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       }
       // every MMA of this thread completes before the block exits
       umma_commit(&bars->fin[hi]);
-      mbar_wait(&bars->fin[hi], 0);
+      if (!mbar_wait(&bars->fin[hi], 0)) atomicExch(&g_tc_fault, 1);
     }
   } else if (tid < WT) {
     // ===================== weight rows (pairs of threads per row)
@@ -536,7 +558,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       for (int h = 0; h < 2; ++h) {
         // the previous sample's MMAs have released this half of A
         bool w_ok = true;
-        if (i >= 1 && tid == 0) w_ok = mbar_wait_abort(&bars->a_free[h], (i - 1) & 1, abort);
+        if (i >= 1 && tid == 0) w_ok = mbar_wait_abort(&bars->a_free[h], (i - 1) & 1, abort, wlim);
         if (i >= 1) w_ok = role_sync_and(kBarWeights, WT, w_ok);
         if (!w_ok) {
           ok = false;
@@ -581,7 +603,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       for (int u = 0; u < nu; ++u) {
         const int s = u & 1;
         bool ok = true;
-        if (dlead) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
+        if (dlead) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort, wlim);
         if (dlead) bulk_wait_read();                          // the previous sample's copy left the block
         if (!role_sync_and(kBarDrain, DT, ok)) break;
         tc_fence_after();
@@ -643,7 +665,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         const int p0 = t * NP, tp = min(NP, HW - p0);       // a multiple of 8
         unsigned char* row = row0 + (size_t)(u % a.nsb) * 128u * pitch;
         bool ok = true;
-        if (dlead) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
+        if (dlead) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort, wlim);
         // this thread's copy out of this buffer, nsb units ago, has read it
         if (a.nsb == 2) bulk_wait_read_all_but1();
         else bulk_wait_read();
@@ -732,7 +754,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         const int s = u & 1, i = u / NT, t = u - (u / NT) * NT;
         const int p0 = t * NP, tp = min(NP, HW - p0);
         bool ok = true;
-        if (dlead) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
+        if (dlead) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort, wlim);
         if (!role_sync_and(kBarDrain, DT, ok)) break;
         tc_fence_after();
         const uint32_t tb = tmem + lane_base + (uint32_t)(s * P * NP);
@@ -780,7 +802,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         const int s = u & 1, i = u / NT, t = u - (u / NT) * NT;
         const int p0 = t * NP, tp = min(NP, HW - p0);         // this tile's pixels
         bool ok = true;
-        if (dlead) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort);
+        if (dlead) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort, wlim);
         bulk_wait_read();                                     // this thread's copy left the staging area
         if (!role_sync_and(kBarDrain, DT, ok)) break;
         tc_fence_after();
@@ -955,6 +977,13 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
                          const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out, void* stream,
                          bool dependent, OutEpilogue ep);
 
+// bound of the kernel's waits on another role, taken at each launch
+static std::atomic<long long> g_wait_ns{kDefaultWaitNs};
+
+extern "C" int64_t moce_tc_wait_limit_ns(int64_t ns) {
+  return (int64_t)(ns > 0 ? g_wait_ns.exchange((long long)ns) : g_wait_ns.load());
+}
+
 extern "C" int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
                            const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
                            const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out,
@@ -1024,7 +1053,7 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
   if (n_bsplit > B) n_bsplit = (int)B;
   TcArgs a{xstage, y, z, idx, ln, gate_w, gate_b, T_out, tmin_tau, trange_tau,
            (int)B, (int)C, (int)HW, (int)E_r, (int)k, Kp, n_tiles, n_bsplit, ns, sh.NP, sh.NA, sh.P, sh.NT,
-           sh.tmem_cols, sh.drain, sh.stg_pitch, sh.nsb, sh.stage_bytes, ep};
+           sh.tmem_cols, (unsigned long long)g_wait_ns.load(), sh.drain, sh.stg_pitch, sh.nsb, sh.stage_bytes, ep};
   return dispatch_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
     if constexpr (sizeof(T) != 2) {
@@ -1064,6 +1093,8 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
 
 extern "C" int moce_tc_fault(int* flag, int clear) {
   MOCE_REQUIRE(flag, MOCE_ERR_INVALID, "moce_tc_fault: null pointer");
+  // every stream's launches (not only the legacy stream's) have finished
+  if (cudaDeviceSynchronize() != cudaSuccess) return set_error(MOCE_ERR_CUDA, "moce_tc_fault: synchronize failed");
   if (cudaMemcpyFromSymbol(flag, g_tc_fault, sizeof(int)) != cudaSuccess)
     return set_error(MOCE_ERR_CUDA, "moce_tc_fault: read failed");
   if (clear) {

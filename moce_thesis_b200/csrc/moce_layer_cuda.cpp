@@ -414,6 +414,26 @@ std::vector<torch::Tensor> forward_scheduled(torch::Tensor x, torch::Tensor ln, 
 }
 
 
+// Shape, dtype and device checks shared by the fast-path bindings below
+// (forward_tc, forward_tc_ep, forward_px, forward_gx): every route tensor
+// must match x and idx, and live on x's device, before any pointer reaches
+// a kernel.
+void check_route_args(const torch::Tensor& x, const torch::Tensor& idx, const torch::Tensor& ln,
+                      const torch::Tensor& mask, const torch::Tensor& meta, const torch::Tensor& gate_w,
+                      const torch::Tensor& gate_b, const Dims& d) {
+  TORCH_CHECK(idx.scalar_type() == torch::kInt32 && ln.scalar_type() == torch::kFloat32, "idx int32, ln float32");
+  TORCH_CHECK(mask.scalar_type() == torch::kInt32 && meta.scalar_type() == torch::kInt32, "mask and meta int32");
+  TORCH_CHECK(gate_w.scalar_type() == torch::kFloat32 && gate_b.scalar_type() == torch::kFloat32,
+              "gate_w and gate_b must be float32");
+  TORCH_CHECK(ln.numel() == d.E_r * d.K, "ln must be (E_r, k)");
+  TORCH_CHECK(mask.numel() == d.C, "mask must have C entries");
+  TORCH_CHECK(meta.numel() >= 2, "meta must have 2 entries");
+  TORCH_CHECK(gate_w.numel() == d.K, "gate_w must have k entries");
+  TORCH_CHECK(gate_b.numel() >= 1, "gate_b must have one entry");
+  for (const torch::Tensor* t : {&idx, &ln, &mask, &meta, &gate_w, &gate_b})
+    TORCH_CHECK(t->device() == x.device(), "all tensors must be on the device of x");
+}
+
 bool tc_supported(torch::Tensor x, int64_t k) {
   if (!(x.scalar_type() == torch::kBFloat16 || x.scalar_type() == torch::kFloat16) || x.dim() != 4) return false;
   return moce_tc_supported(dtype_of(x), x.size(1), x.size(2) * x.size(3), k) != 0;
@@ -427,14 +447,15 @@ std::vector<torch::Tensor> forward_tc(torch::Tensor x, torch::Tensor idx, torch:
   for (auto* t : {&x, &idx, &ln, &mask, &meta, &gate_w, &gate_b}) {
     CHECK_INPUT(*t);
   }
-  TORCH_CHECK(idx.scalar_type() == torch::kInt32 && ln.scalar_type() == torch::kFloat32, "idx int32, ln float32");
   const c10::cuda::CUDAGuard guard(x.device());
   Dims d = dims(x, idx);
+  check_route_args(x, idx, ln, mask, meta, gate_w, gate_b, d);
   torch::Tensor y;
   if (out_opt.has_value()) {
     y = *out_opt;
     CHECK_INPUT(y);
     TORCH_CHECK(y.scalar_type() == x.scalar_type() && y.numel() == d.B * (d.E_r + 1) * d.HW, "out mismatch");
+    TORCH_CHECK(y.device() == x.device(), "out must be on the device of x");
   } else {
     y = torch::empty({d.B, d.E_r + 1, d.H, d.W}, x.options());
   }
@@ -457,17 +478,20 @@ torch::Tensor forward_tc_ep(torch::Tensor x, torch::Tensor idx, torch::Tensor ln
   for (auto* t : {&x, &idx, &ln, &mask, &meta, &gate_w, &gate_b, &out_scale, &out_shift}) {
     CHECK_INPUT(*t);
   }
-  TORCH_CHECK(idx.scalar_type() == torch::kInt32 && ln.scalar_type() == torch::kFloat32, "idx int32, ln float32");
   const c10::cuda::CUDAGuard guard(x.device());
   Dims d = dims(x, idx);
+  check_route_args(x, idx, ln, mask, meta, gate_w, gate_b, d);
   TORCH_CHECK(out_scale.scalar_type() == torch::kFloat32 && out_shift.scalar_type() == torch::kFloat32 &&
                   out_scale.numel() == d.E_r + 1 && out_shift.numel() == d.E_r + 1,
               "out_scale / out_shift must be float32 [E]");
+  TORCH_CHECK(out_scale.device() == x.device() && out_shift.device() == x.device(),
+              "out_scale / out_shift must be on the device of x");
   torch::Tensor y;
   if (out_opt.has_value()) {
     y = *out_opt;
     CHECK_INPUT(y);
     TORCH_CHECK(y.scalar_type() == x.scalar_type() && y.numel() == d.B * (d.E_r + 1) * d.HW, "out mismatch");
+    TORCH_CHECK(y.device() == x.device(), "out must be on the device of x");
   } else {
     y = torch::empty({d.B, d.E_r + 1, d.H, d.W}, x.options());
   }
@@ -494,14 +518,15 @@ std::vector<torch::Tensor> forward_px(torch::Tensor x, torch::Tensor idx, torch:
   for (auto* t : {&x, &idx, &ln, &mask, &meta, &gate_w, &gate_b}) {
     CHECK_INPUT(*t);
   }
-  TORCH_CHECK(idx.scalar_type() == torch::kInt32 && ln.scalar_type() == torch::kFloat32, "idx int32, ln float32");
   const c10::cuda::CUDAGuard guard(x.device());
   Dims d = dims(x, idx);
+  check_route_args(x, idx, ln, mask, meta, gate_w, gate_b, d);
   torch::Tensor y;
   if (out_opt.has_value()) {
     y = *out_opt;
     CHECK_INPUT(y);
     TORCH_CHECK(y.scalar_type() == x.scalar_type() && y.numel() == d.B * (d.E_r + 1) * d.HW, "out mismatch");
+    TORCH_CHECK(y.device() == x.device(), "out must be on the device of x");
   } else {
     y = torch::empty({d.B, d.E_r + 1, d.H, d.W}, x.options());
   }
@@ -529,14 +554,15 @@ std::vector<torch::Tensor> forward_gx(torch::Tensor x, torch::Tensor idx, torch:
   for (auto* t : {&x, &idx, &ln, &mask, &meta, &gate_w, &gate_b}) {
     CHECK_INPUT(*t);
   }
-  TORCH_CHECK(idx.scalar_type() == torch::kInt32 && ln.scalar_type() == torch::kFloat32, "idx int32, ln float32");
   const c10::cuda::CUDAGuard guard(x.device());
   Dims d = dims(x, idx);
+  check_route_args(x, idx, ln, mask, meta, gate_w, gate_b, d);
   torch::Tensor y;
   if (out_opt.has_value()) {
     y = *out_opt;
     CHECK_INPUT(y);
     TORCH_CHECK(y.scalar_type() == x.scalar_type() && y.numel() == d.B * (d.E_r + 1) * d.HW, "out mismatch");
+    TORCH_CHECK(y.device() == x.device(), "out must be on the device of x");
   } else {
     y = torch::empty({d.B, d.E_r + 1, d.H, d.W}, x.options());
   }
@@ -599,4 +625,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("gate_b"), py::arg("tmin_tau"), py::arg("trange_tau"), py::arg("want_T") = false,
         py::arg("out") = py::none());
   m.def("version", []() { return std::string(moce_version()); });
+  m.def("tc_fault", [](bool clear) {
+    int flag = 0;
+    ok(moce_tc_fault(&flag, clear ? 1 : 0));
+    return flag;
+  }, "Device flag set when a bounded wait inside a tensor-core kernel ran out (synchronises)",
+        py::arg("clear") = true);
 }

@@ -22,6 +22,7 @@ logits only and stays a PyTorch expression.
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 import torch.nn as nn
@@ -32,6 +33,21 @@ def native():
     """The compiled binding ``moce_fixed.moce_cuda`` (raises if unbuilt)."""
     import moce_fixed.moce_cuda as m
     return m
+
+
+# MOCE_CHECK_FAULTS=1: synchronise after every tensor-core forward and raise
+# if one of its bounded waits ran out (the launch then left part of y
+# unwritten).  Off by default, because the check synchronises the device.
+_CHECK_FAULTS = os.environ.get("MOCE_CHECK_FAULTS", "0") not in ("", "0")
+
+
+def check_faults(clear: bool = True) -> None:
+    """Raise if a bounded wait inside a tensor-core kernel ran out since the
+    last check (the device flag moce_tc_fault reads).  Synchronises the
+    current device; call it after a batch of forwards."""
+    if native().tc_fault(bool(clear)):
+        raise RuntimeError("MoCE tensor-core kernel: a bounded wait ran out; the outputs of the launches since "
+                           "the last check are incomplete")
 
 
 class _Route:
@@ -73,6 +89,8 @@ class _Route:
         if m.tc_supported(x, k):
             y, z, T = m.forward_tc(x, self.idx, self.ln, self.mask, self.meta, gate_w, gate_b, float(tmin_tau),
                                    float(trange_tau), bool(want_T), out)
+            if _CHECK_FAULTS:
+                check_faults()
             return y, z, (T if want_T else None)
         if m.px_supported(x, k):
             y, z, T = m.forward_px(x, self.idx, self.ln, self.mask, self.meta, gate_w, gate_b, float(tmin_tau),
@@ -268,9 +286,12 @@ class MoCE(nn.Module):
                 shift = shift + bn.bias.float()
         gw = self.cached_gate_weight.detach().reshape(-1).float().contiguous()
         gb = self.cached_gate_bias.detach().reshape(-1).float().contiguous()
-        return m.forward_tc_ep(x.contiguous(), route.idx, route.ln, route.mask, route.meta, gw, gb,
-                               float(self.cached_temp_min_tau), float(self.cached_temp_range_tau),
-                               scale.contiguous(), shift.contiguous(), bool(relu))
+        y = m.forward_tc_ep(x.contiguous(), route.idx, route.ln, route.mask, route.meta, gw, gb,
+                            float(self.cached_temp_min_tau), float(self.cached_temp_range_tau),
+                            scale.contiguous(), shift.contiguous(), bool(relu))
+        if _CHECK_FAULTS:
+            check_faults()
+        return y
 
     # ------------------------------------------------------------------
     def forward_host(self, x, out=None, slices=8):

@@ -2,7 +2,7 @@
 
 Run in the development container, where the reference checkout exists:
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path of the reference checkout>
 
 The reference module does ``import moce_fixed.moce_cuda`` at import time; a
 stub module is installed in ``sys.modules`` first.  The stub restates the one
@@ -132,7 +132,9 @@ def summarize(d, seed=1234):
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path of the reference checkout>")
+    ref_root = sys.argv[1]
     torch.set_num_threads(os.cpu_count() or 1)
     MoCE = _import_reference(ref_root)
     for name, case in CASES.items():

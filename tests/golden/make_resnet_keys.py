@@ -2,7 +2,7 @@
 
 Run in the development container, where the reference checkout exists:
 
-    python tests/golden/make_resnet_keys.py /root/reference
+    python tests/golden/make_resnet_keys.py <path of the reference checkout>
 
 Imports the unmodified ``models_unified.py`` (its ``import moce_fixed.moce_cuda``
 is satisfied by an empty stub module: building the model calls no kernel) and
@@ -42,4 +42,6 @@ def main(ref):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_resnet_keys.py <path of the reference checkout>")
+    main(sys.argv[1])

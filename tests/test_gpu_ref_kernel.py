@@ -1,0 +1,76 @@
+"""The reference's own CUDA path as a second oracle (GPU).
+
+``oracle/_ref`` holds the reference extension built from its unmodified
+sources (``oracle/build_ref.py``; the build travels with the repository),
+and ``oracle/ref_gpu.forward_eval`` runs the reference ``MoCE.forward_eval``
+on it: ATen pool, gate, temperature and softmax, then the reference kernels
+K2/K4 (or K3/K5 for maps of at most 16 pixels).  These tests compare the
+native layer with it at shapes no fixture covers, including the full
+stage-4 batch: fp32 within 1e-5 relative, bf16 within 1e-2 (the reference
+upcasts to fp32 and casts the result back), both with a floor of 1e-3 of
+the largest magnitude.  They are skipped when the reference build is absent.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+TMIN, TMAX, TAU = 0.1, 10.0, 1.0
+
+
+def _ref_mod():
+    from oracle import build_ref
+    if not os.path.exists(build_ref.TARGET):
+        pytest.skip("reference extension not built (oracle/build_ref.py)")
+    return build_ref.load()
+
+
+def close(a, b, rtol, floor):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return bool(np.all(np.abs(a - b) <= rtol * np.abs(b) + floor * max(np.abs(b).max(), 1e-30)))
+
+
+def worst(a, b):
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float((np.abs(a - b) / np.maximum(np.abs(b), 1e-3 * max(np.abs(b).max(), 1e-30))).max())
+
+
+@pytest.mark.parametrize("B,C,Hh,E,k,dtype", [
+    (8, 256, 14, 1024, 16, torch.float32),      # the single-layer CPU-runnable workload
+    (256, 512, 7, 2048, 32, torch.float32),     # the stage-4 layer, full batch, fp32
+    (256, 512, 7, 2048, 32, torch.bfloat16),    # the same in bf16 (tensor-core path here)
+    (16, 128, 4, 200, 40, torch.float32),       # H*W = 16: the reference's K3/K5 kernels
+    (4, 64, 9, 40, 8, torch.float32),           # uncovered channels: the residual expert is non-zero
+])
+def test_layer_matches_reference_kernels(B, C, Hh, E, k, dtype):
+    from moce_thesis_b200 import MoCE
+    from oracle import ref_gpu
+    mod = _ref_mod()
+    gen = torch.Generator().manual_seed(B + C + E + k)
+    X = torch.randn(B, C, Hh, Hh, generator=gen).abs()
+    L = torch.randn(E - 1, C, generator=gen)
+    gw = (torch.rand(1, k, generator=gen) * 2 - 1) * (6.0 / (k + 1)) ** 0.5
+    m = MoCE(in_channels=C, sampling_factor=1, k=k, temp_min=TMIN, temp_max=TMAX).to(DEV)
+    m.num_experts = E
+    m.routing_logits = torch.nn.Parameter(L.to(DEV))
+    with torch.no_grad():
+        m.gate.weight.copy_(gw)
+    m.eval()
+    m.build_eval_cache()
+    x = X.to(DEV, dtype)
+    with torch.no_grad():
+        y = m(x)
+    idx, ln, mask = ref_gpu.cache(L.to(DEV), k)
+    assert torch.equal(idx.to(torch.int32), m._route.idx)
+    assert torch.equal(mask, m._route.mask)
+    want = ref_gpu.forward_eval(mod, x, idx, ln, m.gate.weight.detach(), m.gate.bias.detach(), mask, TMIN, TMAX,
+                                TAU)
+    torch.cuda.synchronize()
+    a, b = y.float().cpu().numpy(), want.float().cpu().numpy()
+    rtol = 1e-5 if dtype == torch.float32 else 1e-2
+    assert close(a, b, rtol, 1e-3), worst(a, b)

@@ -34,28 +34,35 @@ def _inputs(seed, B, C, Hh, W, E, k, dtype):
     return X, r, gw, gb
 
 
-def _noalloc(x, pooled, r, gw, gb, tmin, tmax, tau):
+def _noalloc(x, pooled, idx, r, gw, gb, tmin, tmax, tau):
     B, C, Hh, W = x.shape
-    E_r, k = r["idx"].shape
+    E_r, k = idx.shape
+    bits = 64 if idx.dtype == torch.int64 else 32
     y = torch.empty(B, E_r + 1, Hh, W, dtype=x.dtype, device=x.device)
-    rc = capi.lib().moce_gate_route_noalloc(ptr(x), capi.dtype_code(x), ptr(pooled), ptr(r["idx"]), 32,
+    rc = capi.lib().moce_gate_route_noalloc(ptr(x), capi.dtype_code(x), ptr(pooled), ptr(idx), bits,
                                             ptr(r["ln"]), ptr(gw), ptr(gb), ptr(r["mask"]), tmin, tmax, tau,
                                             ptr(y), B, C, Hh * W, E_r, k, stream_handle())
     capi.check(rc, "moce_gate_route_noalloc")
     return y
 
 
+@pytest.mark.parametrize("index_bits", [32, 64])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("pooled_given", [False, True])
-def test_noalloc_matches_workspace_entry_twice(dtype, pooled_given):
+def test_noalloc_matches_workspace_entry_twice(dtype, pooled_given, index_bits):
+    """Three different calls in a row: none may see an earlier call's
+    scratch.  The last shape has k close to C, so its indices fill most of
+    the scratch region that 64-bit indices are converted into."""
     tol = 1e-5 if dtype == torch.float32 else 1e-2
-    # two different calls in a row: the second must not see the first's scratch
-    for seed, shape in ((1, (4, 64, 7, 7, 65, 8)), (2, (3, 96, 5, 5, 33, 12))):
+    lib = capi.lib()
+    for seed, shape in ((1, (4, 64, 7, 7, 65, 8)), (2, (3, 96, 5, 5, 33, 12)), (3, (2, 64, 3, 3, 1001, 60))):
         B, C, Hh, W, E, k = shape
+        assert lib.moce_gate_route_workspace_bytes(B, C, E - 1) <= lib.moce_noalloc_scratch_bytes()
         x, r, gw, gb = _inputs(seed, B, C, Hh, W, E, k, dtype)
+        idx = r["idx"].long().contiguous() if index_bits == 64 else r["idx"]
         pooled = x.float().mean((2, 3)).contiguous() if pooled_given else None
-        want = H.gate_route(x, pooled, r["idx"], r["ln"], gw, gb, r["mask"], 0.1, 10.0, 1.0)
-        got = _noalloc(x, pooled, r, gw, gb, 0.1, 10.0, 1.0)
+        want = H.gate_route(x, pooled, idx, r["ln"], gw, gb, r["mask"], 0.1, 10.0, 1.0)
+        got = _noalloc(x, pooled, idx, r, gw, gb, 0.1, 10.0, 1.0)
         torch.cuda.synchronize()
         a, b = got.float().cpu().numpy(), want.float().cpu().numpy()
         assert np.all(np.abs(a - b) <= tol * np.abs(b) + 1e-6 * np.abs(b).max()), float(np.abs(a - b).max())
