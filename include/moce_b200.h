@@ -115,6 +115,29 @@ int moce_mix_scheduled(const void* x, int dtype, int64_t B, int64_t C,
                        void* y, float* T_out, void* stream);
 
 /*
+ * Temperatures from the pooled means z fp32 [B, C] (pass 1's output), the
+ * step between the two passes:
+ *   T[b,e] = max(tmin_tau + trange_tau * sigmoid(g[b,e]), 1e-3)  fp32 [B, E_r]
+ * moce_temperature: the shared Linear(k,1) gate of the reference
+ * (MoCE.py:66-68, eval MoCE.py:216-218, train MoCE.py:175-178),
+ *   g[b,e] = gate_w . z[b, idx[e,:]] + gate_b[0];  k <= 128.
+ * moce_temperature_mlp: the two-layer gate C -> Hd -> E_r with ReLU of the
+ * benchmark configurations (no reference counterpart; the reference has only
+ * the Linear(k,1) gate),
+ *   h[b,:] = relu(w1 z[b,:] + b1)  (fp32 [B, Hd] out),
+ *   g[b,e] = w2[e,:] . h[b,:] + b2[e];
+ * w1 fp32 [Hd, C], b1 [Hd], w2 [E_r, Hd], b2 [E_r]; Hd <= 256.
+ */
+int moce_temperature(const float* z, int64_t B, int64_t C, const int32_t* idx,
+                     int64_t E_r, int64_t k, const float* gate_w,
+                     const float* gate_b, float tmin_tau, float trange_tau,
+                     float* T, void* stream);
+int moce_temperature_mlp(const float* z, int64_t B, int64_t C, int64_t Hd,
+                         int64_t E_r, const float* w1, const float* b1,
+                         const float* w2, const float* b2, float tmin_tau,
+                         float trange_tau, float* h, float* T, void* stream);
+
+/*
  * Tensor-core fast path, for bf16 / fp16 inputs with C <= 512 and k <= 64
  * (any H*W) whose operands fit the shared memory of one CTA (the ResNet-50
  * maps from 56x56 to 7x7); moce_tc_supported returns 1 for those.
@@ -128,11 +151,14 @@ int moce_mix_scheduled(const void* x, int dtype, int64_t B, int64_t C,
  * each row's 16-byte units swizzled by (channel mod 8).  moce_tc_stage_bytes
  * gives its size.
  *
- * moce_mix_tc: pass 2.  Same outputs as moce_mix_scheduled; the routed
- * experts are computed per sample as a dense product of the 128-expert weight
- * tile (zero off the supports) with the staged X (bulk copies into shared
- * memory, tcgen05.mma with the accumulator in tensor memory).  Weights are
- * rounded to the input's 16-bit type before the product (fp32 accumulation).
+ * moce_mix_tc: pass 2.  The routed experts 0 .. E_r-1 of y from the staged X
+ * and the temperatures T fp32 [B, E_r] (moce_temperature or
+ * moce_temperature_mlp): the softmax of ln / T (MoCE.py:219-221 / 188) and
+ * the gather-mix (moce_kernel.cu:57-141), computed per sample as a dense
+ * product of the 128-expert weight tile (zero off the supports) with the
+ * staged X (bulk copies into shared memory, tcgen05.mma with the accumulator
+ * in tensor memory).  Weights are rounded to the input's 16-bit type before
+ * the product (fp32 accumulation).
  *
  * Waits inside the kernel are bounded in time.  If a wait of one role of the
  * kernel on another runs out (about one second by default), the kernel sets a
@@ -152,25 +178,38 @@ int moce_pool_stage(const void* x, int dtype, int64_t B, int64_t C,
                     float* z, void* y, int64_t E_r, void* xstage,
                     void* stream);
 int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C,
-                int64_t HW, const float* z, const int32_t* idx,
-                const float* ln, int64_t E_r, int64_t k, const float* gate_w,
-                const float* gate_b, float tmin_tau, float trange_tau,
-                void* y, float* T_out, void* stream);
+                int64_t HW, const float* T, const int32_t* idx,
+                const float* ln, int64_t E_r, int64_t k, void* y,
+                void* stream);
 int moce_tc_fault(int* flag, int clear);
 int64_t moce_tc_wait_limit_ns(int64_t ns);
 
 /*
- * Both tensor-core passes in one call: moce_pool_stage, then moce_mix_tc
- * launched as a programmatic dependent of it (the mix's prologue overlaps
- * pass 1; its reads of z and xstage wait for pass 1 to complete).  Same
- * buffers and conditions as the two calls.
+ * The tensor-core forward in one call: moce_pool_stage, moce_temperature and
+ * moce_mix_tc, each launched as a programmatic dependent of the one before
+ * (its prologue overlaps the previous kernel; its reads wait for that
+ * kernel's results).  Same buffers and conditions as the three calls; T
+ * (fp32 [B, E_r]) is required, the mix reads it.
  */
 int moce_forward_tc(const void* x, int dtype, int64_t B, int64_t C, int64_t HW,
                     const int32_t* mask, const int32_t* meta,
                     const int32_t* idx, const float* ln, int64_t E_r,
                     int64_t k, const float* gate_w, const float* gate_b,
                     float tmin_tau, float trange_tau, float* z, void* xstage,
-                    void* y, float* T_out, void* stream);
+                    void* y, float* T, void* stream);
+
+/*
+ * moce_forward_tc with the two-layer temperature gate (moce_temperature_mlp)
+ * in place of the shared Linear(k, 1): z, the hidden layer h fp32 [B, Hd]
+ * and T are outputs.  No reference counterpart (see moce_temperature_mlp).
+ */
+int moce_forward_tc_mlp(const void* x, int dtype, int64_t B, int64_t C,
+                        int64_t HW, const int32_t* mask, const int32_t* meta,
+                        const int32_t* idx, const float* ln, int64_t E_r,
+                        int64_t k, int64_t Hd, const float* w1,
+                        const float* b1, const float* w2, const float* b2,
+                        float tmin_tau, float trange_tau, float* z, float* h,
+                        void* xstage, void* y, float* T, void* stream);
 
 /*
  * moce_forward_tc with the caller's next two ops folded into the output
@@ -181,7 +220,7 @@ int moce_forward_tc(const void* x, int dtype, int64_t B, int64_t C, int64_t HW,
  * BatchNorm2d folded to scale = weight / sqrt(running_var + eps),
  * shift = bias - running_mean * scale.  Replaces the MoCE -> bn1 -> relu1
  * sequence of BottleneckWithMoCEProjection.forward (models_unified.py:155-165).
- * T_out (when given) and z are the layer's own values, before the epilogue.
+ * T (required) and z are the layer's own values, before the epilogue.
  */
 int moce_forward_tc_ep(const void* x, int dtype, int64_t B, int64_t C,
                        int64_t HW, const int32_t* mask, const int32_t* meta,
@@ -190,7 +229,7 @@ int moce_forward_tc_ep(const void* x, int dtype, int64_t B, int64_t C,
                        float tmin_tau, float trange_tau,
                        const float* out_scale, const float* out_shift,
                        int out_relu, float* z, void* xstage, void* y,
-                       float* T_out, void* stream);
+                       float* T, void* stream);
 
 /*
  * CUDA-core pass 2 with lanes over pixels, any dtype, H*W <= 512, k <= 64,
@@ -208,6 +247,11 @@ int moce_mix_px(const void* x, int dtype, int64_t B, int64_t C, int64_t HW,
                 int64_t E_r, int64_t k, const float* gate_w,
                 const float* gate_b, float tmin_tau, float trange_tau,
                 void* y, float* T_out, void* stream);
+/* moce_mix_px with the temperatures given (fp32 [B, E_r], e.g. from
+ * moce_temperature_mlp) in place of the gate's inputs. */
+int moce_mix_px_t(const void* x, int dtype, int64_t B, int64_t C, int64_t HW,
+                  const float* T, const int32_t* idx, const float* ln,
+                  int64_t E_r, int64_t k, void* y, void* stream);
 
 /*
  * Pass 2 on CUDA cores for samples too large for shared memory (C >= 1024 at
@@ -224,6 +268,10 @@ int moce_mix_gx(const void* x, int dtype, int64_t B, int64_t C, int64_t HW,
                 int64_t E_r, int64_t k, const float* gate_w,
                 const float* gate_b, float tmin_tau, float trange_tau,
                 void* y, float* T_out, void* stream);
+/* moce_mix_gx with the temperatures given (fp32 [B, E_r]). */
+int moce_mix_gx_t(const void* x, int dtype, int64_t B, int64_t C, int64_t HW,
+                  const float* T, const int32_t* idx, const float* ln,
+                  int64_t E_r, int64_t k, void* y, void* stream);
 
 /*
  * Global average pool: pooled[b,c] = mean_p X[b,c,p] (fp32 out).
@@ -342,6 +390,23 @@ int moce_backward(const void* x, const void* dy, int dtype, int64_t B,
                   float trange_tau, const float* z, const float* T, void* dx,
                   float* dL, float* dgate_w, float* dgate_b, void* workspace,
                   size_t workspace_bytes, void* stream);
+
+/*
+ * moce_backward for temperatures that came from a gate the caller
+ * differentiates itself (the two-layer gate of moce_temperature_mlp): the
+ * same dX (mix and residual terms only, no gate term) and dL, and instead of
+ * the gate gradients dT fp32 [B, E_r], the gradient of the loss with respect
+ * to the temperatures the mix used.  The caller adds the gate's own
+ * contribution through z (dz / H*W per channel) to dX.  Same workspace.
+ * (No reference counterpart, as for moce_backward.)
+ */
+int moce_backward_t(const void* x, const void* dy, int dtype, int64_t B,
+                    int64_t C, int64_t HW, const float* logits,
+                    const int32_t* idx, const float* ln, const int32_t* mask,
+                    const int32_t* meta, const int32_t* toff,
+                    const int32_t* tslot, int64_t E_r, int64_t k,
+                    const float* T, void* dx, float* dL, float* dT,
+                    void* workspace, size_t workspace_bytes, void* stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

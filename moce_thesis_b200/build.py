@@ -33,7 +33,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
                      "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]
 
-CU_SOURCES = ["status.cu", "route.cu", "schedule.cu", "forward.cu", "mix.cu", "stage.cu", "mix_tc.cu", "simt.cu", "backward.cu", "noalloc.cu"]
+CU_SOURCES = ["status.cu", "route.cu", "schedule.cu", "forward.cu", "mix.cu", "stage.cu", "gate.cu", "mix_tc.cu", "simt.cu",
+              "backward.cu", "noalloc.cu"]
 
 
 def _run(cmd, verbose):

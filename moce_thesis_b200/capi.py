@@ -36,7 +36,11 @@ SIGNATURES = {
     "moce_tc_stage_bytes": (_sz, [_i64, _i64, _i64]),
     "moce_tc_supported": (_i32, [_i32, _i64, _i64, _i64]),
     "moce_pool_stage": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _p, _p]),
-    "moce_mix_tc": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p, _f32, _f32, _p, _p, _p]),
+    "moce_mix_tc": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p]),
+    "moce_temperature": (_i32, [_p, _i64, _i64, _p, _i64, _i64, _p, _p, _f32, _f32, _p, _p]),
+    "moce_temperature_mlp": (_i32, [_p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _f32, _f32, _p, _p, _p]),
+    "moce_forward_tc_mlp": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _i64, _p, _p, _p, _p,
+                                   _f32, _f32, _p, _p, _p, _p, _p, _p]),
     "moce_tc_fault": (_i32, [_p, _i32]),
     "moce_tc_wait_limit_ns": (_i64, [_i64]),
     "moce_forward_tc": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _p, _p, _f32, _f32, _p, _p, _p,
@@ -45,8 +49,10 @@ SIGNATURES = {
                                   _p, _p, _p, _p, _p]),
     "moce_px_supported": (_i32, [_i32, _i64, _i64, _i64]),
     "moce_mix_px": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p, _f32, _f32, _p, _p, _p]),
+    "moce_mix_px_t": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p]),
     "moce_gx_supported": (_i32, [_i32, _i64, _i64, _i64]),
     "moce_mix_gx": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p, _f32, _f32, _p, _p, _p]),
+    "moce_mix_gx_t": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p]),
     "moce_gate_temperature": (_i32, [_p, _i32, _p, _i64, _i64, _i64, _p, _i64, _i64, _p, _p, _f32, _f32,
                                      _p, _p, _p]),
     "moce_mix": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p, _p]),
@@ -60,6 +66,8 @@ SIGNATURES = {
     "moce_backward_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),
     "moce_backward": (_i32, [_p, _p, _i32, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _p, _p,
                              _f32, _f32, _p, _p, _p, _p, _p, _p, _p, _sz, _p]),
+    "moce_backward_t": (_i32, [_p, _p, _i32, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _p, _p, _p,
+                               _p, _p, _sz, _p]),
 }
 
 _lib = None

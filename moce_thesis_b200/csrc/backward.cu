@@ -12,6 +12,11 @@
 //   dL[e,S_e] = backward of ln = (sel - mean) / max(std, 1) applied to sum_b dln_b
 // Batch reductions run in a fixed order (no atomics), so results are
 // deterministic.
+//
+// Given-temperature mode (gate_w == nullptr; moce_backward_t): T came from a
+// gate the caller differentiates itself (the two-layer gate), so the kernels
+// stop at dT -- stored where dg goes, without the clamp mask or the sigmoid
+// factor, which belong to the caller's gate -- and add no dz term to dX.
 #include "px.cuh"
 
 namespace moce {
@@ -67,12 +72,15 @@ __global__ void __launch_bounds__(kThreads) bwd_route_kernel(
   float* s_pb = s_pw + kWarps * k;        // kWarps
   const int b = blockIdx.y, ch = blockIdx.x, nch = gridDim.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int c = threadIdx.x; c < C; c += kThreads) s_z[c] = z[(size_t)b * C + c];
-  for (int i = threadIdx.x; i < k; i += kThreads) s_w[i] = gate_w[i];
+  const bool tg = gate_w == nullptr;       // given-temperature mode
+  if (!tg) {
+    for (int c = threadIdx.x; c < C; c += kThreads) s_z[c] = z[(size_t)b * C + c];
+    for (int i = threadIdx.x; i < k; i += kThreads) s_w[i] = gate_w[i];
+  }
   for (int i = threadIdx.x; i < kWarps * k; i += kThreads) s_pw[i] = 0.0f;
   if (threadIdx.x < kWarps) s_pb[threadIdx.x] = 0.0f;
   __syncthreads();
-  const float bias = gate_b[0];
+  const float bias = tg ? 0.0f : gate_b[0];
   const int per = (E_r + nch - 1) / nch;
   const int e0 = ch * per, e1 = min(E_r, e0 + per);
   const int E = E_r + 1;
@@ -83,7 +91,8 @@ __global__ void __launch_bounds__(kThreads) bwd_route_kernel(
     const size_t be = (size_t)b * E_r + e;
     const float t = Tb[be];
     float g = 0.0f;
-    for (int i = lane; i < k; i += 32) g += s_w[i] * s_z[ie[i]];
+    if (!tg)
+      for (int i = lane; i < k; i += 32) g += s_w[i] * s_z[ie[i]];
     g = warp_sum(g) + bias;
     float m = -INFINITY;
     for (int i = lane; i < k; i += 32) m = nan_max(m, lne[i] / t);
@@ -125,15 +134,19 @@ __global__ void __launch_bounds__(kThreads) bwd_route_kernel(
       }
     }
     float dT = -warp_sum(dTp) / t;
-    const float sig = 1.0f / (1.0f + expf(-g));
-    const float t_raw = tmin_tau + trange_tau * sig;
-    if (!(t_raw >= 1e-3f)) dT = 0.0f;
-    const float dg = dT * trange_tau * sig * (1.0f - sig);
+    float dg = dT;                          // given-temperature mode: dT itself
+    if (!tg) {
+      const float sig = 1.0f / (1.0f + expf(-g));
+      const float t_raw = tmin_tau + trange_tau * sig;
+      if (!(t_raw >= 1e-3f)) dT = 0.0f;
+      dg = dT * trange_tau * sig * (1.0f - sig);
+    }
     if (lane == 0) {
       ws.dg[be] = dg;
       s_pb[warp] += dg;
     }
-    for (int i = lane; i < k; i += 32) s_pw[warp * k + i] += dg * s_z[ie[i]];
+    if (!tg)
+      for (int i = lane; i < k; i += 32) s_pw[warp * k + i] += dg * s_z[ie[i]];
   }
   __syncthreads();
   const size_t q = (size_t)b * nch + ch;
@@ -163,10 +176,11 @@ __global__ void __launch_bounds__(kThreads) bwd_dx_kernel(
   const int s0 = toff[c], s1 = toff[c + 1];
   const size_t bek = (size_t)b * E_r * k;
   float dz = 0.0f;
-  for (int s = s0 + lane; s < s1; s += 32) {
-    const int slot = tslot[s];
-    dz += ws.dg[(size_t)b * E_r + slot / k] * gate_w[slot % k];
-  }
+  if (gate_w)
+    for (int s = s0 + lane; s < s1; s += 32) {
+      const int slot = tslot[s];
+      dz += ws.dg[(size_t)b * E_r + slot / k] * gate_w[slot % k];
+    }
   dz = warp_sum(dz);
   const int n_u = meta[0];
   const float rw = (mask[c] == 1 && n_u > 0) ? 1.0f / (float)n_u : 0.0f;
@@ -247,12 +261,15 @@ __global__ void __launch_bounds__(kPxThreadsB, 1) bwd_px_route_kernel(
   const int b = blockIdx.y, ch = blockIdx.x, nch = gridDim.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   px_stage_rows<T>(s_x, x + (size_t)b * C * HW, C, HW, HWp);
-  for (int c = threadIdx.x; c < C; c += kPxThreadsB) s_z[c] = z[(size_t)b * C + c];
-  for (int i = threadIdx.x; i < k; i += kPxThreadsB) s_w[i] = gate_w[i];
+  const bool tg = gate_w == nullptr;       // given-temperature mode
+  if (!tg) {
+    for (int c = threadIdx.x; c < C; c += kPxThreadsB) s_z[c] = z[(size_t)b * C + c];
+    for (int i = threadIdx.x; i < k; i += kPxThreadsB) s_w[i] = gate_w[i];
+  }
   for (int i = threadIdx.x; i < kPxWarpsB * k; i += kPxThreadsB) s_pw[i] = 0.0f;
   if (threadIdx.x < kPxWarpsB) s_pb[threadIdx.x] = 0.0f;
   __syncthreads();
-  const float bias = gate_b[0];
+  const float bias = tg ? 0.0f : gate_b[0];
   const int per = (E_r + nch - 1) / nch;
   const int e0 = ch * per, e1 = min(E_r, e0 + per);
   const int E = E_r + 1;
@@ -297,7 +314,7 @@ __global__ void __launch_bounds__(kPxThreadsB, 1) bwd_px_route_kernel(
       ln_n = valid ? ln[(size_t)(e + kPxWarpsB) * k + lane] : 0.0f;
       t_n = Tb[be + kPxWarpsB];
     }
-    const float g = warp_sum(valid ? s_w[lane] * s_z[c_l] : 0.0f) + bias;
+    const float g = warp_sum((valid && !tg) ? s_w[lane] * s_z[c_l] : 0.0f) + bias;
     const float u = valid ? ln_l / t : -INFINITY;
     const float m = warp_max(u);
     const float ex = valid ? expf(u - m) : 0.0f;
@@ -325,14 +342,17 @@ __global__ void __launch_bounds__(kPxThreadsB, 1) bwd_px_route_kernel(
     const float S = warp_sum(valid ? a_l * da : 0.0f);
     const float du = valid ? a_l * (da - S) : 0.0f;
     float dT = -warp_sum(du * (valid ? u : 0.0f)) / t;
-    const float sig = 1.0f / (1.0f + expf(-g));
-    const float t_raw = tmin_tau + trange_tau * sig;
-    if (!(t_raw >= 1e-3f)) dT = 0.0f;
-    const float dg = dT * trange_tau * sig * (1.0f - sig);
+    float dg = dT;                          // given-temperature mode: dT itself
+    if (!tg) {
+      const float sig = 1.0f / (1.0f + expf(-g));
+      const float t_raw = tmin_tau + trange_tau * sig;
+      if (!(t_raw >= 1e-3f)) dT = 0.0f;
+      dg = dT * trange_tau * sig * (1.0f - sig);
+    }
     if (valid) {
       ws.a[be * k + lane] = a_l;
       ws.dlnb[be * k + lane] = du / t;
-      s_pw[warp * k + lane] += dg * s_z[c_l];
+      if (!tg) s_pw[warp * k + lane] += dg * s_z[c_l];
     }
     if (lane == 0) {
       ws.dg[be] = dg;
@@ -390,7 +410,7 @@ __global__ void __launch_bounds__(kDxThreads, 1) bwd_px_dx_kernel(
       const int slot = tslot[s];
       e_l = slot / k;
       a_l = ws.a[bek + slot];
-      g_l = ws.dg[(size_t)b * E_r + e_l] * gate_w[slot - e_l * k];
+      g_l = gate_w ? ws.dg[(size_t)b * E_r + e_l] * gate_w[slot - e_l * k] : 0.0f;
     }
   };
   int c = warp, sc = (c < C) ? toff[c] : 0;
@@ -545,16 +565,19 @@ extern "C" size_t moce_backward_workspace_bytes(int64_t B, int64_t C, int64_t HW
   return ws_layout(B, E_r, k, nullptr, nullptr);
 }
 
-extern "C" int moce_backward(const void* x, const void* dy, int dtype, int64_t B, int64_t C, int64_t HW,
-                             const float* logits, const int32_t* idx, const float* ln, const int32_t* mask,
-                             const int32_t* meta, const int32_t* toff, const int32_t* tslot, int64_t E_r,
-                             int64_t k, const float* gate_w, const float* gate_b, float tmin_tau,
-                             float trange_tau, const float* z, const float* T, void* dx, float* dL,
-                             float* dgate_w, float* dgate_b, void* workspace, size_t workspace_bytes,
-                             void* stream) {
-  MOCE_REQUIRE(logits && idx && ln && mask && meta && toff && tslot && gate_w && gate_b && dL && dgate_w && dgate_b,
+// The linear-gate backward (gate_w given: dgate_w, dgate_b out) or the
+// given-temperature backward (gate_w null: dT out).
+static int backward_run(const void* x, const void* dy, int dtype, int64_t B, int64_t C, int64_t HW,
+                        const float* logits, const int32_t* idx, const float* ln, const int32_t* mask,
+                        const int32_t* meta, const int32_t* toff, const int32_t* tslot, int64_t E_r, int64_t k,
+                        const float* gate_w, const float* gate_b, float tmin_tau, float trange_tau, const float* z,
+                        const float* T, void* dx, float* dL, float* dgate_w, float* dgate_b, float* dT,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  const bool tg = gate_w == nullptr;
+  MOCE_REQUIRE(logits && idx && ln && mask && meta && toff && tslot && dL &&
+                   (tg ? dT != nullptr : (gate_b && dgate_w && dgate_b)),
                MOCE_ERR_INVALID, "moce_backward: null pointer argument");
-  MOCE_REQUIRE(B == 0 || (x && dy && z && T && dx), MOCE_ERR_INVALID, "moce_backward: null pointer argument");
+  MOCE_REQUIRE(B == 0 || (x && dy && (tg || z) && T && dx), MOCE_ERR_INVALID, "moce_backward: null pointer argument");
   MOCE_REQUIRE(dtype_ok(dtype), MOCE_ERR_INVALID, "moce_backward: unknown dtype %d", dtype);
   int rc = check_bwd_shapes(B, C, HW, E_r, k);
   if (rc) return rc;
@@ -567,8 +590,8 @@ extern "C" int moce_backward(const void* x, const void* dy, int dtype, int64_t B
   const int nch = bwd_chunks(B, E_r);
   if (B == 0) {
     if (cudaMemsetAsync(dL, 0, (size_t)E_r * C * 4, st) != cudaSuccess ||
-        cudaMemsetAsync(dgate_w, 0, (size_t)k * 4, st) != cudaSuccess ||
-        cudaMemsetAsync(dgate_b, 0, 4, st) != cudaSuccess)
+        (!tg && (cudaMemsetAsync(dgate_w, 0, (size_t)k * 4, st) != cudaSuccess ||
+                 cudaMemsetAsync(dgate_b, 0, 4, st) != cudaSuccess)))
       return set_error(MOCE_ERR_CUDA, "moce_backward: memset failed");
     return MOCE_OK;
   }
@@ -622,6 +645,34 @@ extern "C" int moce_backward(const void* x, const void* dy, int dtype, int64_t B
                                                                                   (int)E_r, (int)k, ws, dL);
   rc = check_launch("moce_backward/logits");
   if (rc) return rc;
+  if (tg) {
+    // dT [B, E_r] lies in the workspace where dg goes
+    if (cudaMemcpyAsync(dT, ws.dg, (size_t)B * E_r * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+      return set_error(MOCE_ERR_CUDA, "moce_backward_t: copy of dT failed");
+    return MOCE_OK;
+  }
   bwd_gate_reduce_kernel<<<(unsigned)((k + 1 + 7) / 8), 256, 0, st>>>(ws, (int)(B * nch), (int)k, dgate_w, dgate_b);
   return check_launch("moce_backward/gate");
+}
+
+extern "C" int moce_backward(const void* x, const void* dy, int dtype, int64_t B, int64_t C, int64_t HW,
+                             const float* logits, const int32_t* idx, const float* ln, const int32_t* mask,
+                             const int32_t* meta, const int32_t* toff, const int32_t* tslot, int64_t E_r,
+                             int64_t k, const float* gate_w, const float* gate_b, float tmin_tau,
+                             float trange_tau, const float* z, const float* T, void* dx, float* dL,
+                             float* dgate_w, float* dgate_b, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  MOCE_REQUIRE(gate_w, MOCE_ERR_INVALID, "moce_backward: null gate_w (moce_backward_t takes given temperatures)");
+  return backward_run(x, dy, dtype, B, C, HW, logits, idx, ln, mask, meta, toff, tslot, E_r, k, gate_w, gate_b,
+                      tmin_tau, trange_tau, z, T, dx, dL, dgate_w, dgate_b, nullptr, workspace, workspace_bytes,
+                      stream);
+}
+
+extern "C" int moce_backward_t(const void* x, const void* dy, int dtype, int64_t B, int64_t C, int64_t HW,
+                               const float* logits, const int32_t* idx, const float* ln, const int32_t* mask,
+                               const int32_t* meta, const int32_t* toff, const int32_t* tslot, int64_t E_r,
+                               int64_t k, const float* T, void* dx, float* dL, float* dT, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  return backward_run(x, dy, dtype, B, C, HW, logits, idx, ln, mask, meta, toff, tslot, E_r, k, nullptr, nullptr, 0.f,
+                      0.f, nullptr, T, dx, dL, nullptr, nullptr, dT, workspace, workspace_bytes, stream);
 }

@@ -132,13 +132,9 @@ __device__ __forceinline__ uint32_t a_off(int row, int c) {
 struct TcArgs {
   const void* xstage;             // [B, Kp, 128 B] operand-layout copy of X (pass 1)
   void* y;
-  const float* z;
+  const float* T;                 // [B, E_r] temperatures (the temperature kernel, between the passes)
   const int32_t* idx;
   const float* ln;
-  const float* gate_w;
-  const float* gate_b;
-  float* T_out;
-  float tmin_tau, trange_tau;
   int B, C, HW, E_r, k, Kp;       // Kp: C rounded up to 64
   int n_tiles, n_bsplit;
   int ns;                         // X quarter slots in the ring
@@ -293,10 +289,11 @@ constexpr int kWarpIssuer0 = 12, kWarpProducer = 14;
 // Roles (warp-specialized, one CTA per SM):
 //   warps 0-7   weight rows: threads 2r and 2r+1 share expert row e0 + r,
 //               each with half of its supports (a pair of adjacent lanes
-//               combines sums by shuffle); per sample the gate, temperature
-//               and softmax (MoCE.py:216-221 / 175-188), written as bf16/fp16
-//               into A one K-half at a time, as soon as the MMAs of the
-//               previous sample have released that half
+//               combines sums by shuffle); per sample the softmax of
+//               ln / T (MoCE.py:219-221 / 188) with T[b, e] read from the
+//               temperature kernel's output, written as bf16/fp16 into A
+//               one K-half at a time, as soon as the MMAs of the previous
+//               sample have released that half
 //   warps 8-11  drain: sum of the two partial accumulators (tcgen05.ld),
 //               output rows through a shared staging block, one bulk store
 //   warp 12, 13 lane 0: MMA issuers, K-half 0 / 1, each into its own partial
@@ -329,9 +326,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   unsigned char* sA = base;                                   // 128 x Kp : Kp * 256 B
   unsigned char* sB = sA + (size_t)Kp * 256;                  // NS quarter slots
   T* stg = reinterpret_cast<T*>(sB + (size_t)NS * qbytes);    // output staging area
-  float* s_z = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(stg) + a.stage_bytes);
-  float* s_gw = s_z + 2 * Kp;
-  TcBars* bars = reinterpret_cast<TcBars*>(s_gw + KMAX);
+  TcBars* bars = reinterpret_cast<TcBars*>(reinterpret_cast<unsigned char*>(stg) + a.stage_bytes);
   volatile int* abort = &bars->abort;
   const uint64_t wlim = a.wait_ns;
 
@@ -381,12 +376,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   uint32_t chp[KH];                                           // channel << 17 | byte offset in A
   float ln2[KH];
   float mx2 = -INFINITY;
-  // gate weights of this thread's supports in registers (k <= 32), else
-  // read from shared memory per sample
-  constexpr bool kGwReg = KMAX <= 32;
-  float gwr[kGwReg ? KH : 1];
-  constexpr int ZPT = 512 / WT;                               // z values per weight thread (C <= 512)
-  float zr[ZPT];
+  float t_next = 1.0f;                                        // this row's temperature, one sample ahead
   if (tid < WT) {
 #pragma unroll
     for (int jj = 0; jj < KH; ++jj) {
@@ -400,17 +390,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         ln2[jj] = a.ln[o] * 1.4426950408889634f;            // log2(e)
         mx2 = nan_max(mx2, ln2[jj]);
       }
-      if constexpr (kGwReg) gwr[jj] = (j < k) ? a.gate_w[j] : 0.0f;
     }
-    grid_dep_wait();                                          // z comes from pass 1 (see above)
-#pragma unroll
-    for (int u = 0; u < ZPT; ++u) {
-      const int c = tid + u * WT;
-      zr[u] = (nb > 0 && c < C) ? a.z[(size_t)b0 * C + c] : 0.0f;
-    }
+    grid_dep_wait();                                          // T comes from the temperature kernel (see above)
+    if (nb > 0 && w_row) t_next = a.T[(size_t)b0 * E_r + e0 + row];
   }
   for (int q = tid; q < Kp * 256 / 16; q += blockDim.x) reinterpret_cast<int4*>(sA)[q] = make_int4(0, 0, 0, 0);
-  for (int i = tid; i < k; i += blockDim.x) s_gw[i] = a.gate_w[i];
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&bars->tmem)),
                  "r"(a.tmem_cols));
@@ -520,29 +504,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     // recomputed per half to stay within the register budget
     constexpr bool kKeepW = KMAX <= 32;
     if constexpr (!kW1) mx2 = nan_max(mx2, __shfl_xor_sync(kFull, mx2, 1));
-    const float bias = a.gate_b[0];
     bool ok = true;
     for (int i = 0; i < nb && ok; ++i) {
       const int b = b0 + i;
-      float* szb = s_z + (i & 1) * Kp;
-#pragma unroll
-      for (int u = 0; u < ZPT; ++u)
-        if (tid + u * WT < C) szb[tid + u * WT] = zr[u];
-      role_sync(kBarWeights, WT);
-      if (i + 1 < nb) {
-#pragma unroll
-        for (int u = 0; u < ZPT; ++u) {
-          const int c = tid + u * WT;
-          if (c < C) zr[u] = a.z[(size_t)(b + 1) * C + c];
-        }
-      }
-      float gp = 0.0f;
-#pragma unroll
-      for (int jj = 0; jj < KH; ++jj)
-        if (part * KH + jj < k && has_row) gp += (kGwReg ? gwr[jj] : s_gw[part * KH + jj]) * szb[chp[jj] >> 17];
-      const float g = bias + gp + (kW1 ? 0.0f : __shfl_xor_sync(kFull, gp, 1));
-      const float t = temperature(g, a.tmin_tau, a.trange_tau, nullptr);
-      if (a.T_out && has_row && part == 0) a.T_out[(size_t)b * E_r + e] = t;
+      // this sample's temperature (MoCE.py:216-218, computed between the
+      // passes), the next one's load in flight behind the softmax and stores
+      const float t = t_next;
+      if (i + 1 < nb && has_row) t_next = a.T[(size_t)(b + 1) * E_r + e];
       const float it = 1.0f / t;
       const float m2 = mx2 * it;
       float wv[kKeepW ? KH : 1];
@@ -884,7 +852,7 @@ TcShape tc_shape(int64_t C, int64_t HW, int64_t k, bool y_aligned, int np_max) {
   t.tmem_cols = cols;
   t.KMAX = k <= 16 ? 16 : k <= 32 ? 32 : 64;
   t.qbytes = (size_t)t.Kp * t.NA * 32;
-  const size_t base = 1024 + (size_t)t.Kp * 256 + (size_t)t.Kp * 8 + (size_t)t.KMAX * 4 + sizeof(TcBars);
+  const size_t base = 1024 + (size_t)t.Kp * 256 + sizeof(TcBars);
   const size_t smem_max = (size_t)smem_optin_tc();
   auto slots = [&](size_t stage) -> int {
     const size_t f = base + stage;
@@ -972,9 +940,8 @@ extern "C" size_t moce_tc_stage_bytes(int64_t B, int64_t C, int64_t HW) {
   return (size_t)B * (size_t)NT * (size_t)((C + 63) / 64 * 64) * (size_t)NA * 128;
 }
 
-static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
-                         const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
-                         const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out, void* stream,
+static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* T,
+                         const int32_t* idx, const float* ln, int64_t E_r, int64_t k, void* y, void* stream,
                          bool dependent, OutEpilogue ep);
 
 // bound of the kernel's waits on another role, taken at each launch
@@ -984,57 +951,77 @@ extern "C" int64_t moce_tc_wait_limit_ns(int64_t ns) {
   return (int64_t)(ns > 0 ? g_wait_ns.exchange((long long)ns) : g_wait_ns.load());
 }
 
-extern "C" int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
-                           const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
-                           const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out,
-                           void* stream) {
-  return mix_tc_launch(xstage, dtype, B, C, HW, z, idx, ln, E_r, k, gate_w, gate_b, tmin_tau, trange_tau, y, T_out,
-                       stream, false, OutEpilogue{nullptr, nullptr, 0});
+extern "C" int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* T,
+                           const int32_t* idx, const float* ln, int64_t E_r, int64_t k, void* y, void* stream) {
+  return mix_tc_launch(xstage, dtype, B, C, HW, T, idx, ln, E_r, k, y, stream, false, OutEpilogue{nullptr, nullptr, 0});
 }
 
 namespace moce {
 int pool_stage_run(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
                    const int32_t* meta, float* z, void* y, int64_t E_r, void* xstage, OutEpilogue ep, void* stream);
+int temperature_run(const float* z, int64_t B, int64_t C, const int32_t* idx, int64_t E_r, int64_t k,
+                    const float* gate_w, const float* gate_b, float tmin_tau, float trange_tau, float* T,
+                    void* stream, bool dependent);                                            // gate.cu
+int temperature_mlp_run(const float* z, int64_t B, int64_t C, int64_t Hd, int64_t E_r, const float* w1,
+                        const float* b1, const float* w2, const float* b2, float tmin_tau, float trange_tau,
+                        float* h, float* T, void* stream, bool dependent);                    // gate.cu
 }
 
+// The three launches of the tensor-core forward, each a programmatic
+// dependent of the one before (its prologue overlaps the previous kernel's
+// tail; griddepcontrol.wait orders its reads after that kernel's writes):
+// pass 1 (pool, residual, operand staging) -> temperatures -> pass 2 (mix).
 static int forward_tc_run(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
                           const int32_t* meta, const int32_t* idx, const float* ln, int64_t E_r, int64_t k,
                           const float* gate_w, const float* gate_b, float tmin_tau, float trange_tau, float* z,
-                          void* xstage, void* y, float* T_out, OutEpilogue ep, void* stream) {
+                          void* xstage, void* y, float* T, OutEpilogue ep, void* stream) {
   if (B == 0) return MOCE_OK;
+  MOCE_REQUIRE(T, MOCE_ERR_INVALID, "moce_forward_tc: T (fp32 [B, E_r]) is required");
   int rc = pool_stage_run(x, dtype, B, C, HW, mask, meta, z, y, E_r, xstage, ep, stream);
   if (rc) return rc;
-  // pass 2 as a programmatic dependent of pass 1: its prologue (A zeroing,
-  // tensor-memory allocation, route loads) overlaps pass 1's tail
-  return mix_tc_launch(xstage, dtype, B, C, HW, z, idx, ln, E_r, k, gate_w, gate_b, tmin_tau, trange_tau, y, T_out,
-                       stream, true, ep);
+  rc = temperature_run(z, B, C, idx, E_r, k, gate_w, gate_b, tmin_tau, trange_tau, T, stream, true);
+  if (rc) return rc;
+  return mix_tc_launch(xstage, dtype, B, C, HW, T, idx, ln, E_r, k, y, stream, true, ep);
 }
 
 extern "C" int moce_forward_tc(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
                                const int32_t* meta, const int32_t* idx, const float* ln, int64_t E_r, int64_t k,
                                const float* gate_w, const float* gate_b, float tmin_tau, float trange_tau, float* z,
-                               void* xstage, void* y, float* T_out, void* stream) {
+                               void* xstage, void* y, float* T, void* stream) {
   return forward_tc_run(x, dtype, B, C, HW, mask, meta, idx, ln, E_r, k, gate_w, gate_b, tmin_tau, trange_tau, z,
-                        xstage, y, T_out, OutEpilogue{nullptr, nullptr, 0}, stream);
+                        xstage, y, T, OutEpilogue{nullptr, nullptr, 0}, stream);
 }
 
 extern "C" int moce_forward_tc_ep(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
                                   const int32_t* meta, const int32_t* idx, const float* ln, int64_t E_r, int64_t k,
                                   const float* gate_w, const float* gate_b, float tmin_tau, float trange_tau,
                                   const float* out_scale, const float* out_shift, int out_relu, float* z,
-                                  void* xstage, void* y, float* T_out, void* stream) {
+                                  void* xstage, void* y, float* T, void* stream) {
   MOCE_REQUIRE(out_scale && out_shift, MOCE_ERR_INVALID, "moce_forward_tc_ep: null scale or shift");
   return forward_tc_run(x, dtype, B, C, HW, mask, meta, idx, ln, E_r, k, gate_w, gate_b, tmin_tau, trange_tau, z,
-                        xstage, y, T_out, OutEpilogue{out_scale, out_shift, out_relu ? 1 : 0}, stream);
+                        xstage, y, T, OutEpilogue{out_scale, out_shift, out_relu ? 1 : 0}, stream);
 }
 
-static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
-                         const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
-                         const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out, void* stream,
+extern "C" int moce_forward_tc_mlp(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
+                                   const int32_t* meta, const int32_t* idx, const float* ln, int64_t E_r, int64_t k,
+                                   int64_t Hd, const float* w1, const float* b1, const float* w2, const float* b2,
+                                   float tmin_tau, float trange_tau, float* z, float* h, void* xstage, void* y,
+                                   float* T, void* stream) {
+  if (B == 0) return MOCE_OK;
+  MOCE_REQUIRE(T, MOCE_ERR_INVALID, "moce_forward_tc_mlp: T (fp32 [B, E_r]) is required");
+  int rc = pool_stage_run(x, dtype, B, C, HW, mask, meta, z, y, E_r, xstage, OutEpilogue{nullptr, nullptr, 0},
+                          stream);
+  if (rc) return rc;
+  rc = temperature_mlp_run(z, B, C, Hd, E_r, w1, b1, w2, b2, tmin_tau, trange_tau, h, T, stream, true);
+  if (rc) return rc;
+  return mix_tc_launch(xstage, dtype, B, C, HW, T, idx, ln, E_r, k, y, stream, true, OutEpilogue{nullptr, nullptr, 0});
+}
+
+static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* T,
+                         const int32_t* idx, const float* ln, int64_t E_r, int64_t k, void* y, void* stream,
                          bool dependent, OutEpilogue ep) {
   if (B == 0) return MOCE_OK;
-  MOCE_REQUIRE(xstage && z && idx && ln && gate_w && gate_b && y, MOCE_ERR_INVALID,
-               "moce_mix_tc: null pointer argument");
+  MOCE_REQUIRE(xstage && T && idx && ln && y, MOCE_ERR_INVALID, "moce_mix_tc: null pointer argument");
   MOCE_REQUIRE(B > 0 && C >= 1 && HW >= 1 && E_r >= 1 && k >= 1 && k <= C, MOCE_ERR_INVALID,
                "moce_mix_tc: invalid shape");
   MOCE_REQUIRE(tc_supported(dtype, C, HW, k), MOCE_ERR_UNSUPPORTED,
@@ -1051,7 +1038,7 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
   int n_bsplit = num_sms() / n_tiles;
   if (n_bsplit < 1) n_bsplit = 1;
   if (n_bsplit > B) n_bsplit = (int)B;
-  TcArgs a{xstage, y, z, idx, ln, gate_w, gate_b, T_out, tmin_tau, trange_tau,
+  TcArgs a{xstage, y, T, idx, ln,
            (int)B, (int)C, (int)HW, (int)E_r, (int)k, Kp, n_tiles, n_bsplit, ns, sh.NP, sh.NA, sh.P, sh.NT,
            sh.tmem_cols, (unsigned long long)g_wait_ns.load(), sh.drain, sh.stg_pitch, sh.nsb, sh.stage_bytes, ep};
   return dispatch_dtype(dtype, [&](auto tag) {

@@ -460,13 +460,13 @@ std::vector<torch::Tensor> forward_tc(torch::Tensor x, torch::Tensor idx, torch:
     y = torch::empty({d.B, d.E_r + 1, d.H, d.W}, x.options());
   }
   auto z = f32_opts_like(x, {d.B, d.C});
-  auto T = want_T ? f32_opts_like(x, {d.B, d.E_r}) : f32_opts_like(x, {0});
+  auto T = f32_opts_like(x, {d.B, d.E_r});      // the mix reads it (returned when wanted)
   auto xstage = torch::empty({(int64_t)moce_tc_stage_bytes(d.B, d.C, d.HW)}, x.options().dtype(torch::kUInt8));
   ok(moce_forward_tc(x.data_ptr(), dtype_of(x), d.B, d.C, d.HW, mask.data_ptr<int32_t>(), meta.data_ptr<int32_t>(),
                      idx.data_ptr<int32_t>(), ln.data_ptr<float>(), d.E_r, d.K, gate_w.data_ptr<float>(),
                      gate_b.data_ptr<float>(), (float)tmin_tau, (float)trange_tau, z.data_ptr<float>(),
-                     xstage.data_ptr(), y.data_ptr(), want_T ? T.data_ptr<float>() : nullptr, cur_stream()));
-  return {y, z, T};
+                     xstage.data_ptr(), y.data_ptr(), T.data_ptr<float>(), cur_stream()));
+  return {y, z, want_T ? T : f32_opts_like(x, {0})};
 }
 
 // the tensor-core forward with the caller's eval BatchNorm (folded to a
@@ -496,12 +496,13 @@ torch::Tensor forward_tc_ep(torch::Tensor x, torch::Tensor idx, torch::Tensor ln
     y = torch::empty({d.B, d.E_r + 1, d.H, d.W}, x.options());
   }
   auto z = f32_opts_like(x, {d.B, d.C});
+  auto T = f32_opts_like(x, {d.B, d.E_r});
   auto xstage = torch::empty({(int64_t)moce_tc_stage_bytes(d.B, d.C, d.HW)}, x.options().dtype(torch::kUInt8));
   ok(moce_forward_tc_ep(x.data_ptr(), dtype_of(x), d.B, d.C, d.HW, mask.data_ptr<int32_t>(),
                         meta.data_ptr<int32_t>(), idx.data_ptr<int32_t>(), ln.data_ptr<float>(), d.E_r, d.K,
                         gate_w.data_ptr<float>(), gate_b.data_ptr<float>(), (float)tmin_tau, (float)trange_tau,
                         out_scale.data_ptr<float>(), out_shift.data_ptr<float>(), relu ? 1 : 0, z.data_ptr<float>(),
-                        xstage.data_ptr(), y.data_ptr(), nullptr, cur_stream()));
+                        xstage.data_ptr(), y.data_ptr(), T.data_ptr<float>(), cur_stream()));
   return y;
 }
 
@@ -577,6 +578,208 @@ std::vector<torch::Tensor> forward_gx(torch::Tensor x, torch::Tensor idx, torch:
   return {y, z, T};
 }
 
+// ------------------------------------------------------- two-layer gate
+
+void check_mlp(const torch::Tensor& z, const torch::Tensor& w1, const torch::Tensor& b1, const torch::Tensor& w2,
+               const torch::Tensor& b2, int64_t C, int64_t E_r) {
+  for (const torch::Tensor* t : {&z, &w1, &b1, &w2, &b2}) {
+    CHECK_INPUT(*t);
+    TORCH_CHECK(t->scalar_type() == torch::kFloat32, "two-layer gate tensors must be float32");
+    TORCH_CHECK(t->device() == z.device(), "all tensors must be on one device");
+  }
+  TORCH_CHECK(w1.dim() == 2 && w1.size(1) == C, "w1 must be (Hd, C)");
+  const int64_t Hd = w1.size(0);
+  TORCH_CHECK(b1.numel() == Hd && w2.dim() == 2 && w2.size(0) == E_r && w2.size(1) == Hd && b2.numel() == E_r,
+              "b1 (Hd), w2 (E_r, Hd), b2 (E_r) expected");
+}
+
+// temperatures of the two-layer gate from pooled means z [B, C]: (T, h)
+std::vector<torch::Tensor> temperature_mlp(torch::Tensor z, torch::Tensor w1, torch::Tensor b1, torch::Tensor w2,
+                                           torch::Tensor b2, double tmin_tau, double trange_tau) {
+  TORCH_CHECK(z.dim() == 2, "z must be (B, C)");
+  const c10::cuda::CUDAGuard guard(z.device());
+  const int64_t B = z.size(0), C = z.size(1), E_r = w2.size(0), Hd = w1.size(0);
+  check_mlp(z, w1, b1, w2, b2, C, E_r);
+  auto T = f32_opts_like(z, {B, E_r});
+  auto h = f32_opts_like(z, {B, Hd});
+  ok(moce_temperature_mlp(z.data_ptr<float>(), B, C, Hd, E_r, w1.data_ptr<float>(), b1.data_ptr<float>(),
+                          w2.data_ptr<float>(), b2.data_ptr<float>(), (float)tmin_tau, (float)trange_tau,
+                          h.data_ptr<float>(), T.data_ptr<float>(), cur_stream()));
+  return {T, h};
+}
+
+// temperatures of the shared Linear(k,1) gate from pooled means z [B, C]
+torch::Tensor temperature(torch::Tensor z, torch::Tensor idx, torch::Tensor gate_w, torch::Tensor gate_b,
+                          double tmin_tau, double trange_tau) {
+  for (auto* t : {&z, &idx, &gate_w, &gate_b}) {
+    CHECK_INPUT(*t);
+    TORCH_CHECK(t->device() == z.device(), "all tensors must be on one device");
+  }
+  TORCH_CHECK(z.dim() == 2 && idx.dim() == 2 && idx.scalar_type() == torch::kInt32 &&
+                  z.scalar_type() == torch::kFloat32, "z float32 (B, C), idx int32 (E_r, k)");
+  TORCH_CHECK(gate_w.numel() == idx.size(1) && gate_b.numel() >= 1 && gate_w.scalar_type() == torch::kFloat32 &&
+                  gate_b.scalar_type() == torch::kFloat32, "gate shape mismatch");
+  const c10::cuda::CUDAGuard guard(z.device());
+  auto T = f32_opts_like(z, {z.size(0), idx.size(0)});
+  ok(moce_temperature(z.data_ptr<float>(), z.size(0), z.size(1), idx.data_ptr<int32_t>(), idx.size(0), idx.size(1),
+                      gate_w.data_ptr<float>(), gate_b.data_ptr<float>(), (float)tmin_tau, (float)trange_tau,
+                      T.data_ptr<float>(), cur_stream()));
+  return T;
+}
+
+// tensor-core forward with the two-layer gate: (y, z, T, h)
+std::vector<torch::Tensor> forward_tc_mlp(torch::Tensor x, torch::Tensor idx, torch::Tensor ln, torch::Tensor mask,
+                                          torch::Tensor meta, torch::Tensor w1, torch::Tensor b1, torch::Tensor w2,
+                                          torch::Tensor b2, double tmin_tau, double trange_tau,
+                                          c10::optional<torch::Tensor> out_opt) {
+  for (auto* t : {&x, &idx, &ln, &mask, &meta}) {
+    CHECK_INPUT(*t);
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  Dims d = dims(x, idx);
+  TORCH_CHECK(idx.scalar_type() == torch::kInt32 && ln.scalar_type() == torch::kFloat32 && ln.numel() == d.E_r * d.K &&
+                  mask.numel() == d.C && meta.numel() >= 2, "route tensors do not match x");
+  auto z = f32_opts_like(x, {d.B, d.C});
+  check_mlp(z, w1, b1, w2, b2, d.C, d.E_r);
+  torch::Tensor y;
+  if (out_opt.has_value()) {
+    y = *out_opt;
+    CHECK_INPUT(y);
+    TORCH_CHECK(y.scalar_type() == x.scalar_type() && y.numel() == d.B * (d.E_r + 1) * d.HW, "out mismatch");
+  } else {
+    y = torch::empty({d.B, d.E_r + 1, d.H, d.W}, x.options());
+  }
+  const int64_t Hd = w1.size(0);
+  auto T = f32_opts_like(x, {d.B, d.E_r});
+  auto h = f32_opts_like(x, {d.B, Hd});
+  auto xstage = torch::empty({(int64_t)moce_tc_stage_bytes(d.B, d.C, d.HW)}, x.options().dtype(torch::kUInt8));
+  ok(moce_forward_tc_mlp(x.data_ptr(), dtype_of(x), d.B, d.C, d.HW, mask.data_ptr<int32_t>(),
+                         meta.data_ptr<int32_t>(), idx.data_ptr<int32_t>(), ln.data_ptr<float>(), d.E_r, d.K, Hd,
+                         w1.data_ptr<float>(), b1.data_ptr<float>(), w2.data_ptr<float>(), b2.data_ptr<float>(),
+                         (float)tmin_tau, (float)trange_tau, z.data_ptr<float>(), h.data_ptr<float>(),
+                         xstage.data_ptr(), y.data_ptr(), T.data_ptr<float>(), cur_stream()));
+  return {y, z, T, h};
+}
+
+// pass 1 of the CUDA-core paths: (y with the residual row written, z)
+std::vector<torch::Tensor> pool_residual(torch::Tensor x, torch::Tensor mask, torch::Tensor meta, int64_t E_r,
+                                         c10::optional<torch::Tensor> out_opt) {
+  for (auto* t : {&x, &mask, &meta}) {
+    CHECK_INPUT(*t);
+    TORCH_CHECK(t->device() == x.device(), "all tensors must be on one device");
+  }
+  TORCH_CHECK(x.dim() == 4 && mask.numel() == x.size(1) && meta.numel() >= 2 && mask.scalar_type() == torch::kInt32 &&
+                  meta.scalar_type() == torch::kInt32, "x (B, C, H, W), mask int32 [C], meta int32 [2]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t B = x.size(0), C = x.size(1), H = x.size(2), W = x.size(3);
+  torch::Tensor y;
+  if (out_opt.has_value()) {
+    y = *out_opt;
+    CHECK_INPUT(y);
+    TORCH_CHECK(y.scalar_type() == x.scalar_type() && y.numel() == B * (E_r + 1) * H * W, "out mismatch");
+  } else {
+    y = torch::empty({B, E_r + 1, H, W}, x.options());
+  }
+  auto z = f32_opts_like(x, {B, C});
+  ok(moce_pool_residual(x.data_ptr(), dtype_of(x), B, C, H * W, mask.data_ptr<int32_t>(), meta.data_ptr<int32_t>(),
+                        z.data_ptr<float>(), y.data_ptr(), E_r, cur_stream()));
+  return {y, z};
+}
+
+// the routed experts of y from given temperatures T [B, E_r]: the
+// lanes-over-pixels mix, the global-memory mix, or the general mix (which
+// also rewrites the residual row), by shape
+void mix_given_t(torch::Tensor x, torch::Tensor idx, torch::Tensor ln, torch::Tensor mask, torch::Tensor T,
+                 torch::Tensor y) {
+  for (auto* t : {&x, &idx, &ln, &mask, &T, &y}) {
+    CHECK_INPUT(*t);
+    TORCH_CHECK(t->device() == x.device(), "all tensors must be on one device");
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  Dims d = dims(x, idx);
+  TORCH_CHECK(idx.scalar_type() == torch::kInt32 && ln.scalar_type() == torch::kFloat32 && ln.numel() == d.E_r * d.K &&
+                  mask.numel() == d.C && T.scalar_type() == torch::kFloat32 && T.numel() == d.B * d.E_r,
+              "route tensors or T do not match x");
+  TORCH_CHECK(y.scalar_type() == x.scalar_type() && y.numel() == d.B * (d.E_r + 1) * d.HW, "out mismatch");
+  const int dt = dtype_of(x);
+  if (moce_px_supported(dt, d.C, d.HW, d.K)) {
+    ok(moce_mix_px_t(x.data_ptr(), dt, d.B, d.C, d.HW, T.data_ptr<float>(), idx.data_ptr<int32_t>(),
+                     ln.data_ptr<float>(), d.E_r, d.K, y.data_ptr(), cur_stream()));
+  } else if (moce_gx_supported(dt, d.C, d.HW, d.K)) {
+    ok(moce_mix_gx_t(x.data_ptr(), dt, d.B, d.C, d.HW, T.data_ptr<float>(), idx.data_ptr<int32_t>(),
+                     ln.data_ptr<float>(), d.E_r, d.K, y.data_ptr(), cur_stream()));
+  } else {
+    ok(moce_mix(x.data_ptr(), dt, d.B, d.C, d.HW, idx.data_ptr<int32_t>(), ln.data_ptr<float>(),
+                T.data_ptr<float>(), d.E_r, d.K, mask.data_ptr<int32_t>(), y.data_ptr(), cur_stream()));
+  }
+}
+
+// pass 1 and the mix from given temperatures T [B, E_r]: the tensor-core
+// path (operand staging, tcgen05 mix) where it takes the input, else the
+// CUDA-core pass 1 and mix_given_t; returns y
+torch::Tensor forward_given_t(torch::Tensor x, torch::Tensor idx, torch::Tensor ln, torch::Tensor mask,
+                              torch::Tensor meta, torch::Tensor T, c10::optional<torch::Tensor> out_opt) {
+  for (auto* t : {&x, &idx, &ln, &mask, &meta, &T}) {
+    CHECK_INPUT(*t);
+    TORCH_CHECK(t->device() == x.device(), "all tensors must be on one device");
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  Dims d = dims(x, idx);
+  TORCH_CHECK(idx.scalar_type() == torch::kInt32 && ln.scalar_type() == torch::kFloat32 && ln.numel() == d.E_r * d.K &&
+                  mask.numel() == d.C && meta.numel() >= 2 && T.scalar_type() == torch::kFloat32 &&
+                  T.numel() == d.B * d.E_r, "route tensors or T do not match x");
+  torch::Tensor y;
+  if (out_opt.has_value()) {
+    y = *out_opt;
+    CHECK_INPUT(y);
+    TORCH_CHECK(y.scalar_type() == x.scalar_type() && y.numel() == d.B * (d.E_r + 1) * d.HW, "out mismatch");
+  } else {
+    y = torch::empty({d.B, d.E_r + 1, d.H, d.W}, x.options());
+  }
+  auto z = f32_opts_like(x, {d.B, d.C});
+  const int dt = dtype_of(x);
+  if (tc_supported(x, d.K)) {
+    auto xstage = torch::empty({(int64_t)moce_tc_stage_bytes(d.B, d.C, d.HW)}, x.options().dtype(torch::kUInt8));
+    ok(moce_pool_stage(x.data_ptr(), dt, d.B, d.C, d.HW, mask.data_ptr<int32_t>(), meta.data_ptr<int32_t>(),
+                       z.data_ptr<float>(), y.data_ptr(), d.E_r, xstage.data_ptr(), cur_stream()));
+    ok(moce_mix_tc(xstage.data_ptr(), dt, d.B, d.C, d.HW, T.data_ptr<float>(), idx.data_ptr<int32_t>(),
+                   ln.data_ptr<float>(), d.E_r, d.K, y.data_ptr(), cur_stream()));
+  } else {
+    ok(moce_pool_residual(x.data_ptr(), dt, d.B, d.C, d.HW, mask.data_ptr<int32_t>(), meta.data_ptr<int32_t>(),
+                          z.data_ptr<float>(), y.data_ptr(), d.E_r, cur_stream()));
+    mix_given_t(x, idx, ln, mask, T, y);
+  }
+  return y;
+}
+
+// backward from given temperatures: (dx, dL, dT)
+std::vector<torch::Tensor> backward_t(torch::Tensor x, torch::Tensor dy, torch::Tensor logits, torch::Tensor idx,
+                                      torch::Tensor ln, torch::Tensor mask, torch::Tensor meta, torch::Tensor toff,
+                                      torch::Tensor tslot, torch::Tensor T) {
+  for (auto* t : {&x, &dy, &logits, &idx, &ln, &mask, &meta, &toff, &tslot, &T}) {
+    CHECK_INPUT(*t);
+    TORCH_CHECK(t->device() == x.device(), "all tensors must be on one device");
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  Dims d = dims(x, idx);
+  TORCH_CHECK(dy.scalar_type() == x.scalar_type() && dy.numel() == d.B * (d.E_r + 1) * d.HW, "dy must be (B, E, H, W)");
+  TORCH_CHECK(toff.numel() == d.C + 1 && tslot.numel() == d.E_r * d.K, "transposed lists missing");
+  TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.numel() == d.E_r * d.C && T.numel() == d.B * d.E_r &&
+                  T.scalar_type() == torch::kFloat32 && ln.numel() == d.E_r * d.K && mask.numel() == d.C,
+              "shape mismatch");
+  auto dx = torch::empty_like(x);
+  auto dL = f32_opts_like(x, {d.E_r, d.C});
+  auto dT = f32_opts_like(x, {d.B, d.E_r});
+  const size_t nb = moce_backward_workspace_bytes(d.B, d.C, d.HW, d.E_r, d.K);
+  auto ws = torch::empty({(int64_t)nb + 256}, x.options().dtype(torch::kUInt8));
+  void* wp = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(ws.data_ptr()) + 255) & ~uintptr_t(255));
+  ok(moce_backward_t(x.data_ptr(), dy.data_ptr(), dtype_of(x), d.B, d.C, d.HW, logits.data_ptr<float>(),
+                     idx.data_ptr<int32_t>(), ln.data_ptr<float>(), mask.data_ptr<int32_t>(), meta.data_ptr<int32_t>(),
+                     toff.data_ptr<int32_t>(), tslot.data_ptr<int32_t>(), d.E_r, d.K, T.data_ptr<float>(),
+                     dx.data_ptr(), dL.data_ptr<float>(), dT.data_ptr<float>(), wp, nb, cur_stream()));
+  return {dx, dL, dT};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -625,6 +828,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("gate_b"), py::arg("tmin_tau"), py::arg("trange_tau"), py::arg("want_T") = false,
         py::arg("out") = py::none());
   m.def("version", []() { return std::string(moce_version()); });
+  m.def("temperature", &temperature, "Linear-gate temperatures T [B, E_r] from pooled means z [B, C]");
+  m.def("temperature_mlp", &temperature_mlp, "Two-layer-gate temperatures from pooled means: (T, h)");
+  m.def("forward_tc_mlp", &forward_tc_mlp, "Tensor-core forward with the two-layer gate: (y, z, T, h)",
+        py::arg("x"), py::arg("idx"), py::arg("ln"), py::arg("mask"), py::arg("meta"), py::arg("w1"), py::arg("b1"),
+        py::arg("w2"), py::arg("b2"), py::arg("tmin_tau"), py::arg("trange_tau"), py::arg("out") = py::none());
+  m.def("pool_residual", &pool_residual, "Pass 1 of the CUDA-core paths: (y with the residual row, z)",
+        py::arg("x"), py::arg("mask"), py::arg("meta"), py::arg("E_r"), py::arg("out") = py::none());
+  m.def("mix_given_t", &mix_given_t, "Routed experts of y from given temperatures (CUDA-core mix)");
+  m.def("forward_given_t", &forward_given_t, "Pass 1 and the mix from given temperatures: y", py::arg("x"),
+        py::arg("idx"), py::arg("ln"), py::arg("mask"), py::arg("meta"), py::arg("T"), py::arg("out") = py::none());
+  m.def("backward_t", &backward_t, "Backward from given temperatures: (dx, dL, dT)");
   m.def("tc_fault", [](bool clear) {
     int flag = 0;
     ok(moce_tc_fault(&flag, clear ? 1 : 0));

@@ -37,6 +37,7 @@ struct PxArgs {
   const float* gate_b;
   float* T_out;
   float tmin_tau, trange_tau;
+  const float* T_in;              // given temperatures [B, E_r] (z and the gate unused), or null
   int B, C, HW, HWp, E_r, k;
   int vec_out;                    // Y rows allow 4-element vector stores
   int vec_in;                     // X rows allow 4-element vector loads (global-memory kernel)
@@ -64,8 +65,10 @@ __global__ void __launch_bounds__(px_threads(NSLAB), 1) mix_px_kernel(PxArgs a) 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const T* xg = static_cast<const T*>(a.x);
   px_stage_rows<T>(s_x, xg + ((size_t)b * C + cs0) * HW, chn, HW, HWp);
-  for (int c = threadIdx.x; c < C; c += kPxThreads) s_z[c] = a.z[(size_t)b * C + c];
-  for (int i = threadIdx.x; i < k; i += kPxThreads) s_gw[i] = a.gate_w[i];
+  if (!a.T_in) {
+    for (int c = threadIdx.x; c < C; c += kPxThreads) s_z[c] = a.z[(size_t)b * C + c];
+    for (int i = threadIdx.x; i < k; i += kPxThreads) s_gw[i] = a.gate_w[i];
+  }
   __syncthreads();
   const T* s_peer = nullptr;
   if constexpr (CL > 1) {
@@ -73,7 +76,7 @@ __global__ void __launch_bounds__(px_threads(NSLAB), 1) mix_px_kernel(PxArgs a) 
     cluster.sync();                                     // both halves staged
     s_peer = cluster.map_shared_rank(s_x, rank ^ 1);
   }
-  const float bias = a.gate_b[0];
+  const float bias = a.T_in ? 0.0f : a.gate_b[0];
   const int per = (E_r + nch - 1) / nch;
   const int e0 = ch * per, e1 = min(E_r, e0 + per);
   const int E = E_r + 1;
@@ -105,11 +108,11 @@ __global__ void __launch_bounds__(px_threads(NSLAB), 1) mix_px_kernel(PxArgs a) 
 #pragma unroll
     for (int q = 0; q < KL; ++q) {
       const int i = lane + 32 * q;
-      if (i < k) gp += s_gw[i] * s_z[c_l[q]];
-      else u_l[q] = -INFINITY;
+      if (i >= k) u_l[q] = -INFINITY;
+      else if (!a.T_in) gp += s_gw[i] * s_z[c_l[q]];
     }
     const float g = warp_sum(gp) + bias;
-    const float t = temperature(g, a.tmin_tau, a.trange_tau, nullptr);
+    const float t = a.T_in ? a.T_in[(size_t)b * E_r + e] : temperature(g, a.tmin_tau, a.trange_tau, nullptr);
     if (a.T_out && lane == 0) a.T_out[(size_t)b * E_r + e] = t;
     float m = -INFINITY;
 #pragma unroll
@@ -196,10 +199,12 @@ __global__ void __launch_bounds__(px_threads(1), 1) mix_px_half_kernel(PxArgs a)
   const int hl = lane & 15, hsel = lane >> 4;
   const T* xg = static_cast<const T*>(a.x);
   px_stage_rows<T>(s_x, xg + (size_t)b * C * HW, C, HW, HWp);
-  for (int c = threadIdx.x; c < C; c += kPxThreads) s_z[c] = a.z[(size_t)b * C + c];
-  for (int i = threadIdx.x; i < k; i += kPxThreads) s_gw[i] = a.gate_w[i];
+  if (!a.T_in) {
+    for (int c = threadIdx.x; c < C; c += kPxThreads) s_z[c] = a.z[(size_t)b * C + c];
+    for (int i = threadIdx.x; i < k; i += kPxThreads) s_gw[i] = a.gate_w[i];
+  }
   __syncthreads();
-  const float bias = a.gate_b[0];
+  const float bias = a.T_in ? 0.0f : a.gate_b[0];
   const int per = (E_r + nch - 1) / nch;
   const int e0 = ch * per, e1 = min(E_r, e0 + per);
   const int E = E_r + 1;
@@ -219,11 +224,12 @@ __global__ void __launch_bounds__(px_threads(1), 1) mix_px_half_kernel(PxArgs a)
     float gp = 0.0f;
 #pragma unroll
     for (int q = 0; q < KL16; ++q)
-      if (hl + 16 * q < k) gp += s_gw[hl + 16 * q] * s_z[c_l[q]];
+      if (hl + 16 * q < k && !a.T_in) gp += s_gw[hl + 16 * q] * s_z[c_l[q]];
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) gp += __shfl_xor_sync(kFull, gp, o);
     const float g = gp + bias;
-    const float t = temperature(g, a.tmin_tau, a.trange_tau, nullptr);
+    const float t = a.T_in ? (ve ? a.T_in[(size_t)b * E_r + e] : 1.0f)
+                           : temperature(g, a.tmin_tau, a.trange_tau, nullptr);
     if (a.T_out && ve && hl == 0) a.T_out[(size_t)b * E_r + e] = t;
     float m = -INFINITY;
 #pragma unroll
@@ -290,10 +296,12 @@ __global__ void __launch_bounds__(px_threads(NSLAB), 1) mix_px_grouped_kernel(Px
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const T* xg = static_cast<const T*>(a.x);
   px_stage_rows<T>(s_x, xg + (size_t)b * C * HW, C, HW, HWp);
-  for (int c = threadIdx.x; c < C; c += kPxThreads) s_z[c] = a.z[(size_t)b * C + c];
-  for (int i = threadIdx.x; i < k; i += kPxThreads) s_gw[i] = a.gate_w[i];
+  if (!a.T_in) {
+    for (int c = threadIdx.x; c < C; c += kPxThreads) s_z[c] = a.z[(size_t)b * C + c];
+    for (int i = threadIdx.x; i < k; i += kPxThreads) s_gw[i] = a.gate_w[i];
+  }
   __syncthreads();
-  const float bias = a.gate_b[0];
+  const float bias = a.T_in ? 0.0f : a.gate_b[0];
   const int per = (E_r + nch - 1) / nch;
   const int e0 = ch * per, e1 = min(E_r, e0 + per);
   const int E = E_r + 1;
@@ -317,8 +325,9 @@ __global__ void __launch_bounds__(px_threads(NSLAB), 1) mix_px_grouped_kernel(Px
     float g = 0.0f;
 #pragma unroll
     for (int i = 0; i < KMAX; ++i)
-      if (i < k) g += s_gw[i] * s_z[cr[i]];
-    const float t = temperature(g + bias, a.tmin_tau, a.trange_tau, nullptr);
+      if (i < k && !a.T_in) g += s_gw[i] * s_z[cr[i]];
+    const float t = a.T_in ? (has ? a.T_in[(size_t)b * E_r + em] : 1.0f)
+                           : temperature(g + bias, a.tmin_tau, a.trange_tau, nullptr);
     if (a.T_out && has) a.T_out[(size_t)b * E_r + em] = t;
     float m = -INFINITY;
 #pragma unroll
@@ -393,10 +402,12 @@ __global__ void __launch_bounds__(px_threads(NSLAB), 1) mix_gx_kernel(PxArgs a) 
   const int b = blockIdx.y, ch = blockIdx.x, nch = gridDim.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const T* xb = static_cast<const T*>(a.x) + (size_t)b * C * HW;
-  for (int c = threadIdx.x; c < C; c += kPxThreads) s_z[c] = a.z[(size_t)b * C + c];
-  for (int i = threadIdx.x; i < k; i += kPxThreads) s_gw[i] = a.gate_w[i];
+  if (!a.T_in) {
+    for (int c = threadIdx.x; c < C; c += kPxThreads) s_z[c] = a.z[(size_t)b * C + c];
+    for (int i = threadIdx.x; i < k; i += kPxThreads) s_gw[i] = a.gate_w[i];
+  }
   __syncthreads();
-  const float bias = a.gate_b[0];
+  const float bias = a.T_in ? 0.0f : a.gate_b[0];
   const int per = (E_r + nch - 1) / nch;
   const int e0 = ch * per, e1 = min(E_r, e0 + per);
   const int E = E_r + 1;
@@ -414,9 +425,9 @@ __global__ void __launch_bounds__(px_threads(NSLAB), 1) mix_gx_kernel(PxArgs a) 
     float gp = 0.0f;
 #pragma unroll
     for (int q = 0; q < KL; ++q)
-      if (lane + 32 * q < k) gp += s_gw[lane + 32 * q] * s_z[c_l[q]];
+      if (lane + 32 * q < k && !a.T_in) gp += s_gw[lane + 32 * q] * s_z[c_l[q]];
     const float g = warp_sum(gp) + bias;
-    const float t = temperature(g, a.tmin_tau, a.trange_tau, nullptr);
+    const float t = a.T_in ? a.T_in[(size_t)b * E_r + e] : temperature(g, a.tmin_tau, a.trange_tau, nullptr);
     if (a.T_out && lane == 0) a.T_out[(size_t)b * E_r + e] = t;
     float m = -INFINITY;
 #pragma unroll
@@ -522,12 +533,14 @@ using namespace moce;
 
 extern "C" int moce_px_supported(int dtype, int64_t C, int64_t HW, int64_t k) { return px_supported(dtype, C, HW, k); }
 
-extern "C" int moce_mix_px(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
-                           const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
-                           const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out,
-                           void* stream) {
+// the gate from z and gate_w / gate_b, or (T_in given) the temperatures as given
+static int mix_px_run(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
+                        const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
+                        const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out,
+                        const float* T_in, void* stream) {
   if (B == 0) return MOCE_OK;  // an empty batch is a no-op
-  MOCE_REQUIRE(x && z && idx && ln && gate_w && gate_b && y, MOCE_ERR_INVALID, "moce_mix_px: null pointer argument");
+  MOCE_REQUIRE(x && idx && ln && y && (T_in || (z && gate_w && gate_b)), MOCE_ERR_INVALID,
+               "moce_mix_px: null pointer argument");
   MOCE_REQUIRE(dtype_ok(dtype), MOCE_ERR_INVALID, "moce_mix_px: unknown dtype %d", dtype);
   MOCE_REQUIRE(B > 0 && C >= 1 && HW >= 1 && E_r >= 1 && k >= 1 && k <= C, MOCE_ERR_INVALID,
                "moce_mix_px: invalid shape");
@@ -555,7 +568,7 @@ extern "C" int moce_mix_px(const void* x, int dtype, int64_t B, int64_t C, int64
   const bool grouped = CL == 1 && k <= 16 && per >= 8 * kPxWarps;
   if (grouped && per > 32 * kPxWarps) nch = (E_r + 32 * kPxWarps - 1) / (32 * kPxWarps);
   const int vec = (HW % 4 == 0) && (((uintptr_t)y) % 16 == 0);
-  PxArgs a{x, y, z, idx, ln, gate_w, gate_b, T_out, tmin_tau, trange_tau,
+  PxArgs a{x, y, z, idx, ln, gate_w, gate_b, T_in ? nullptr : T_out, tmin_tau, trange_tau, T_in,
            (int)B, (int)C, (int)HW, HWp, (int)E_r, (int)k, vec, 0, (int)Ch};
   return dispatch_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
@@ -602,12 +615,14 @@ extern "C" int moce_mix_px(const void* x, int dtype, int64_t B, int64_t C, int64
 
 extern "C" int moce_gx_supported(int dtype, int64_t C, int64_t HW, int64_t k) { return gx_supported(dtype, C, HW, k); }
 
-extern "C" int moce_mix_gx(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
-                           const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
-                           const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out,
-                           void* stream) {
+// the gate from z and gate_w / gate_b, or (T_in given) the temperatures as given
+static int mix_gx_run(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
+                        const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
+                        const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out,
+                        const float* T_in, void* stream) {
   if (B == 0) return MOCE_OK;  // an empty batch is a no-op
-  MOCE_REQUIRE(x && z && idx && ln && gate_w && gate_b && y, MOCE_ERR_INVALID, "moce_mix_gx: null pointer argument");
+  MOCE_REQUIRE(x && idx && ln && y && (T_in || (z && gate_w && gate_b)), MOCE_ERR_INVALID,
+               "moce_mix_gx: null pointer argument");
   MOCE_REQUIRE(dtype_ok(dtype), MOCE_ERR_INVALID, "moce_mix_gx: unknown dtype %d", dtype);
   MOCE_REQUIRE(B > 0 && C >= 1 && HW >= 1 && E_r >= 1 && k >= 1 && k <= C, MOCE_ERR_INVALID,
                "moce_mix_gx: invalid shape");
@@ -627,7 +642,7 @@ extern "C" int moce_mix_gx(const void* x, int dtype, int64_t B, int64_t C, int64
   if (nch < 1) nch = 1;
   const int vout = (HW % 4 == 0) && (((uintptr_t)y) % 16 == 0);
   const int vin = (HW % 4 == 0) && (((uintptr_t)x) % (4 * esize) == 0);
-  PxArgs a{x, y, z, idx, ln, gate_w, gate_b, T_out, tmin_tau, trange_tau,
+  PxArgs a{x, y, z, idx, ln, gate_w, gate_b, T_in ? nullptr : T_out, tmin_tau, trange_tau, T_in,
            (int)B, (int)C, (int)HW, (int)HW, (int)E_r, (int)k, vout, vin, (int)C};
   return dispatch_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
@@ -651,4 +666,32 @@ extern "C" int moce_mix_gx(const void* x, int dtype, int64_t B, int64_t C, int64
     kern<<<dim3((unsigned)nch, (unsigned)B), nthr, smem, (cudaStream_t)stream>>>(a);
     return check_launch("mix_gx_kernel");
   });
+}
+
+extern "C" int moce_mix_px(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
+                           const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
+                           const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out,
+                           void* stream) {
+  return mix_px_run(x, dtype, B, C, HW, z, idx, ln, E_r, k, gate_w, gate_b, tmin_tau, trange_tau, y, T_out, nullptr,
+                    stream);
+}
+
+extern "C" int moce_mix_px_t(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const float* T,
+                             const int32_t* idx, const float* ln, int64_t E_r, int64_t k, void* y, void* stream) {
+  MOCE_REQUIRE(T || B == 0, MOCE_ERR_INVALID, "moce_mix_px_t: null T");
+  return mix_px_run(x, dtype, B, C, HW, nullptr, idx, ln, E_r, k, nullptr, nullptr, 0.f, 0.f, y, nullptr, T, stream);
+}
+
+extern "C" int moce_mix_gx(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
+                           const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
+                           const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out,
+                           void* stream) {
+  return mix_gx_run(x, dtype, B, C, HW, z, idx, ln, E_r, k, gate_w, gate_b, tmin_tau, trange_tau, y, T_out, nullptr,
+                    stream);
+}
+
+extern "C" int moce_mix_gx_t(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const float* T,
+                             const int32_t* idx, const float* ln, int64_t E_r, int64_t k, void* y, void* stream) {
+  MOCE_REQUIRE(T || B == 0, MOCE_ERR_INVALID, "moce_mix_gx_t: null T");
+  return mix_gx_run(x, dtype, B, C, HW, nullptr, idx, ln, E_r, k, nullptr, nullptr, 0.f, 0.f, y, nullptr, T, stream);
 }

@@ -143,15 +143,53 @@ class MoCEFunction(torch.autograd.Function):
         return (dx, dL.to(logits.dtype), dgw.reshape(wshape), dgb.reshape(bshape), None, None, None)
 
 
+class MoCEFunctionT(torch.autograd.Function):
+    """Y = MoCE(X; L, T) with the temperatures T [B, E_r] given.
+
+    For a gate the caller differentiates itself (the two-layer gate): the
+    native forward from given temperatures and the native backward, which
+    returns dX (mix and residual terms), dL and dT; autograd carries dT back
+    through the caller's gate (and its dz / H*W term into dX).
+    """
+
+    @staticmethod
+    def forward(ctx, x, logits, T, route):
+        x = x.contiguous()
+        Tc = T.detach().float().contiguous()
+        y = native().forward_given_t(x, route.idx, route.ln, route.mask, route.meta, Tc)
+        if _CHECK_FAULTS:
+            check_faults()
+        ctx.save_for_backward(x, logits.detach(), Tc)
+        ctx.route = route
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, logits, T = ctx.saved_tensors
+        r = ctx.route
+        if r.toff.numel() == 0:
+            raise RuntimeError("MoCEFunctionT: route cache was built without transposed lists")
+        dx, dL, dT = native().backward_t(x, dy.to(x.dtype).contiguous(), logits.float().contiguous(), r.idx, r.ln,
+                                         r.mask, r.meta, r.toff, r.tslot, T)
+        return dx, dL.to(logits.dtype), dT, None
+
+
 class MoCE(nn.Module):
     """Mixture of Channel Experts: E-1 routed experts + 1 residual expert.
 
     Same constructor and attributes as the reference (``MoCE.py:26-79``).
+    ``gate_type="mlp"`` (an addition, off by default) replaces the reference's
+    shared Linear(k,1) temperature gate with a two-layer gate
+    C -> C/16 -> E-1 with ReLU and Kaiming-normal weights, ``gate_mlp``.
     """
 
     def __init__(self, in_channels=256, sampling_factor=4, k=8, tau=1.0, balance_weight=0.05,
-                 specialization_weight=0.1, diversity_weight=0.01, temp_min=0.2, temp_max=5.0):
+                 specialization_weight=0.1, diversity_weight=0.01, temp_min=0.2, temp_max=5.0,
+                 gate_type="linear"):
         super().__init__()
+        if gate_type not in ("linear", "mlp"):
+            raise ValueError("gate_type must be 'linear' or 'mlp'")
+        self.gate_type = gate_type
         self.in_channels = in_channels
         self.num_experts = in_channels // sampling_factor
         self.k = k
@@ -177,6 +215,24 @@ class MoCE(nn.Module):
         self.cached_gate_weight = None
         self.cached_gate_bias = None
         self._route = None        # native eval cache (int32 supports etc.)
+        if gate_type == "mlp":
+            self.reset_gate_mlp()
+
+    def reset_gate_mlp(self):
+        """(Re)create the two-layer gate for the current ``in_channels`` and
+        ``num_experts`` (call it after changing ``num_experts``): Linear(C,
+        C/16) -> ReLU -> Linear(C/16, E-1), weights Kaiming-normal (ReLU
+        gain), biases zero, on the device of ``routing_logits``."""
+        hd = max(1, self.in_channels // 16)
+        mlp = nn.Sequential(nn.Linear(self.in_channels, hd), nn.ReLU(), nn.Linear(hd, self.num_experts - 1))
+        for lin in (mlp[0], mlp[2]):
+            nn.init.kaiming_normal_(lin.weight, nonlinearity="relu")
+            nn.init.zeros_(lin.bias)
+        self.gate_mlp = mlp.to(self.routing_logits.device)
+
+    def _mlp_params(self):
+        lin1, lin2 = self.gate_mlp[0], self.gate_mlp[2]
+        return tuple(t.detach().float().contiguous() for t in (lin1.weight, lin1.bias, lin2.weight, lin2.bias))
 
     # ------------------------------------------------------------------
     def forward(self, x):
@@ -238,6 +294,13 @@ class MoCE(nn.Module):
             # identity here (balancing is a sequential pass worth doing once)
             route = _Route(self.routing_logits, self.k, transposed=True, balance=False)
         self._compute_aux_losses(x, E_routed, tau)
+        if self.gate_type == "mlp":
+            # the two-layer gate in torch (3 small ops), differentiated by
+            # autograd; the mix and its backward native, from the given T
+            z = x.float().mean(dim=(2, 3))
+            g = self.gate_mlp(z)
+            T = (self.temp_min * tau + (self.temp_max - self.temp_min) * tau * torch.sigmoid(g)).clamp(min=1e-3)
+            return MoCEFunctionT.apply(x, self.routing_logits, T, route)
         y = MoCEFunction.apply(x, self.routing_logits, self.gate.weight, self.gate.bias,
                                self.temp_min * tau, (self.temp_max - self.temp_min) * tau, route)
         return y
@@ -251,9 +314,30 @@ class MoCE(nn.Module):
             # cache restored from a state_dict, or moved: rebuild the native part
             route = _Route(self.routing_logits, self.k, transposed=False)
             self._route = route
+        return self._eval_native(route, x.contiguous())
+
+    def _eval_native(self, route, x, out=None):
+        """The eval forward of either gate on the native kernels, into `out`
+        when given: the fused tensor-core chain (pass 1 -> temperatures ->
+        mix) where it takes the input, else pass 1, the gate and the
+        CUDA-core mix."""
+        if self.gate_type == "mlp":
+            m = native()
+            w1, b1, w2, b2 = self._mlp_params()
+            tmin_tau, trange_tau = float(self.cached_temp_min_tau), float(self.cached_temp_range_tau)
+            if m.tc_supported(x, self.k):
+                y = m.forward_tc_mlp(x, route.idx, route.ln, route.mask, route.meta, w1, b1, w2, b2, tmin_tau,
+                                     trange_tau, out)[0]
+            else:
+                y, z = m.pool_residual(x, route.mask, route.meta, int(route.idx.shape[0]), out)
+                T, _ = m.temperature_mlp(z, w1, b1, w2, b2, tmin_tau, trange_tau)
+                m.mix_given_t(x, route.idx, route.ln, route.mask, T, y)
+            if _CHECK_FAULTS:
+                check_faults()
+            return y
         gw = self.cached_gate_weight.detach().reshape(-1).float().contiguous()
         gb = self.cached_gate_bias.detach().reshape(-1).float().contiguous()
-        y, _, _ = route.forward(x.contiguous(), gw, gb, self.cached_temp_min_tau, self.cached_temp_range_tau)
+        y, _, _ = route.forward(x, gw, gb, self.cached_temp_min_tau, self.cached_temp_range_tau, False, out)
         return y
 
     # ------------------------------------------------------------------
@@ -271,7 +355,7 @@ class MoCE(nn.Module):
             raise RuntimeError("MoCE eval cache not built. Call build_moce_cache(model) before eval.")
         m = native()
         use_bn_stats = (not bn.training) and bn.running_mean is not None and bn.running_var is not None
-        if not (use_bn_stats and m.tc_supported(x, self.k)):
+        if not (use_bn_stats and m.tc_supported(x, self.k)) or self.gate_type == "mlp":
             y = bn(self.forward_eval(x))
             return F.relu(y) if relu else y
         route = self._route
@@ -329,8 +413,6 @@ class MoCE(nn.Module):
         if route is None or route.idx.device != dev:
             route = _Route(self.routing_logits, self.k, transposed=False)
             self._route = route
-        gw = self.cached_gate_weight.detach().reshape(-1).float().contiguous()
-        gb = self.cached_gate_bias.detach().reshape(-1).float().contiguous()
         n = max(1, min(int(slices), B))
         run = (B + n - 1) // n
         st = self.__dict__.get("_host_pipe")
@@ -367,7 +449,7 @@ class MoCE(nn.Module):
             cur.wait_event(st["in"][j])
             if st["used"][j]:
                 cur.wait_event(st["out"][j])               # the copy that read yb is done
-            route.forward(xb, gw, gb, self.cached_temp_min_tau, self.cached_temp_range_tau, False, yb)
+            self._eval_native(route, xb, yb)
             st["done"][j].record(cur)
             d2h.wait_event(st["done"][j])
             with torch.cuda.stream(d2h):

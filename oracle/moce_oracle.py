@@ -28,7 +28,7 @@ import numpy as np
 __all__ = [
     "select_supports", "normalize_selected", "uncovered_mask", "transposed_lists",
     "gap", "gate_temperature", "softmax_weights", "routed_mix", "residual",
-    "forward", "forward_with_weights", "backward", "aux_loss",
+    "forward", "forward_with_weights", "backward", "aux_loss", "gate_temperature_mlp",
 ]
 
 
@@ -122,6 +122,26 @@ def gate_temperature(z, idx, gate_w, gate_b, temp_min, temp_max, tau, dtype=np.f
     return np.maximum(T, dtype(1e-3)), g
 
 
+def gate_temperature_mlp(z, w1, b1, w2, b2, temp_min, temp_max, tau, dtype=np.float64):
+    """Temperatures from the opt-in two-layer gate C -> Hd -> E_r with ReLU:
+    h = relu(z w1^T + b1), g = h w2^T + b2, T = clamp((tmin + (tmax-tmin)
+    sigmoid(g)) * tau, 1e-3).
+
+    No reference counterpart (the reference's gate is the Linear(k,1) of
+    ``MoCE.py:66-68``); this restates the two-layer gate of the benchmark
+    configurations with the reference's temperature map (``MoCE.py:177-178``).
+    Parity for it is against this restatement only (unpinned by the
+    reference).  Returns (T, g, h) as [B, E_r], [B, E_r], [B, Hd].
+    """
+    z = np.asarray(z, dtype=dtype)
+    a1 = z @ np.asarray(w1, dtype=dtype).T + np.asarray(b1, dtype=dtype).reshape(1, -1)
+    h = np.maximum(a1, 0.0)
+    g = h @ np.asarray(w2, dtype=dtype).T + np.asarray(b2, dtype=dtype).reshape(1, -1)
+    sig = 1.0 / (1.0 + np.exp(-g))
+    T = (dtype(temp_min) + dtype(temp_max - temp_min) * sig) * dtype(tau)
+    return np.maximum(T, dtype(1e-3)), g, h
+
+
 def softmax_weights(ln, T):
     """a[b,e,:] = softmax(ln[e,:] / T[b,e]).
 
@@ -167,12 +187,14 @@ def residual(X, mask, dtype=np.float64):
 
 
 def forward(X, L, gate_w, gate_b, k, temp_min=0.2, temp_max=5.0, tau=1.0,
-            mode="eval", dtype=np.float64, return_aux=False):
+            mode="eval", dtype=np.float64, return_aux=False, mlp=None):
     """Full MoCE forward: Y [B, E_r+1, H, W].
 
     mode="train" follows ``MoCE.forward_train`` (``MoCE.py:153-201``, where
     tau is floored at 1e-4, ``MoCE.py:157``); mode="eval" follows
-    ``MoCE.forward_eval`` (``MoCE.py:204-230``).
+    ``MoCE.forward_eval`` (``MoCE.py:204-230``).  ``mlp=(w1, b1, w2, b2)``
+    replaces the Linear(k,1) gate by the two-layer gate
+    (``gate_temperature_mlp``; gate_w / gate_b are then unused).
     """
     X = np.asarray(X)
     B, C, H, W = X.shape
@@ -181,12 +203,16 @@ def forward(X, L, gate_w, gate_b, k, temp_min=0.2, temp_max=5.0, tau=1.0,
     ln = normalize_selected(L, idx, dtype=dtype)
     mask = uncovered_mask(C, idx)
     z = gap(X, dtype=dtype)
-    T, g = gate_temperature(z, idx, gate_w, gate_b, temp_min, temp_max, tau_eff, dtype=dtype)
+    h = None
+    if mlp is None:
+        T, g = gate_temperature(z, idx, gate_w, gate_b, temp_min, temp_max, tau_eff, dtype=dtype)
+    else:
+        T, g, h = gate_temperature_mlp(z, *mlp, temp_min, temp_max, tau_eff, dtype=dtype)
     a = softmax_weights(ln, T)
     Y = np.concatenate([routed_mix(X, idx, a, dtype=dtype), residual(X, mask, dtype=dtype)], axis=1)
     Y = Y.reshape(B, idx.shape[0] + 1, H, W)
     if return_aux:
-        return Y, dict(idx=idx, ln=ln, mask=mask, z=z, T=T, g=g, a=a)
+        return Y, dict(idx=idx, ln=ln, mask=mask, z=z, T=T, g=g, a=a, h=h)
     return Y
 
 
@@ -204,20 +230,23 @@ def forward_with_weights(X, idx, weights, mask, dtype=np.float64):
 
 
 def backward(X, L, gate_w, gate_b, k, dY, temp_min=0.2, temp_max=5.0, tau=1.0,
-             mode="train", dtype=np.float64):
+             mode="train", dtype=np.float64, mlp=None):
     """Gradients of sum(Y * dY) w.r.t. X, L (main path only) and the gate.
 
     Derived by hand from ``MoCE.forward_train`` (``MoCE.py:153-201``); the
     reference has no backward kernel and trains through autograd.  The
     auxiliary-loss gradient of L is not included (see ``aux_loss``).
-    Returns dict(dX, dL, dgate_w, dgate_b).
+    Returns dict(dX, dL, dgate_w, dgate_b, dT), and with ``mlp`` (the
+    two-layer gate) dict(dX, dL, dw1, db1, dw2, db2, dT) instead of the
+    Linear(k,1) gate's gradients.  dT is the gradient with respect to the
+    temperatures after the 1e-3 clamp.
     """
     X = np.asarray(X, dtype=dtype)
     B, C, H, W = X.shape
     HW = H * W
     tau_eff = max(float(tau), 1e-4) if mode == "train" else float(tau)
     _, aux = forward(X, L, gate_w, gate_b, k, temp_min, temp_max, tau, mode=mode,
-                     dtype=dtype, return_aux=True)
+                     dtype=dtype, return_aux=True, mlp=mlp)
     idx, ln, mask, z, T, g, a = (aux[n] for n in ("idx", "ln", "mask", "z", "T", "g", "a"))
     E_r = idx.shape[0]
     Xf = X.reshape(B, C, HW)
@@ -232,18 +261,31 @@ def backward(X, L, gate_w, gate_b, k, dY, temp_min=0.2, temp_max=5.0, tau=1.0,
     dln_b = du / T[:, :, None]
     u = ln[None] / T[:, :, None]
     dT = -(du * u).sum(-1) / T
+    dT_out = dT.copy()
     T_raw = (temp_min + (temp_max - temp_min) / (1.0 + np.exp(-g))) * tau_eff
     dT = np.where(T_raw >= 1e-3, dT, 0.0) * tau_eff
     sig = 1.0 / (1.0 + np.exp(-g))
     dg = dT * (temp_max - temp_min) * sig * (1.0 - sig)
 
-    zs = z[:, idx]
-    w = np.asarray(gate_w, dtype=dtype).reshape(-1)
-    dgate_w = (dg[:, :, None] * zs).sum((0, 1))
-    dgate_b = np.array([dg.sum()], dtype=dtype)
-    dz = np.zeros((B, C), dtype=dtype)
-    for i in range(k):
-        np.add.at(dz, (slice(None), idx[:, i]), dg * w[i])
+    gate_grads = {}
+    if mlp is None:
+        zs = z[:, idx]
+        w = np.asarray(gate_w, dtype=dtype).reshape(-1)
+        gate_grads["dgate_w"] = (dg[:, :, None] * zs).sum((0, 1)).reshape(1, -1)
+        gate_grads["dgate_b"] = np.array([dg.sum()], dtype=dtype)
+        dz = np.zeros((B, C), dtype=dtype)
+        for i in range(k):
+            np.add.at(dz, (slice(None), idx[:, i]), dg * w[i])
+    else:
+        # g = h w2^T + b2, h = relu(a1), a1 = z w1^T + b1
+        w1, b1, w2, b2 = (np.asarray(t, dtype=dtype) for t in mlp)
+        h = aux["h"]
+        gate_grads["dw2"] = dg.T @ h
+        gate_grads["db2"] = dg.sum(0)
+        da1 = (dg @ w2) * (h > 0)
+        gate_grads["dw1"] = da1.T @ z
+        gate_grads["db1"] = da1.sum(0)
+        dz = da1 @ w1
 
     dX = np.zeros((B, C, HW), dtype=dtype)
     for i in range(k):
@@ -266,7 +308,7 @@ def backward(X, L, gate_w, gate_b, k, dY, temp_min=0.2, temp_max=5.0, tau=1.0,
     dsel = dcen - dcen.mean(1, keepdims=True)
     dL = np.zeros(np.asarray(L).shape, dtype=dtype)
     np.put_along_axis(dL, idx, dsel, axis=1)
-    return dict(dX=dX.reshape(B, C, H, W), dL=dL, dgate_w=dgate_w.reshape(1, -1), dgate_b=dgate_b)
+    return dict(dX=dX.reshape(B, C, H, W), dL=dL, dT=dT_out, **gate_grads)
 
 
 def aux_loss(L, k, tau=1.0, balance_weight=0.05, specialization_weight=0.1,

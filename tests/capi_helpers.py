@@ -82,18 +82,56 @@ def tc_supported(x, k):
 
 
 def forward_tc(x, r, gate_w, gate_b, tmin_tau, trange_tau, want_T=True):
-    """Tensor-core path through the C ABI: pass 1 (pool + residual), tcgen05 mix."""
+    """Tensor-core path through the C ABI: pass 1 (pool + residual + operand
+    staging), the temperatures, then the tcgen05 mix, as three calls."""
     B, C, H, W = x.shape
     E_r, k = r["idx"].shape
     y = torch.empty(B, E_r + 1, H, W, dtype=x.dtype, device=x.device)
     z = torch.empty(B, C, dtype=torch.float32, device=x.device)
-    T = torch.empty(B, E_r, dtype=torch.float32, device=x.device) if want_T else None
+    T = torch.empty(B, E_r, dtype=torch.float32, device=x.device)
     xs = torch.empty(capi.lib().moce_tc_stage_bytes(B, C, H * W), dtype=torch.uint8, device=x.device)
     call("moce_pool_stage", ptr(x), dtype_code(x), B, C, H * W, ptr(r["mask"]), ptr(r["meta"]), ptr(z), ptr(y),
          E_r, ptr(xs), stream_handle())
-    call("moce_mix_tc", ptr(xs), dtype_code(x), B, C, H * W, ptr(z), ptr(r["idx"]), ptr(r["ln"]), E_r, k,
-         ptr(gate_w), ptr(gate_b), tmin_tau, trange_tau, ptr(y), ptr(T), stream_handle())
+    call("moce_temperature", ptr(z), B, C, ptr(r["idx"]), E_r, k, ptr(gate_w), ptr(gate_b), tmin_tau, trange_tau,
+         ptr(T), stream_handle())
+    call("moce_mix_tc", ptr(xs), dtype_code(x), B, C, H * W, ptr(T), ptr(r["idx"]), ptr(r["ln"]), E_r, k, ptr(y),
+         stream_handle())
     return y, z, T
+
+
+def temperature(z, idx, gate_w, gate_b, tmin_tau, trange_tau):
+    B, C = z.shape
+    E_r, k = idx.shape
+    T = torch.empty(B, E_r, dtype=torch.float32, device=z.device)
+    call("moce_temperature", ptr(z), B, C, ptr(idx), E_r, k, ptr(gate_w), ptr(gate_b), tmin_tau, trange_tau, ptr(T),
+         stream_handle())
+    return T
+
+
+def temperature_mlp(z, w1, b1, w2, b2, tmin_tau, trange_tau):
+    B, C = z.shape
+    Hd, E_r = w1.shape[0], w2.shape[0]
+    T = torch.empty(B, E_r, dtype=torch.float32, device=z.device)
+    h = torch.empty(B, Hd, dtype=torch.float32, device=z.device)
+    call("moce_temperature_mlp", ptr(z), B, C, Hd, E_r, ptr(w1), ptr(b1), ptr(w2), ptr(b2), tmin_tau, trange_tau,
+         ptr(h), ptr(T), stream_handle())
+    return T, h
+
+
+def forward_tc_mlp(x, r, w1, b1, w2, b2, tmin_tau, trange_tau):
+    """Tensor-core forward with the two-layer gate, one call (three launches)."""
+    B, C, H, W = x.shape
+    E_r, k = r["idx"].shape
+    Hd = w1.shape[0]
+    y = torch.empty(B, E_r + 1, H, W, dtype=x.dtype, device=x.device)
+    z = torch.empty(B, C, dtype=torch.float32, device=x.device)
+    T = torch.empty(B, E_r, dtype=torch.float32, device=x.device)
+    h = torch.empty(B, Hd, dtype=torch.float32, device=x.device)
+    xs = torch.empty(capi.lib().moce_tc_stage_bytes(B, C, H * W), dtype=torch.uint8, device=x.device)
+    call("moce_forward_tc_mlp", ptr(x), dtype_code(x), B, C, H * W, ptr(r["mask"]), ptr(r["meta"]), ptr(r["idx"]),
+         ptr(r["ln"]), E_r, k, Hd, ptr(w1), ptr(b1), ptr(w2), ptr(b2), tmin_tau, trange_tau, ptr(z), ptr(h), ptr(xs),
+         ptr(y), ptr(T), stream_handle())
+    return y, z, T, h
 
 
 def px_supported(x, k):
