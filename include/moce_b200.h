@@ -408,6 +408,33 @@ int moce_backward_t(const void* x, const void* dy, int dtype, int64_t B,
                     const float* T, void* dx, float* dL, float* dT,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * The auxiliary (coverage) loss of the layer, MoCE._compute_aux_losses
+ * (MoCE.py:118-151), and its gradient with respect to the routing logits:
+ *   P = softmax(logits / tau) over channels, logits fp32 [E_r, C]
+ *   aux = balance_weight * var_c(mean_e P)
+ *       + specialization_weight * mean_c relu(H_c - log_target)
+ *       + diversity_weight * mean of the off-diagonal of P P^T
+ * with H_c the entropy of column c of P normalised to sum 1 (clamped at
+ * 1e-8 as the reference does) and log_target = log(max(E_r k / C, 1)).  The
+ * E_r x E_r product is not formed (its sum is the sum of squared column sums,
+ * its trace the sum of squares).  aux_out: fp32 [1] on the device.
+ * moce_aux_loss_backward writes dL fp32 [E_r, C] = grad_aux[0] * d aux /
+ * d logits (grad_aux fp32 [1] on the device).  Both are deterministic.
+ * workspace: moce_aux_workspace_bytes(E_r, C) bytes, 256-aligned.
+ */
+size_t moce_aux_workspace_bytes(int64_t E_r, int64_t C);
+int moce_aux_loss(const float* logits, int64_t E_r, int64_t C, float tau,
+                  float balance_weight, float specialization_weight,
+                  float diversity_weight, float log_target, float* aux_out,
+                  void* workspace, size_t workspace_bytes, void* stream);
+int moce_aux_loss_backward(const float* logits, int64_t E_r, int64_t C,
+                           float tau, float balance_weight,
+                           float specialization_weight, float diversity_weight,
+                           float log_target, const float* grad_aux, float* dL,
+                           void* workspace, size_t workspace_bytes,
+                           void* stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

@@ -8,10 +8,11 @@
 // pooled values of the expert's own supports:
 //     g[b, e] = gate_w . z[b, S_e] + gate_b;
 //     T[b, e] = max(tmin_tau + trange_tau * sigmoid(g), 1e-3)
-// temp_linear_kernel: expert-major.  A CTA owns a tile of 128 experts and a
-// range of samples; threads 2r and 2r+1 hold half of row r's supports and
-// gate weights in registers, so the routing tables are read once per CTA and
-// only z streams (one row of C floats per sample, from L2).
+// temp_linear_kernel: a CTA owns a tile of 128 experts and a group of up to
+// 8 samples; threads 2r and 2r+1 hold half of row r's supports and gate
+// weights in registers, the group's z rows (contiguous) are staged in shared
+// memory in one coalesced pass, then each thread pair gathers its row's
+// inputs for every sample of the group.
 //
 // Two-layer gate (opt-in, no reference counterpart: the two-layer gate of the
 // benchmark configurations, C -> C/16 -> E_r with ReLU):
@@ -28,13 +29,17 @@ namespace {
 constexpr int kGateThreads = 256;
 constexpr int kGateRows = 128;                 // experts per CTA (two threads each)
 
-// expert tiles x sample ranges: about two CTAs per SM
-void gate_grid(int64_t B, int64_t E_r, int* n_tiles, int* n_bsplit) {
+// expert tiles x groups of `spb` samples: each CTA loads its samples' input
+// rows in one coalesced pass (no load latency per sample); the group size
+// keeps that staging within `smem_cap` bytes and the grid at several CTAs
+// per SM
+void gate_grid(int64_t B, int64_t E_r, int64_t row_floats, int* n_tiles, int* spb, int* n_groups) {
   *n_tiles = (int)((E_r + kGateRows - 1) / kGateRows);
-  int64_t nb = (2LL * num_sms() + *n_tiles - 1) / *n_tiles;
-  if (nb > B) nb = B;
-  if (nb < 1) nb = 1;
-  *n_bsplit = (int)nb;
+  int64_t g = 8;
+  while (g > 1 && g * row_floats * 4 > 48 * 1024) g /= 2;
+  while (g > 1 && *n_tiles * ((B + g - 1) / g) < 4LL * num_sms()) g /= 2;
+  *spb = (int)g;
+  *n_groups = (int)((B + g - 1) / g);
 }
 
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -44,14 +49,14 @@ template <int KH>
 __global__ void __launch_bounds__(kGateThreads) temp_linear_kernel(
     const float* __restrict__ z, int B, int C, const int32_t* __restrict__ idx, int E_r, int k,
     const float* __restrict__ gate_w, const float* __restrict__ gate_b, float tmin_tau, float trange_tau,
-    float* __restrict__ T, int n_tiles, int n_bsplit) {
-  extern __shared__ float s_zb[];                          // 2 x C: z of the current and the next sample
+    float* __restrict__ T, int n_tiles, int spb) {
+  extern __shared__ float s_zb[];                          // spb x C: z of this CTA's samples
   grid_dep_launch();                                       // the mix may start its prologue
   const int tid = threadIdx.x, row = tid >> 1, part = tid & 1;
-  const int tile = blockIdx.x % n_tiles, bs = blockIdx.x / n_tiles;
+  const int tile = blockIdx.x % n_tiles, grp = blockIdx.x / n_tiles;
   const int e = tile * kGateRows + row;
   const bool has = e < E_r;
-  const int b0 = (int)((long long)bs * B / n_bsplit), b1 = (int)((long long)(bs + 1) * B / n_bsplit);
+  const int b0 = grp * spb, nb = min(spb, B - b0);
   int ch[KH];
   float w[KH];
 #pragma unroll
@@ -66,20 +71,19 @@ __global__ void __launch_bounds__(kGateThreads) temp_linear_kernel(
   }
   const float bias = gate_b[0];
   grid_dep_wait();                                         // z comes from pass 1
-  if (b0 >= b1) return;
-  for (int c = tid; c < C; c += kGateThreads) s_zb[c] = z[(size_t)b0 * C + c];
+  // the samples' z rows are contiguous: one coalesced copy, many loads in flight
+  const int n = nb * C;
+  const float* zs = z + (size_t)b0 * C;
+#pragma unroll 4
+  for (int q = tid; q < n; q += kGateThreads) s_zb[q] = zs[q];
   __syncthreads();
-  for (int b = b0; b < b1; ++b) {
-    const float* zc = s_zb + ((b - b0) & 1) * C;
-    float* zn = s_zb + ((b - b0 + 1) & 1) * C;
-    if (b + 1 < b1)                                        // the next sample's z into the other buffer
-      for (int c = tid; c < C; c += kGateThreads) zn[c] = z[(size_t)(b + 1) * C + c];
+  for (int s = 0; s < nb; ++s) {
+    const float* zc = s_zb + s * C;
     float g = 0.0f;
 #pragma unroll
     for (int j = 0; j < KH; ++j) g += w[j] * zc[ch[j]];
     g += __shfl_xor_sync(kFull, g, 1);
-    if (has && part == 0) T[(size_t)b * E_r + e] = temperature(g + bias, tmin_tau, trange_tau, nullptr);
-    __syncthreads();
+    if (has && part == 0) T[(size_t)(b0 + s) * E_r + e] = temperature(g + bias, tmin_tau, trange_tau, nullptr);
   }
 }
 
@@ -108,14 +112,14 @@ __global__ void __launch_bounds__(kGateThreads) mlp_hidden_kernel(const float* _
 template <int HH>
 __global__ void __launch_bounds__(kGateThreads) mlp_temp_kernel(
     const float* __restrict__ h, int B, int Hd, const float* __restrict__ w2, const float* __restrict__ b2,
-    int E_r, float tmin_tau, float trange_tau, float* __restrict__ T, int n_tiles, int n_bsplit) {
-  extern __shared__ float s_h[];                           // 2 x Hd
+    int E_r, float tmin_tau, float trange_tau, float* __restrict__ T, int n_tiles, int spb) {
+  extern __shared__ float s_h[];                           // spb x Hd
   grid_dep_launch();
   const int tid = threadIdx.x, row = tid >> 1, part = tid & 1;
-  const int tile = blockIdx.x % n_tiles, bs = blockIdx.x / n_tiles;
+  const int tile = blockIdx.x % n_tiles, grp = blockIdx.x / n_tiles;
   const int e = tile * kGateRows + row;
   const bool has = e < E_r;
-  const int bb0 = (int)((long long)bs * B / n_bsplit), bb1 = (int)((long long)(bs + 1) * B / n_bsplit);
+  const int b0 = grp * spb, nb = min(spb, B - b0);
   float w[HH];
 #pragma unroll
   for (int j = 0; j < HH; ++j) {
@@ -124,21 +128,19 @@ __global__ void __launch_bounds__(kGateThreads) mlp_temp_kernel(
   }
   const float bias = has ? b2[e] : 0.0f;
   grid_dep_wait();                                         // h comes from mlp_hidden_kernel
-  if (bb0 >= bb1) return;
-  for (int j = tid; j < Hd; j += kGateThreads) s_h[j] = h[(size_t)bb0 * Hd + j];
+  const int n = nb * Hd;
+  const float* hs = h + (size_t)b0 * Hd;
+#pragma unroll 4
+  for (int q = tid; q < n; q += kGateThreads) s_h[q] = hs[q];
   __syncthreads();
-  for (int b = bb0; b < bb1; ++b) {
-    const float* hc = s_h + ((b - bb0) & 1) * Hd;
-    float* hn = s_h + ((b - bb0 + 1) & 1) * Hd;
-    if (b + 1 < bb1)
-      for (int j = tid; j < Hd; j += kGateThreads) hn[j] = h[(size_t)(b + 1) * Hd + j];
+  for (int s = 0; s < nb; ++s) {
+    const float* hc = s_h + s * Hd;
     float g = 0.0f;
 #pragma unroll
     for (int j = 0; j < HH; ++j)
       if (part * HH + j < Hd) g += w[j] * hc[part * HH + j];
     g += __shfl_xor_sync(kFull, g, 1);
-    if (has && part == 0) T[(size_t)b * E_r + e] = temperature(g + bias, tmin_tau, trange_tau, nullptr);
-    __syncthreads();
+    if (has && part == 0) T[(size_t)(b0 + s) * E_r + e] = temperature(g + bias, tmin_tau, trange_tau, nullptr);
   }
 }
 
@@ -175,25 +177,25 @@ int temperature_run(const float* z, int64_t B, int64_t C, const int32_t* idx, in
   MOCE_REQUIRE(z && idx && gate_w && gate_b && T, MOCE_ERR_INVALID, "moce_temperature: null pointer argument");
   MOCE_REQUIRE(B > 0 && C >= 1 && E_r >= 1 && k >= 1 && k <= C, MOCE_ERR_INVALID, "moce_temperature: invalid shape");
   MOCE_REQUIRE(k <= 128, MOCE_ERR_UNSUPPORTED, "moce_temperature: k <= 128");
-  MOCE_REQUIRE(B * E_r < ((int64_t)1 << 40) && 2 * C * 4 <= 200 * 1024, MOCE_ERR_UNSUPPORTED,
+  MOCE_REQUIRE(B * E_r < ((int64_t)1 << 40) && C * 4 <= 200 * 1024, MOCE_ERR_UNSUPPORTED,
                "moce_temperature: shape too large");
-  int n_tiles, n_bsplit;
-  gate_grid(B, E_r, &n_tiles, &n_bsplit);
-  const dim3 grid((unsigned)(n_tiles * n_bsplit)), block(kGateThreads);
-  const size_t smem = (size_t)2 * C * 4;
+  int n_tiles, spb, n_groups;
+  gate_grid(B, E_r, C, &n_tiles, &spb, &n_groups);
+  const dim3 grid((unsigned)(n_tiles * n_groups)), block(kGateThreads);
+  const size_t smem = (size_t)spb * C * 4;
   cudaStream_t st = (cudaStream_t)stream;
   const int ki = (int)k, Ci = (int)C, Ei = (int)E_r, Bi = (int)B;
   if (k <= 16)
     return launch_pdl(temp_linear_kernel<8>, grid, block, smem, st, dependent, "temp_linear_kernel", z, Bi, Ci, idx,
-                      Ei, ki, gate_w, gate_b, tmin_tau, trange_tau, T, n_tiles, n_bsplit);
+                      Ei, ki, gate_w, gate_b, tmin_tau, trange_tau, T, n_tiles, spb);
   if (k <= 32)
     return launch_pdl(temp_linear_kernel<16>, grid, block, smem, st, dependent, "temp_linear_kernel", z, Bi, Ci,
-                      idx, Ei, ki, gate_w, gate_b, tmin_tau, trange_tau, T, n_tiles, n_bsplit);
+                      idx, Ei, ki, gate_w, gate_b, tmin_tau, trange_tau, T, n_tiles, spb);
   if (k <= 64)
     return launch_pdl(temp_linear_kernel<32>, grid, block, smem, st, dependent, "temp_linear_kernel", z, Bi, Ci,
-                      idx, Ei, ki, gate_w, gate_b, tmin_tau, trange_tau, T, n_tiles, n_bsplit);
+                      idx, Ei, ki, gate_w, gate_b, tmin_tau, trange_tau, T, n_tiles, spb);
   return launch_pdl(temp_linear_kernel<64>, grid, block, smem, st, dependent, "temp_linear_kernel", z, Bi, Ci, idx,
-                    Ei, ki, gate_w, gate_b, tmin_tau, trange_tau, T, n_tiles, n_bsplit);
+                    Ei, ki, gate_w, gate_b, tmin_tau, trange_tau, T, n_tiles, spb);
 }
 
 int temperature_mlp_run(const float* z, int64_t B, int64_t C, int64_t Hd, int64_t E_r, const float* w1,
@@ -209,21 +211,21 @@ int temperature_mlp_run(const float* z, int64_t B, int64_t C, int64_t Hd, int64_
   int rc = launch_pdl(mlp_hidden_kernel, dim3((unsigned)((B + 7) / 8)), dim3(kGateThreads), 0, st, dependent,
                       "mlp_hidden_kernel", z, Bi, Ci, Hi, w1, b1, h);
   if (rc) return rc;
-  int n_tiles, n_bsplit;
-  gate_grid(B, E_r, &n_tiles, &n_bsplit);
-  const dim3 grid((unsigned)(n_tiles * n_bsplit)), block(kGateThreads);
-  const size_t smem = (size_t)2 * Hd * 4;
+  int n_tiles, spb, n_groups;
+  gate_grid(B, E_r, Hd, &n_tiles, &spb, &n_groups);
+  const dim3 grid((unsigned)(n_tiles * n_groups)), block(kGateThreads);
+  const size_t smem = (size_t)spb * Hd * 4;
   if (Hd <= 32)
     return launch_pdl(mlp_temp_kernel<16>, grid, block, smem, st, true, "mlp_temp_kernel", (const float*)h, Bi, Hi,
-                      w2, b2, Ei, tmin_tau, trange_tau, T, n_tiles, n_bsplit);
+                      w2, b2, Ei, tmin_tau, trange_tau, T, n_tiles, spb);
   if (Hd <= 64)
     return launch_pdl(mlp_temp_kernel<32>, grid, block, smem, st, true, "mlp_temp_kernel", (const float*)h, Bi, Hi,
-                      w2, b2, Ei, tmin_tau, trange_tau, T, n_tiles, n_bsplit);
+                      w2, b2, Ei, tmin_tau, trange_tau, T, n_tiles, spb);
   if (Hd <= 128)
     return launch_pdl(mlp_temp_kernel<64>, grid, block, smem, st, true, "mlp_temp_kernel", (const float*)h, Bi, Hi,
-                      w2, b2, Ei, tmin_tau, trange_tau, T, n_tiles, n_bsplit);
+                      w2, b2, Ei, tmin_tau, trange_tau, T, n_tiles, spb);
   return launch_pdl(mlp_temp_kernel<128>, grid, block, smem, st, true, "mlp_temp_kernel", (const float*)h, Bi, Hi,
-                    w2, b2, Ei, tmin_tau, trange_tau, T, n_tiles, n_bsplit);
+                    w2, b2, Ei, tmin_tau, trange_tau, T, n_tiles, spb);
 }
 
 }  // namespace moce

@@ -780,6 +780,51 @@ std::vector<torch::Tensor> backward_t(torch::Tensor x, torch::Tensor dy, torch::
   return {dx, dL, dT};
 }
 
+// ------------------------------------------------------- auxiliary loss
+
+torch::Tensor aux_workspace(const torch::Tensor& logits, void** wp, size_t* nb) {
+  *nb = moce_aux_workspace_bytes(logits.size(0), logits.size(1));
+  auto ws = torch::empty({(int64_t)*nb + 256}, logits.options().dtype(torch::kUInt8));
+  *wp = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(ws.data_ptr()) + 255) & ~uintptr_t(255));
+  return ws;
+}
+
+void check_logits(const torch::Tensor& logits) {
+  CHECK_INPUT(logits);
+  TORCH_CHECK(logits.dim() == 2 && logits.scalar_type() == torch::kFloat32, "logits must be float32 (E_r, C)");
+}
+
+// the auxiliary loss as a 0-d float32 tensor
+torch::Tensor aux_loss(torch::Tensor logits, double tau, double wb, double ws_, double wd, double log_target) {
+  check_logits(logits);
+  const c10::cuda::CUDAGuard guard(logits.device());
+  void* wp;
+  size_t nb;
+  auto ws = aux_workspace(logits, &wp, &nb);
+  auto out = torch::empty({}, logits.options());
+  ok(moce_aux_loss(logits.data_ptr<float>(), logits.size(0), logits.size(1), (float)tau, (float)wb, (float)ws_,
+                   (float)wd, (float)log_target, out.data_ptr<float>(), wp, nb, cur_stream()));
+  return out;
+}
+
+// grad * d aux / d logits
+torch::Tensor aux_loss_backward(torch::Tensor logits, double tau, double wb, double ws_, double wd, double log_target,
+                                torch::Tensor grad) {
+  check_logits(logits);
+  CHECK_INPUT(grad);
+  TORCH_CHECK(grad.numel() == 1 && grad.scalar_type() == torch::kFloat32 && grad.device() == logits.device(),
+              "grad must be one float32 on the device of logits");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  void* wp;
+  size_t nb;
+  auto ws = aux_workspace(logits, &wp, &nb);
+  auto dL = torch::empty_like(logits);
+  ok(moce_aux_loss_backward(logits.data_ptr<float>(), logits.size(0), logits.size(1), (float)tau, (float)wb,
+                            (float)ws_, (float)wd, (float)log_target, grad.data_ptr<float>(), dL.data_ptr<float>(), wp,
+                            nb, cur_stream()));
+  return dL;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -839,6 +884,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("forward_given_t", &forward_given_t, "Pass 1 and the mix from given temperatures: y", py::arg("x"),
         py::arg("idx"), py::arg("ln"), py::arg("mask"), py::arg("meta"), py::arg("T"), py::arg("out") = py::none());
   m.def("backward_t", &backward_t, "Backward from given temperatures: (dx, dL, dT)");
+  m.def("aux_loss", &aux_loss, "Auxiliary (coverage) loss of the routing logits, a 0-d tensor");
+  m.def("aux_loss_backward", &aux_loss_backward, "grad * d aux / d logits");
   m.def("tc_fault", [](bool clear) {
     int flag = 0;
     ok(moce_tc_fault(&flag, clear ? 1 : 0));

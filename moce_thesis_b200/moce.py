@@ -17,7 +17,8 @@ changes is where the work runs:
   re-selected every step, as the reference does (``MoCE.py:160``).
 
 The auxiliary/coverage loss (``MoCE.py:118-151``) depends on the routing
-logits only and stays a PyTorch expression.
+logits only; its forward and gradient are native kernels too
+(``AuxLossFunction``).
 """
 from __future__ import annotations
 
@@ -143,6 +144,30 @@ class MoCEFunction(torch.autograd.Function):
         return (dx, dL.to(logits.dtype), dgw.reshape(wshape), dgb.reshape(bshape), None, None, None)
 
 
+class AuxLossFunction(torch.autograd.Function):
+    """The auxiliary (coverage) loss of the routing logits on the native
+    kernels: balance + specialisation + diversity of ``MoCE.py:118-151``
+    (softmax over channels, usage variance, per-channel entropy, mean
+    off-diagonal overlap), forward and gradient, with deterministic
+    reductions.  Returns a 0-d float32 tensor."""
+
+    @staticmethod
+    def forward(ctx, logits, tau, balance_w, spec_w, div_w, log_target):
+        L = logits.detach().float().contiguous()
+        consts = (float(tau), float(balance_w), float(spec_w), float(div_w), float(log_target))
+        out = native().aux_loss(L, *consts)
+        ctx.save_for_backward(L)
+        ctx.consts = consts
+        ctx.ldtype = logits.dtype
+        return out
+
+    @staticmethod
+    def backward(ctx, go):
+        (L,) = ctx.saved_tensors
+        dL = native().aux_loss_backward(L, *ctx.consts, go.detach().float().reshape(1).contiguous())
+        return dL.to(ctx.ldtype), None, None, None, None, None
+
+
 class MoCEFunctionT(torch.autograd.Function):
     """Y = MoCE(X; L, T) with the temperatures T [B, E_r] given.
 
@@ -266,24 +291,13 @@ class MoCE(nn.Module):
 
     # ------------------------------------------------------------------
     def _compute_aux_losses(self, x, E_routed, tau):
-        """Balance + specialisation + diversity losses (``MoCE.py:118-151``)."""
-        P = F.softmax(self.routing_logits / tau, dim=1)               # [E_r, C]
-        usage = P.mean(dim=0)
-        balance = (usage - usage.mean()).pow(2).mean()
-        per_channel = P / P.sum(dim=0, keepdim=True).clamp(min=1e-8)
-        entropy = -(per_channel * per_channel.clamp(min=1e-8).log()).sum(dim=0)
+        """Balance + specialisation + diversity losses (``MoCE.py:118-151``),
+        on the native kernels (AuxLossFunction): the mean off-diagonal of
+        P P^T is (sum of squared column sums - sum of squares) / (E (E - 1)),
+        so the E x C x E product is never formed."""
         target = math.log(max(float(self.target_experts_per_channel), 1.0))
-        specialization = F.relu(entropy - target).mean()
-        if E_routed > 1:
-            # mean of the off-diagonal entries of P P^T (MoCE.py:145-148), as
-            # (sum - trace) / (E (E - 1)): the same quantity without the
-            # boolean-mask gather, whose backward is a sorted scatter
-            overlap = P @ P.t()
-            diversity = (overlap.sum() - overlap.diagonal().sum()) / float(E_routed * (E_routed - 1))
-        else:
-            diversity = P.new_zeros(())
-        self.aux_loss = (self.balance_weight * balance + self.specialization_weight * specialization
-                         + self.diversity_weight * diversity)
+        self.aux_loss = AuxLossFunction.apply(self.routing_logits, tau, self.balance_weight,
+                                              self.specialization_weight, self.diversity_weight, target)
 
     def forward_train(self, x):
         B, C, H, W = x.shape
