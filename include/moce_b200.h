@@ -183,6 +183,15 @@ int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C,
                 void* stream);
 int moce_tc_fault(int* flag, int clear);
 int64_t moce_tc_wait_limit_ns(int64_t ns);
+/* Where the first wait that ran out gave up, for diagnostics (synchronises):
+ * info[0] 1 if recorded, [1] wait site (1 producer: ring slot free, 2 issuer:
+ * accumulator drained (one tile per sample), 3 issuer: weights written,
+ * 4 issuer: accumulator drained (pixel tiles), 5 issuer: X quarter landed,
+ * 6 weight rows: previous sample's MMAs done, 7 drain: accumulator
+ * complete), [2] parity, [3] unit or sample index, [4] block, [5] thread,
+ * [6] C, [7] H*W, [8] E_r, [9] k, [10] B, [11] pixel tiles per sample,
+ * [12] MMA N, [13] nanoseconds waited.  Fills min(n, 14) entries. */
+int moce_tc_fault_info(int64_t* info, int n, int clear);
 
 /*
  * The tensor-core forward in one call: moce_pool_stage, moce_temperature and

@@ -43,6 +43,7 @@ SIGNATURES = {
                                    _f32, _f32, _p, _p, _p, _p, _p, _p]),
     "moce_tc_fault": (_i32, [_p, _i32]),
     "moce_tc_wait_limit_ns": (_i64, [_i64]),
+    "moce_tc_fault_info": (_i32, [_p, _i32, _i32]),
     "moce_forward_tc": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _p, _p, _f32, _f32, _p, _p, _p,
                                 _p, _p]),
     "moce_forward_tc_ep": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _p, _p, _f32, _f32, _p, _p, _i32,

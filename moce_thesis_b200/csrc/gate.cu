@@ -8,11 +8,8 @@
 // pooled values of the expert's own supports:
 //     g[b, e] = gate_w . z[b, S_e] + gate_b;
 //     T[b, e] = max(tmin_tau + trange_tau * sigmoid(g), 1e-3)
-// temp_linear_kernel: a CTA owns a tile of 128 experts and a group of up to
-// 8 samples; threads 2r and 2r+1 hold half of row r's supports and gate
-// weights in registers, the group's z rows (contiguous) are staged in shared
-// memory in one coalesced pass, then each thread pair gathers its row's
-// inputs for every sample of the group.
+// temp_linear_kernel: lanes over samples (see the kernel), so the gathers of
+// z are conflict-free shared-memory reads.
 //
 // Two-layer gate (opt-in, no reference counterpart: the two-layer gate of the
 // benchmark configurations, C -> C/16 -> E_r with ReLU):
@@ -45,45 +42,64 @@ void gate_grid(int64_t B, int64_t E_r, int64_t row_floats, int* n_tiles, int* sp
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-template <int KH>
+// Linear gate with lanes over samples.  A CTA owns a tile of 32 samples and
+// a range of experts.  z of the 32 samples is staged transposed, zt[c][b]
+// (row pitch 33 words), so that for one support channel the warp's 32 lanes
+// (32 samples) read 32 consecutive banks: one conflict-free wavefront per
+// support step.  The expert's supports and gate weights are warp-uniform
+// (one load per lane, broadcast by shuffle).  Temperatures of 32 experts x
+// 32 samples collect in a shared tile and leave as rows of T [B, E_r].
+constexpr int kTs = 32;                        // samples per CTA
+constexpr int kTeWarp = 4;                     // experts per warp per round (32 per CTA round of 8 warps)
+
 __global__ void __launch_bounds__(kGateThreads) temp_linear_kernel(
     const float* __restrict__ z, int B, int C, const int32_t* __restrict__ idx, int E_r, int k,
     const float* __restrict__ gate_w, const float* __restrict__ gate_b, float tmin_tau, float trange_tau,
-    float* __restrict__ T, int n_tiles, int spb) {
-  extern __shared__ float s_zb[];                          // spb x C: z of this CTA's samples
+    float* __restrict__ T, int n_stiles, int e_per_cta) {
+  extern __shared__ float s_zt[];                          // C x 33: z transposed
+  __shared__ float s_t[kTs][33];                           // 32 experts x 32 samples of T
   grid_dep_launch();                                       // the mix may start its prologue
-  const int tid = threadIdx.x, row = tid >> 1, part = tid & 1;
-  const int tile = blockIdx.x % n_tiles, grp = blockIdx.x / n_tiles;
-  const int e = tile * kGateRows + row;
-  const bool has = e < E_r;
-  const int b0 = grp * spb, nb = min(spb, B - b0);
-  int ch[KH];
-  float w[KH];
-#pragma unroll
-  for (int j = 0; j < KH; ++j) {
-    const int i = part * KH + j;
-    ch[j] = 0;
-    w[j] = 0.0f;
-    if (has && i < k) {
-      ch[j] = idx[(size_t)e * k + i];
-      w[j] = gate_w[i];
-    }
-  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int st = blockIdx.x % n_stiles, eg = blockIdx.x / n_stiles;
+  const int b0 = st * kTs, nb = min(kTs, B - b0);
+  const int ea = eg * e_per_cta, eb = min(E_r, ea + e_per_cta);
   const float bias = gate_b[0];
   grid_dep_wait();                                         // z comes from pass 1
-  // the samples' z rows are contiguous: one coalesced copy, many loads in flight
-  const int n = nb * C;
-  const float* zs = z + (size_t)b0 * C;
-#pragma unroll 4
-  for (int q = tid; q < n; q += kGateThreads) s_zb[q] = zs[q];
+  // z[b0 .. b0+nb, :] -> zt[c][b]: consecutive threads take consecutive
+  // channels of one sample (coalesced reads, conflict-free writes)
+  for (int q = threadIdx.x; q < nb * C; q += kGateThreads) {
+    const int bb = q / C, c = q - bb * C;
+    s_zt[c * 33 + bb] = z[(size_t)(b0 + bb) * C + c];
+  }
   __syncthreads();
-  for (int s = 0; s < nb; ++s) {
-    const float* zc = s_zb + s * C;
-    float g = 0.0f;
+  for (int e00 = ea; e00 < eb; e00 += 8 * kTeWarp) {       // rounds of 32 experts
 #pragma unroll
-    for (int j = 0; j < KH; ++j) g += w[j] * zc[ch[j]];
-    g += __shfl_xor_sync(kFull, g, 1);
-    if (has && part == 0) T[(size_t)(b0 + s) * E_r + e] = temperature(g + bias, tmin_tau, trange_tau, nullptr);
+    for (int r = 0; r < kTeWarp; ++r) {
+      const int el = warp * kTeWarp + r;                   // expert within the round, 0..31
+      const int e = e00 + el;
+      float g = 0.0f;
+      if (e < eb) {                                        // uniform across the warp
+        for (int i0 = 0; i0 < k; i0 += 32) {
+          const int i = i0 + lane;
+          const int c_l = i < k ? idx[(size_t)e * k + i] : 0;
+          const float w_l = i < k ? gate_w[i] : 0.0f;
+          const int n = min(32, k - i0);
+          for (int j = 0; j < n; ++j) {
+            const int c = __shfl_sync(kFull, c_l, j);
+            const float w = __shfl_sync(kFull, w_l, j);
+            g += w * s_zt[c * 33 + lane];
+          }
+        }
+      }
+      s_t[el][lane] = temperature(g + bias, tmin_tau, trange_tau, nullptr);
+    }
+    __syncthreads();
+    // rows of T: sample b0 + bb, experts e00 .. e00+31
+    for (int q = threadIdx.x; q < kTs * 32; q += kGateThreads) {
+      const int bb = q >> 5, el = q & 31;
+      if (bb < nb && e00 + el < eb) T[(size_t)(b0 + bb) * E_r + e00 + el] = s_t[el][bb];
+    }
+    __syncthreads();
   }
 }
 
@@ -176,26 +192,21 @@ int temperature_run(const float* z, int64_t B, int64_t C, const int32_t* idx, in
   if (B == 0) return MOCE_OK;
   MOCE_REQUIRE(z && idx && gate_w && gate_b && T, MOCE_ERR_INVALID, "moce_temperature: null pointer argument");
   MOCE_REQUIRE(B > 0 && C >= 1 && E_r >= 1 && k >= 1 && k <= C, MOCE_ERR_INVALID, "moce_temperature: invalid shape");
-  MOCE_REQUIRE(k <= 128, MOCE_ERR_UNSUPPORTED, "moce_temperature: k <= 128");
-  MOCE_REQUIRE(B * E_r < ((int64_t)1 << 40) && C * 4 <= 200 * 1024, MOCE_ERR_UNSUPPORTED,
-               "moce_temperature: shape too large");
-  int n_tiles, spb, n_groups;
-  gate_grid(B, E_r, C, &n_tiles, &spb, &n_groups);
-  const dim3 grid((unsigned)(n_tiles * n_groups)), block(kGateThreads);
-  const size_t smem = (size_t)spb * C * 4;
-  cudaStream_t st = (cudaStream_t)stream;
-  const int ki = (int)k, Ci = (int)C, Ei = (int)E_r, Bi = (int)B;
-  if (k <= 16)
-    return launch_pdl(temp_linear_kernel<8>, grid, block, smem, st, dependent, "temp_linear_kernel", z, Bi, Ci, idx,
-                      Ei, ki, gate_w, gate_b, tmin_tau, trange_tau, T, n_tiles, spb);
-  if (k <= 32)
-    return launch_pdl(temp_linear_kernel<16>, grid, block, smem, st, dependent, "temp_linear_kernel", z, Bi, Ci,
-                      idx, Ei, ki, gate_w, gate_b, tmin_tau, trange_tau, T, n_tiles, spb);
-  if (k <= 64)
-    return launch_pdl(temp_linear_kernel<32>, grid, block, smem, st, dependent, "temp_linear_kernel", z, Bi, Ci,
-                      idx, Ei, ki, gate_w, gate_b, tmin_tau, trange_tau, T, n_tiles, spb);
-  return launch_pdl(temp_linear_kernel<64>, grid, block, smem, st, dependent, "temp_linear_kernel", z, Bi, Ci, idx,
-                    Ei, ki, gate_w, gate_b, tmin_tau, trange_tau, T, n_tiles, spb);
+  MOCE_REQUIRE(B * E_r < ((int64_t)1 << 40) && C * 33 * 4 <= 200 * 1024 && E_r * k < ((int64_t)1 << 31),
+               MOCE_ERR_UNSUPPORTED, "moce_temperature: shape too large (C <= 1551)");
+  // 32-sample tiles x expert ranges (multiples of 32): about two CTAs per SM
+  const int n_stiles = (int)((B + kTs - 1) / kTs);
+  const int64_t rounds = (E_r + 31) / 32;
+  int64_t n_eg = (2LL * num_sms() + n_stiles - 1) / n_stiles;
+  if (n_eg > rounds) n_eg = rounds;
+  if (n_eg < 1) n_eg = 1;
+  const int e_per_cta = (int)(((rounds + n_eg - 1) / n_eg) * 32);
+  n_eg = (E_r + e_per_cta - 1) / e_per_cta;
+  const dim3 grid((unsigned)(n_stiles * n_eg)), block(kGateThreads);
+  const size_t smem = (size_t)C * 33 * 4;
+  return launch_pdl(temp_linear_kernel, grid, block, smem, (cudaStream_t)stream, dependent, "temp_linear_kernel", z,
+                    (int)B, (int)C, idx, (int)E_r, (int)k, gate_w, gate_b, tmin_tau, trange_tau, T, n_stiles,
+                    e_per_cta);
 }
 
 int temperature_mlp_run(const float* z, int64_t B, int64_t C, int64_t Hd, int64_t E_r, const float* w1,

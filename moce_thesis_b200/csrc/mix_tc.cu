@@ -39,6 +39,13 @@ namespace moce {
 
 __device__ int g_tc_fault = 0;
 
+// Where the first wait that ran out gave up (diagnostics; moce_tc_fault_info):
+// [0] set, [1] wait site (TcWaitSite), [2] parity, [3] unit or sample index,
+// [4] block, [5] thread, [6] C, [7] H*W, [8] E_r, [9] k, [10] B, [11] pixel
+// tiles per sample, [12] MMA N, [13] nanoseconds waited
+constexpr int kFaultInfoLen = 14;
+__device__ long long g_tc_fault_info[kFaultInfoLen];
+
 namespace {
 
 constexpr int kTcMaxN = 256;              // pixels per MMA (N), padded to 16
@@ -181,23 +188,48 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
+// The waits on another role, by barrier (recorded when one runs out).
+enum TcWaitSite {
+  kSiteSlotFree = 1,      // producer: a ring slot's MMAs done
+  kSiteDEmptySample = 2,  // issuer: accumulator buffer drained (one tile per sample)
+  kSiteAFull = 3,         // issuer: weights of a K-half written
+  kSiteDEmptyTile = 4,    // issuer: accumulator buffer drained (pixel tiles)
+  kSiteFullB = 5,         // issuer: staged X quarter landed
+  kSiteAFree = 6,         // weight rows: a K-half's MMAs of the previous sample done
+  kSiteDFull = 7,         // drain: accumulator complete
+};
+
 // Wait on another role, bounded by limit_ns; also gives up when another role
-// has aborted.  A wait that runs out raises the CTA's abort flag and
-// g_tc_fault.
-__device__ __forceinline__ bool mbar_wait_abort(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                                uint64_t limit_ns) {
+// has aborted.  Returns 1 when the phase completed, 0 when another role
+// aborted, -1 when this wait ran out (the CTA's abort flag and g_tc_fault
+// are then raised).
+__device__ __forceinline__ int mbar_wait_peer(uint64_t* bar, uint32_t parity, volatile int* abort, uint64_t limit_ns,
+                                              uint64_t* waited) {
   const uint32_t a = smem_u32(bar);
-  if (mbar_try(a, parity)) return true;
+  if (mbar_try(a, parity)) return 1;
   const uint64_t t0 = global_ns();
+  uint64_t dt = 0;
   for (;;) {
     for (int i = 0; i < 32; ++i)
-      if (mbar_try(a, parity)) return true;
-    if (*abort) return false;
-    if (global_ns() - t0 > limit_ns) break;
+      if (mbar_try(a, parity)) return 1;
+    if (*abort) return 0;
+    dt = global_ns() - t0;
+    if (dt > limit_ns) break;
   }
   *abort = 1;
   atomicExch(&g_tc_fault, 1);
-  return false;
+  *waited = dt;
+  return -1;
+}
+
+// Records the first wait that ran out on the device (later ones are dropped).
+__device__ __noinline__ void record_tc_fault(int site, int parity, int unit, int C, int HW, int E_r, int k, int B,
+                                             int NT, int NP, uint64_t waited) {
+  if (atomicCAS(reinterpret_cast<unsigned long long*>(&g_tc_fault_info[0]), 0ull, 1ull) != 0ull) return;
+  const long long v[kFaultInfoLen] = {1, site, parity, unit, (long long)blockIdx.x, (long long)threadIdx.x, C, HW,
+                                      E_r, k, B, NT, NP, (long long)waited};
+  for (int i = 1; i < kFaultInfoLen; ++i) g_tc_fault_info[i] = v[i];
+  __threadfence();
 }
 
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -329,8 +361,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   TcBars* bars = reinterpret_cast<TcBars*>(reinterpret_cast<unsigned char*>(stg) + a.stage_bytes);
   volatile int* abort = &bars->abort;
   const uint64_t wlim = a.wait_ns;
+  const int Bn = a.B;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // a bounded wait on another role; one that runs out records where
+  auto wait_peer = [&](uint64_t* bar, uint32_t parity, int site, int unit) -> bool {
+    uint64_t waited = 0;
+    const int r = mbar_wait_peer(bar, parity, abort, wlim, &waited);
+    if (r < 0) record_tc_fault(site, (int)parity, unit, C, HW, E_r, k, Bn, NT, NP, waited);
+    return r > 0;
+  };
   const int tile = blockIdx.x % a.n_tiles, bsplit = blockIdx.x / a.n_tiles;
   const int e0 = tile * 128;
   const int rows = min(128, E_r - e0);
@@ -344,7 +384,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   // all threads zero A, so that those latencies overlap the zeroing.
   const unsigned char* xs = static_cast<const unsigned char*>(a.xstage) + (size_t)b0 * NT * sbytes;
   const int nu = nb * NT;                                     // units (sample, pixel tile) of this CTA
-  const int n_pre = min(NS, 4 * nu);                          // copies issued in the prologue
+  // X quarter n = 4u + q of unit u goes to a slot of the ring.  With two
+  // issuers (P == 2) issuer h consumes quarters 2h and 2h+1 of every unit
+  // from a ring of its own (slots [0, NS0) for K-half 0, [NS0, NS) for K-half
+  // 1), so that every slot's full barrier has one consumer, which has waited
+  // for each earlier phase of it.  (A slot shared by the two issuers lets one
+  // of them wait for a copy while the slot's previous copy, consumed by the
+  // other, is still landing; a parity wait for a phase two ahead of the
+  // barrier then passes at once, and the ring's accounting breaks.)
+  const int NS0 = (P == 2) ? (NS + 1) / 2 : NS, NS1 = (P == 2) ? NS / 2 : 0;
+  auto ring_slot = [&](int n, int& slot, int& use) {
+    if (P == 2) {
+      const int h = (n >> 1) & 1, m = 2 * (n >> 2) + (n & 1);
+      const int nsh = h ? NS1 : NS0;
+      slot = (h ? NS0 : 0) + m % nsh;
+      use = m / nsh;
+    } else {
+      slot = n % NS;
+      use = n / NS;
+    }
+  };
+  int n_pre = 0;                                              // copies issued in the prologue
   if (tid == kWarpProducer * 32) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&bars->full_b[s], 1);
@@ -362,10 +422,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     // staged X comes from pass 1, which may still run when this grid is a
     // programmatic dependent of it (moce_forward_tc); a no-op otherwise
     grid_dep_wait();
-    for (int n = 0; n < n_pre; ++n) {
-      mbar_expect_tx(&bars->full_b[n], qbytes);
-      bulk_g2s(smem_u32(sB) + (uint32_t)n * qbytes, xs + (size_t)(n >> 2) * sbytes + (size_t)(n & 3) * qbytes,
-               qbytes, &bars->full_b[n]);
+    // the leading copies that take a slot's first use need no wait
+    for (; n_pre < 4 * nu; ++n_pre) {
+      int slot, use;
+      ring_slot(n_pre, slot, use);
+      if (use > 0) break;
+      mbar_expect_tx(&bars->full_b[slot], qbytes);
+      bulk_g2s(smem_u32(sB) + (uint32_t)slot * qbytes,
+               xs + (size_t)(n_pre >> 2) * sbytes + (size_t)(n_pre & 3) * qbytes, qbytes, &bars->full_b[slot]);
     }
   }
   // weight rows: threads 2r and 2r+1 share expert row e0 + r, each with KH
@@ -413,16 +477,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       const int total = 4 * nu;
       int n = n_pre;
       for (; n < total; ++n) {
-        const int slot = n % NS, use = n / NS;
-        if (use >= 1 && !mbar_wait_abort(&bars->slot_free[slot], (use - 1) & 1, abort, wlim)) break;
+        int slot, use;
+        ring_slot(n, slot, use);
+        if (use >= 1 && !wait_peer(&bars->slot_free[slot], (use - 1) & 1, kSiteSlotFree, n)) break;
         mbar_expect_tx(&bars->full_b[slot], qbytes);
         bulk_g2s(aB + (uint32_t)slot * qbytes, xs + (size_t)(n >> 2) * sbytes + (size_t)(n & 3) * qbytes, qbytes,
                  &bars->full_b[slot]);
       }
       // copies still in flight land before the block can exit (no-op on the
-      // normal path: the issuers consumed every slot)
-      for (int m = (n > NS ? n - NS : 0); m < n; ++m)
-        if (!mbar_wait(&bars->full_b[m % NS], (m / NS) & 1)) atomicExch(&g_tc_fault, 1);
+      // normal path: the issuers consumed every slot): the most recent use
+      // of every slot of each ring
+      for (int h = 0; h < (P == 2 ? 2 : 1); ++h) {
+        const int nsh = (P == 2 && h) ? NS1 : NS0, base = h ? NS0 : 0;
+        const int issued = (P == 2) ? 2 * (n >> 2) + min(2, max(0, (n & 3) - 2 * h)) : n;
+        for (int j = max(0, issued - nsh); j < issued; ++j)
+          if (!mbar_wait(&bars->full_b[base + j % nsh], (j / nsh) & 1)) atomicExch(&g_tc_fault, 1);
+      }
     }
   } else if (warp == kWarpIssuer0 || warp == kWarpIssuer0 + 1) {
     // ===================== MMA issuers.  P == 2: issuer h takes K-half h
@@ -443,16 +513,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       for (int i = 0; i < nb && run; ++i) {
         // one tile per sample: the accumulator buffer first, as it frees
         // earlier than the next weights
-        if (NT == 1 && i >= 2 && !mbar_wait_abort(&bars->d_empty[i & 1], ((i - 2) >> 1) & 1, abort, wlim)) break;
+        if (NT == 1 && i >= 2 && !wait_peer(&bars->d_empty[i & 1], ((i - 2) >> 1) & 1, kSiteDEmptySample, i)) break;
         // this sample's weights (A), both halves of this issuer
         for (int h = h0; h < h1 && run; ++h)
-          if (!mbar_wait_abort(&bars->a_full[h], i & 1, abort, wlim)) run = false;
+          if (!wait_peer(&bars->a_full[h], i & 1, kSiteAFull, i)) run = false;
         if (!run) break;
         tc_fence_after();
         for (int t = 0; t < NT && run; ++t) {
           const int u = i * NT + t, s = u & 1;
           if (NT > 1 && u >= 2) {
-            if (!mbar_wait_abort(&bars->d_empty[s], ((u - 2) >> 1) & 1, abort, wlim)) {
+            if (!wait_peer(&bars->d_empty[s], ((u - 2) >> 1) & 1, kSiteDEmptyTile, u)) {
               run = false;
               break;
             }
@@ -461,8 +531,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
           for (int h = h0; h < h1 && run; ++h) {
             const uint32_t d = tmem + (uint32_t)(s * P * NP + (P == 2 ? h : 0) * NP);
             for (int qq = 0; qq < 2; ++qq) {
-              const int q = 2 * h + qq, n = 4 * u + q, slot = n % NS;
-              if (!mbar_wait_abort(&bars->full_b[slot], (n / NS) & 1, abort, wlim)) {
+              const int q = 2 * h + qq, n = 4 * u + q;
+              int slot, use;
+              ring_slot(n, slot, use);
+              if (!wait_peer(&bars->full_b[slot], use & 1, kSiteFullB, n)) {
                 run = false;
                 break;
               }
@@ -526,7 +598,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       for (int h = 0; h < 2; ++h) {
         // the previous sample's MMAs have released this half of A
         bool w_ok = true;
-        if (i >= 1 && tid == 0) w_ok = mbar_wait_abort(&bars->a_free[h], (i - 1) & 1, abort, wlim);
+        if (i >= 1 && tid == 0) w_ok = wait_peer(&bars->a_free[h], (i - 1) & 1, kSiteAFree, i);
         if (i >= 1) w_ok = role_sync_and(kBarWeights, WT, w_ok);
         if (!w_ok) {
           ok = false;
@@ -571,7 +643,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       for (int u = 0; u < nu; ++u) {
         const int s = u & 1;
         bool ok = true;
-        if (dlead) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort, wlim);
+        if (dlead) ok = wait_peer(&bars->d_full[s], (u >> 1) & 1, kSiteDFull, u);
         if (dlead) bulk_wait_read();                          // the previous sample's copy left the block
         if (!role_sync_and(kBarDrain, DT, ok)) break;
         tc_fence_after();
@@ -633,7 +705,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         const int p0 = t * NP, tp = min(NP, HW - p0);       // a multiple of 8
         unsigned char* row = row0 + (size_t)(u % a.nsb) * 128u * pitch;
         bool ok = true;
-        if (dlead) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort, wlim);
+        if (dlead) ok = wait_peer(&bars->d_full[s], (u >> 1) & 1, kSiteDFull, u);
         // this thread's copy out of this buffer, nsb units ago, has read it
         if (a.nsb == 2) bulk_wait_read_all_but1();
         else bulk_wait_read();
@@ -722,7 +794,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         const int s = u & 1, i = u / NT, t = u - (u / NT) * NT;
         const int p0 = t * NP, tp = min(NP, HW - p0);
         bool ok = true;
-        if (dlead) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort, wlim);
+        if (dlead) ok = wait_peer(&bars->d_full[s], (u >> 1) & 1, kSiteDFull, u);
         if (!role_sync_and(kBarDrain, DT, ok)) break;
         tc_fence_after();
         const uint32_t tb = tmem + lane_base + (uint32_t)(s * P * NP);
@@ -770,7 +842,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         const int s = u & 1, i = u / NT, t = u - (u / NT) * NT;
         const int p0 = t * NP, tp = min(NP, HW - p0);         // this tile's pixels
         bool ok = true;
-        if (dlead) ok = mbar_wait_abort(&bars->d_full[s], (u >> 1) & 1, abort, wlim);
+        if (dlead) ok = wait_peer(&bars->d_full[s], (u >> 1) & 1, kSiteDFull, u);
         bulk_wait_read();                                     // this thread's copy left the staging area
         if (!role_sync_and(kBarDrain, DT, ok)) break;
         tc_fence_after();
@@ -1076,6 +1148,21 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
       return check_launch("mix_tc_kernel");
     }
   });
+}
+
+extern "C" int moce_tc_fault_info(int64_t* info, int n, int clear) {
+  MOCE_REQUIRE(info && n >= 1, MOCE_ERR_INVALID, "moce_tc_fault_info: null pointer");
+  long long v[kFaultInfoLen];
+  if (cudaDeviceSynchronize() != cudaSuccess ||
+      cudaMemcpyFromSymbol(v, g_tc_fault_info, sizeof(v)) != cudaSuccess)
+    return set_error(MOCE_ERR_CUDA, "moce_tc_fault_info: read failed");
+  for (int i = 0; i < n; ++i) info[i] = i < kFaultInfoLen ? (int64_t)v[i] : 0;
+  if (clear) {
+    const long long zero[kFaultInfoLen] = {};
+    if (cudaMemcpyToSymbol(g_tc_fault_info, zero, sizeof(zero)) != cudaSuccess)
+      return set_error(MOCE_ERR_CUDA, "moce_tc_fault_info: clear failed");
+  }
+  return MOCE_OK;
 }
 
 extern "C" int moce_tc_fault(int* flag, int clear) {

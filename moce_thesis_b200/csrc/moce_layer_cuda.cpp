@@ -892,4 +892,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     return flag;
   }, "Device flag set when a bounded wait inside a tensor-core kernel ran out (synchronises)",
         py::arg("clear") = true);
+  m.def("tc_fault_info", [](bool clear) {
+    std::vector<int64_t> v(14, 0);
+    ok(moce_tc_fault_info(v.data(), 14, clear ? 1 : 0));
+    return v;
+  }, "Where the first bounded wait that ran out gave up (14 integers, see moce_tc_fault_info)",
+        py::arg("clear") = true);
 }

@@ -46,9 +46,14 @@ def check_faults(clear: bool = True) -> None:
     """Raise if a bounded wait inside a tensor-core kernel ran out since the
     last check (the device flag moce_tc_fault reads).  Synchronises the
     current device; call it after a batch of forwards."""
-    if native().tc_fault(bool(clear)):
+    m = native()
+    if m.tc_fault(bool(clear)):
+        info = m.tc_fault_info(bool(clear))
+        names = ("set", "site", "parity", "unit", "block", "thread", "C", "HW", "E_r", "k", "B", "tiles", "N",
+                 "waited_ns")
         raise RuntimeError("MoCE tensor-core kernel: a bounded wait ran out; the outputs of the launches since "
-                           "the last check are incomplete")
+                           "the last check are incomplete (" + ", ".join(f"{n}={v}" for n, v in zip(names, info)) +
+                           ")")
 
 
 class _Route:
