@@ -156,21 +156,17 @@ def pass_fns(mc, r, xs, ys, zs, nsets, Bs, Cs, HW, Es, Ks, gwf, gbf, tmin_tau, t
     if mc.tc_supported(x0, Ks):
         nst = capi.lib().moce_tc_stage_bytes(Bs, Cs, HW)
         sts = [torch.empty(nst, dtype=torch.uint8, device=dev) for _ in range(nsets)]
-        Ts = [torch.empty(Bs, Es - 1, device=dev) for _ in range(nsets)]
 
         def pass1(i):
-            # pass 1 (pool, residual, operand staging) and the temperatures
             capi.call("moce_pool_stage", xs[i % nsets].data_ptr(), dcode, Bs, Cs, HW, r.mask.data_ptr(),
                       r.meta.data_ptr(), zs[i % nsets].data_ptr(), ys[i % nsets].data_ptr(), Es - 1,
                       sts[i % nsets].data_ptr(), capi.stream_handle())
-            capi.call("moce_temperature", zs[i % nsets].data_ptr(), Bs, Cs, r.idx.data_ptr(), Es - 1, Ks,
-                      gwf.data_ptr(), gbf.data_ptr(), tmin_tau, trange_tau, Ts[i % nsets].data_ptr(),
-                      capi.stream_handle())
 
         def pass2(i):
-            capi.call("moce_mix_tc", sts[i % nsets].data_ptr(), dcode, Bs, Cs, HW, Ts[i % nsets].data_ptr(),
-                      r.idx.data_ptr(), r.ln.data_ptr(), Es - 1, Ks, ys[i % nsets].data_ptr(), capi.stream_handle())
-        return pass1, pass2, ("pass1_pool_stage_and_temperature", "pass2_mix_tc")
+            capi.call("moce_mix_tc", sts[i % nsets].data_ptr(), dcode, Bs, Cs, HW, zs[i % nsets].data_ptr(),
+                      r.idx.data_ptr(), r.ln.data_ptr(), Es - 1, Ks, gwf.data_ptr(), gbf.data_ptr(), tmin_tau,
+                      trange_tau, ys[i % nsets].data_ptr(), None, capi.stream_handle())
+        return pass1, pass2, ("pass1_pool_stage", "pass2_mix_tc")
 
     def pool(i):
         capi.call("moce_pool_residual", xs[i % nsets].data_ptr(), dcode, Bs, Cs, HW, r.mask.data_ptr(),
@@ -354,7 +350,7 @@ def run_ours(args):
                      "peak_kind": f"{peak_kind} copy bandwidth"},
         "e2e": {"value": round(e2e, 3), "unit": "GB/s", "h2d_bytes_per_step": xb, "d2h_bytes_per_step": yb,
                 "api": "moce_thesis_b200.MoCE.forward_host, pinned host X in, host Y out"},
-        "gpu_launches": (3 if use_tc else 2) * args.steps,
+        "gpu_launches": 2 * args.steps,
         "clocks": clk.summary(),
     }
     check_faults()

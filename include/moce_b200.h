@@ -151,14 +151,15 @@ int moce_temperature_mlp(const float* z, int64_t B, int64_t C, int64_t Hd,
  * each row's 16-byte units swizzled by (channel mod 8).  moce_tc_stage_bytes
  * gives its size.
  *
- * moce_mix_tc: pass 2.  The routed experts 0 .. E_r-1 of y from the staged X
- * and the temperatures T fp32 [B, E_r] (moce_temperature or
- * moce_temperature_mlp): the softmax of ln / T (MoCE.py:219-221 / 188) and
- * the gather-mix (moce_kernel.cu:57-141), computed per sample as a dense
- * product of the 128-expert weight tile (zero off the supports) with the
- * staged X (bulk copies into shared memory, tcgen05.mma with the accumulator
- * in tensor memory).  Weights are rounded to the input's 16-bit type before
- * the product (fp32 accumulation).
+ * moce_mix_tc: pass 2.  Same outputs as moce_mix_scheduled; the routed
+ * experts are computed per sample as a dense product of the 128-expert weight
+ * tile (zero off the supports) with the staged X (bulk copies into shared
+ * memory, tcgen05.mma with the accumulator in tensor memory).  The gate and
+ * temperature (MoCE.py:216-218) and the softmax of ln / T (MoCE.py:219-221)
+ * are computed in the kernel from z.  Weights are rounded to the input's
+ * 16-bit type before the product (fp32 accumulation).
+ * moce_mix_tc_t: the same with the temperatures T fp32 [B, E_r] given (e.g.
+ * from moce_temperature_mlp) in place of z and the Linear(k,1) gate.
  *
  * Waits inside the kernel are bounded in time.  If a wait of one role of the
  * kernel on another runs out (about one second by default), the kernel sets a
@@ -178,9 +179,14 @@ int moce_pool_stage(const void* x, int dtype, int64_t B, int64_t C,
                     float* z, void* y, int64_t E_r, void* xstage,
                     void* stream);
 int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C,
-                int64_t HW, const float* T, const int32_t* idx,
-                const float* ln, int64_t E_r, int64_t k, void* y,
-                void* stream);
+                int64_t HW, const float* z, const int32_t* idx,
+                const float* ln, int64_t E_r, int64_t k, const float* gate_w,
+                const float* gate_b, float tmin_tau, float trange_tau,
+                void* y, float* T_out, void* stream);
+int moce_mix_tc_t(const void* xstage, int dtype, int64_t B, int64_t C,
+                  int64_t HW, const float* T, const int32_t* idx,
+                  const float* ln, int64_t E_r, int64_t k, void* y,
+                  void* stream);
 int moce_tc_fault(int* flag, int clear);
 int64_t moce_tc_wait_limit_ns(int64_t ns);
 /* Where the first wait that ran out gave up, for diagnostics (synchronises):
@@ -194,23 +200,24 @@ int64_t moce_tc_wait_limit_ns(int64_t ns);
 int moce_tc_fault_info(int64_t* info, int n, int clear);
 
 /*
- * The tensor-core forward in one call: moce_pool_stage, moce_temperature and
- * moce_mix_tc, each launched as a programmatic dependent of the one before
- * (its prologue overlaps the previous kernel; its reads wait for that
- * kernel's results).  Same buffers and conditions as the three calls; T
- * (fp32 [B, E_r]) is required, the mix reads it.
+ * Both tensor-core passes in one call: moce_pool_stage, then moce_mix_tc
+ * launched as a programmatic dependent of it (the mix's prologue overlaps
+ * pass 1; its reads of z and xstage wait for pass 1 to complete).  Same
+ * buffers and conditions as the two calls.
  */
 int moce_forward_tc(const void* x, int dtype, int64_t B, int64_t C, int64_t HW,
                     const int32_t* mask, const int32_t* meta,
                     const int32_t* idx, const float* ln, int64_t E_r,
                     int64_t k, const float* gate_w, const float* gate_b,
                     float tmin_tau, float trange_tau, float* z, void* xstage,
-                    void* y, float* T, void* stream);
+                    void* y, float* T_out, void* stream);
 
 /*
- * moce_forward_tc with the two-layer temperature gate (moce_temperature_mlp)
- * in place of the shared Linear(k, 1): z, the hidden layer h fp32 [B, Hd]
- * and T are outputs.  No reference counterpart (see moce_temperature_mlp).
+ * The tensor-core forward with the two-layer temperature gate
+ * (moce_temperature_mlp) in place of the shared Linear(k, 1): pass 1, the
+ * gate, then moce_mix_tc_t, each a programmatic dependent of the launch
+ * before.  z, the hidden layer h fp32 [B, Hd] and T (required) are outputs.
+ * No reference counterpart (see moce_temperature_mlp).
  */
 int moce_forward_tc_mlp(const void* x, int dtype, int64_t B, int64_t C,
                         int64_t HW, const int32_t* mask, const int32_t* meta,
@@ -229,7 +236,7 @@ int moce_forward_tc_mlp(const void* x, int dtype, int64_t B, int64_t C,
  * BatchNorm2d folded to scale = weight / sqrt(running_var + eps),
  * shift = bias - running_mean * scale.  Replaces the MoCE -> bn1 -> relu1
  * sequence of BottleneckWithMoCEProjection.forward (models_unified.py:155-165).
- * T (required) and z are the layer's own values, before the epilogue.
+ * T_out (when given) and z are the layer's own values, before the epilogue.
  */
 int moce_forward_tc_ep(const void* x, int dtype, int64_t B, int64_t C,
                        int64_t HW, const int32_t* mask, const int32_t* meta,
@@ -238,7 +245,7 @@ int moce_forward_tc_ep(const void* x, int dtype, int64_t B, int64_t C,
                        float tmin_tau, float trange_tau,
                        const float* out_scale, const float* out_shift,
                        int out_relu, float* z, void* xstage, void* y,
-                       float* T, void* stream);
+                       float* T_out, void* stream);
 
 /*
  * CUDA-core pass 2 with lanes over pixels, any dtype, H*W <= 512, k <= 64,

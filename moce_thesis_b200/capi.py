@@ -36,7 +36,8 @@ SIGNATURES = {
     "moce_tc_stage_bytes": (_sz, [_i64, _i64, _i64]),
     "moce_tc_supported": (_i32, [_i32, _i64, _i64, _i64]),
     "moce_pool_stage": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _p, _p]),
-    "moce_mix_tc": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p]),
+    "moce_mix_tc": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p, _f32, _f32, _p, _p, _p]),
+    "moce_mix_tc_t": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _p, _p]),
     "moce_temperature": (_i32, [_p, _i64, _i64, _p, _i64, _i64, _p, _p, _f32, _f32, _p, _p]),
     "moce_temperature_mlp": (_i32, [_p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _f32, _f32, _p, _p, _p]),
     "moce_forward_tc_mlp": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _i64, _p, _p, _p, _p,

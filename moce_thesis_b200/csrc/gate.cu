@@ -192,8 +192,13 @@ int temperature_run(const float* z, int64_t B, int64_t C, const int32_t* idx, in
   if (B == 0) return MOCE_OK;
   MOCE_REQUIRE(z && idx && gate_w && gate_b && T, MOCE_ERR_INVALID, "moce_temperature: null pointer argument");
   MOCE_REQUIRE(B > 0 && C >= 1 && E_r >= 1 && k >= 1 && k <= C, MOCE_ERR_INVALID, "moce_temperature: invalid shape");
-  MOCE_REQUIRE(B * E_r < ((int64_t)1 << 40) && C * 33 * 4 <= 200 * 1024 && E_r * k < ((int64_t)1 << 31),
-               MOCE_ERR_UNSUPPORTED, "moce_temperature: shape too large (C <= 1551)");
+  MOCE_REQUIRE(B * E_r < ((int64_t)1 << 40) && E_r * k < ((int64_t)1 << 31), MOCE_ERR_UNSUPPORTED,
+               "moce_temperature: shape too large");
+  // channels beyond the transposed staging's shared memory: the general gate
+  // kernel from the pooled means (a warp per expert row)
+  if (C * 33 * 4 > 200 * 1024)
+    return moce_gate_temperature(nullptr, MOCE_F32, z, B, C, 1, idx, E_r, k, gate_w, gate_b, tmin_tau, trange_tau,
+                                 nullptr, T, stream);
   // 32-sample tiles x expert ranges (multiples of 32): about two CTAs per SM
   const int n_stiles = (int)((B + kTs - 1) / kTs);
   const int64_t rounds = (E_r + 31) / 32;

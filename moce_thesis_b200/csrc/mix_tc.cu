@@ -139,9 +139,14 @@ __device__ __forceinline__ uint32_t a_off(int row, int c) {
 struct TcArgs {
   const void* xstage;             // [B, Kp, 128 B] operand-layout copy of X (pass 1)
   void* y;
-  const float* T;                 // [B, E_r] temperatures (the temperature kernel, between the passes)
+  const float* z;                 // [B, C] pooled means (pass 1), for the Linear(k,1) gate in the weight rows
   const int32_t* idx;
   const float* ln;
+  const float* gate_w;
+  const float* gate_b;
+  float* T_out;                   // [B, E_r] temperatures out, or null
+  float tmin_tau, trange_tau;
+  const float* T;                 // [B, E_r] temperatures given (kTin: a gate computed before the pass)
   int B, C, HW, E_r, k, Kp;       // Kp: C rounded up to 64
   int n_tiles, n_bsplit;
   int ns;                         // X quarter slots in the ring
@@ -182,6 +187,14 @@ struct TcBars {
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// One arrival for the whole warp: every lane's preceding writes (ordered for
+// the async proxy, or its tensor-memory loads, by the fence the caller ran)
+// are covered by the warp barrier, then lane 0 arrives.
+__device__ __forceinline__ void mbar_arrive_warp(uint64_t* bar) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
 }
 
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
@@ -321,11 +334,12 @@ constexpr int kWarpIssuer0 = 12, kWarpProducer = 14;
 // Roles (warp-specialized, one CTA per SM):
 //   warps 0-7   weight rows: threads 2r and 2r+1 share expert row e0 + r,
 //               each with half of its supports (a pair of adjacent lanes
-//               combines sums by shuffle); per sample the softmax of
-//               ln / T (MoCE.py:219-221 / 188) with T[b, e] read from the
-//               temperature kernel's output, written as bf16/fp16 into A
-//               one K-half at a time, as soon as the MMAs of the previous
-//               sample have released that half
+//               combines sums by shuffle); per sample the gate and
+//               temperature (MoCE.py:216-218 / 175-178; kTin: T[b, e] read
+//               from a gate computed before the pass) and the softmax
+//               (MoCE.py:219-221 / 188), written as bf16/fp16 into A one
+//               K-half at a time, as soon as the MMAs of the previous sample
+//               have released that half
 //   warps 8-11  drain: sum of the two partial accumulators (tcgen05.ld),
 //               output rows through a shared staging block, one bulk store
 //   warp 12, 13 lane 0: MMA issuers, K-half 0 / 1, each into its own partial
@@ -343,7 +357,7 @@ constexpr int kWarpIssuer0 = 12, kWarpProducer = 14;
 // tiles) and eight drain warps (4-11), two per tensor-memory lane quarter,
 // each taking one half of a tile's 32-column chunks: the drain of a
 // 128 x 256 tile, not the MMAs, sets the pace of these maps.
-template <typename T, int KMAX, bool kGen, bool kEp, bool kW1>
+template <typename T, int KMAX, bool kGen, bool kEp, bool kW1, bool kTin>
 __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   constexpr int WT = kW1 ? 128 : kWeightThreads;              // weight threads
   constexpr int DT = kW1 ? 256 : kDrainThreads;               // drain threads
@@ -358,7 +372,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   unsigned char* sA = base;                                   // 128 x Kp : Kp * 256 B
   unsigned char* sB = sA + (size_t)Kp * 256;                  // NS quarter slots
   T* stg = reinterpret_cast<T*>(sB + (size_t)NS * qbytes);    // output staging area
-  TcBars* bars = reinterpret_cast<TcBars*>(reinterpret_cast<unsigned char*>(stg) + a.stage_bytes);
+  float* s_z = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(stg) + a.stage_bytes);
+  float* s_gw = s_z + 2 * Kp;
+  TcBars* bars = reinterpret_cast<TcBars*>(s_gw + KMAX);
   volatile int* abort = &bars->abort;
   const uint64_t wlim = a.wait_ns;
   const int Bn = a.B;
@@ -411,10 +427,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       mbar_init(&bars->slot_free[s], 1);
     }
     for (int h = 0; h < 2; ++h) {
-      mbar_init(&bars->a_full[h], WT);
+      mbar_init(&bars->a_full[h], WT / 32);                    // one arrival per weight warp
       mbar_init(&bars->a_free[h], 1);
       mbar_init(&bars->d_full[h], P);
-      mbar_init(&bars->d_empty[h], DT);
+      mbar_init(&bars->d_empty[h], DT / 32);                   // one arrival per drain warp
       mbar_init(&bars->fin[h], 1);
     }
     bars->abort = 0;
@@ -440,7 +456,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   uint32_t chp[KH];                                           // channel << 17 | byte offset in A
   float ln2[KH];
   float mx2 = -INFINITY;
-  float t_next = 1.0f;                                        // this row's temperature, one sample ahead
+  float t_next = 1.0f;                                        // kTin: this row's temperature, one sample ahead
+  // !kTin: gate weights of this thread's supports in registers (k <= 32),
+  // else read from shared memory per sample; z of the next sample in flight
+  constexpr bool kGwReg = KMAX <= 32 && !kTin;
+  float gwr[kGwReg ? KH : 1];
+  constexpr int ZPT = kTin ? 1 : 512 / WT;                    // z values per weight thread (C <= 512)
+  float zr[ZPT];
   if (tid < WT) {
 #pragma unroll
     for (int jj = 0; jj < KH; ++jj) {
@@ -454,11 +476,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         ln2[jj] = a.ln[o] * 1.4426950408889634f;            // log2(e)
         mx2 = nan_max(mx2, ln2[jj]);
       }
+      if constexpr (kGwReg) gwr[jj] = (j < k) ? a.gate_w[j] : 0.0f;
     }
-    grid_dep_wait();                                          // T comes from the temperature kernel (see above)
-    if (nb > 0 && w_row) t_next = a.T[(size_t)b0 * E_r + e0 + row];
+    grid_dep_wait();                                          // z or T come from the launch before (see above)
+    if constexpr (kTin) {
+      if (nb > 0 && w_row) t_next = a.T[(size_t)b0 * E_r + e0 + row];
+    } else {
+#pragma unroll
+      for (int u = 0; u < ZPT; ++u) {
+        const int c = tid + u * WT;
+        zr[u] = (nb > 0 && c < C) ? a.z[(size_t)b0 * C + c] : 0.0f;
+      }
+    }
   }
   for (int q = tid; q < Kp * 256 / 16; q += blockDim.x) reinterpret_cast<int4*>(sA)[q] = make_int4(0, 0, 0, 0);
+  if constexpr (!kTin)
+    for (int i = tid; i < k; i += blockDim.x) s_gw[i] = a.gate_w[i];
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&bars->tmem)),
                  "r"(a.tmem_cols));
@@ -576,13 +609,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     // recomputed per half to stay within the register budget
     constexpr bool kKeepW = KMAX <= 32;
     if constexpr (!kW1) mx2 = nan_max(mx2, __shfl_xor_sync(kFull, mx2, 1));
+    const float bias = kTin ? 0.0f : a.gate_b[0];
     bool ok = true;
     for (int i = 0; i < nb && ok; ++i) {
       const int b = b0 + i;
-      // this sample's temperature (MoCE.py:216-218, computed between the
-      // passes), the next one's load in flight behind the softmax and stores
-      const float t = t_next;
-      if (i + 1 < nb && has_row) t_next = a.T[(size_t)(b + 1) * E_r + e];
+      float t;
+      if constexpr (kTin) {
+        // the temperature computed before the pass, the next sample's load
+        // in flight behind this sample's softmax and stores
+        t = t_next;
+        if (i + 1 < nb && has_row) t_next = a.T[(size_t)(b + 1) * E_r + e];
+      } else {
+        // the shared Linear(k,1) gate on the pooled values of this row's
+        // supports and the temperature (MoCE.py:216-218 / 175-178)
+        float* szb = s_z + (i & 1) * Kp;
+#pragma unroll
+        for (int u = 0; u < ZPT; ++u)
+          if (tid + u * WT < C) szb[tid + u * WT] = zr[u];
+        role_sync(kBarWeights, WT);
+        if (i + 1 < nb) {
+#pragma unroll
+          for (int u = 0; u < ZPT; ++u) {
+            const int c = tid + u * WT;
+            if (c < C) zr[u] = a.z[(size_t)(b + 1) * C + c];
+          }
+        }
+        float gp = 0.0f;
+#pragma unroll
+        for (int jj = 0; jj < KH; ++jj)
+          if (part * KH + jj < k && has_row) gp += (kGwReg ? gwr[jj] : s_gw[part * KH + jj]) * szb[chp[jj] >> 17];
+        const float g = bias + gp + (kW1 ? 0.0f : __shfl_xor_sync(kFull, gp, 1));
+        t = temperature(g, a.tmin_tau, a.trange_tau, nullptr);
+        if (a.T_out && has_row && part == 0) a.T_out[(size_t)b * E_r + e] = t;
+      }
       const float it = 1.0f / t;
       const float m2 = mx2 * it;
       float wv[kKeepW ? KH : 1];
@@ -617,7 +676,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
           }
         }
         proxy_fence_smem();
-        mbar_arrive(&bars->a_full[h]);
+        mbar_arrive_warp(&bars->a_full[h]);
       }
     }
   } else if (tid < WT + DT) {
@@ -679,7 +738,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
           }
         }
         tc_fence_before();
-        mbar_arrive(&bars->d_empty[s]);
+        mbar_arrive_warp(&bars->d_empty[s]);
         proxy_fence_smem();
         role_sync(kBarDrain, DT);
         T* dst = yg + ((size_t)(b0 + u) * E + e0) * HW;
@@ -741,7 +800,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         }
         if (c_lo >= c_hi) {                                   // nothing to read (uniform across the warp)
           tc_fence_before();
-          mbar_arrive(&bars->d_empty[s]);
+          mbar_arrive_warp(&bars->d_empty[s]);
         } else if (P == 1) {
           // one accumulator: two 32-column chunks in flight (r0 / r1), so
           // each load's latency overlaps the conversion and stores of the
@@ -754,7 +813,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
               tmem_ld32_nowait(tb + cb + 32, r1);
             } else {
               tc_fence_before();
-              mbar_arrive(&bars->d_empty[s]);
+              mbar_arrive_warp(&bars->d_empty[s]);
             }
             put(r0, r0, cb);
             if (cb + 32 >= c_hi) break;
@@ -763,7 +822,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
               tmem_ld32_nowait(tb + cb + 64, r0);
             } else {
               tc_fence_before();
-              mbar_arrive(&bars->d_empty[s]);
+              mbar_arrive_warp(&bars->d_empty[s]);
             }
             put(r1, r1, cb + 32);
             tmem_wait_ld();
@@ -776,7 +835,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
             tmem_wait_ld();
             if (cb + 32 >= c_hi) {                            // last read of the buffer
               tc_fence_before();
-              mbar_arrive(&bars->d_empty[s]);
+              mbar_arrive_warp(&bars->d_empty[s]);
             }
             put(r0, r1, cb);
           }
@@ -806,7 +865,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
           tmem_wait_ld();
           if (cb + 32 >= tp) {                                // last read of the buffer
             tc_fence_before();
-            mbar_arrive(&bars->d_empty[s]);
+            mbar_arrive_warp(&bars->d_empty[s]);
           }
           if (has_row) {
             float v[32];
@@ -862,7 +921,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
           }
         }
         tc_fence_before();
-        mbar_arrive(&bars->d_empty[s]);
+        mbar_arrive_warp(&bars->d_empty[s]);
         if (has_row) {
           T* dst = yg + ((size_t)(b0 + i) * E + e0 + dt) * HW + p0;
           const uint32_t nbytes = (uint32_t)(tp * sizeof(T));
@@ -924,7 +983,7 @@ TcShape tc_shape(int64_t C, int64_t HW, int64_t k, bool y_aligned, int np_max) {
   t.tmem_cols = cols;
   t.KMAX = k <= 16 ? 16 : k <= 32 ? 32 : 64;
   t.qbytes = (size_t)t.Kp * t.NA * 32;
-  const size_t base = 1024 + (size_t)t.Kp * 256 + sizeof(TcBars);
+  const size_t base = 1024 + (size_t)t.Kp * 256 + (size_t)t.Kp * 8 + (size_t)t.KMAX * 4 + sizeof(TcBars);
   const size_t smem_max = (size_t)smem_optin_tc();
   auto slots = [&](size_t stage) -> int {
     const size_t f = base + stage;
@@ -1012,9 +1071,20 @@ extern "C" size_t moce_tc_stage_bytes(int64_t B, int64_t C, int64_t HW) {
   return (size_t)B * (size_t)NT * (size_t)((C + 63) / 64 * 64) * (size_t)NA * 128;
 }
 
-static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* T,
-                         const int32_t* idx, const float* ln, int64_t E_r, int64_t k, void* y, void* stream,
-                         bool dependent, OutEpilogue ep);
+// Pass 2 with the Linear(k,1) gate computed in the weight rows from z, or
+// (T_in given) from temperatures computed before the pass.
+struct TcGate {
+  const float* z;
+  const float* gate_w;
+  const float* gate_b;
+  float tmin_tau, trange_tau;
+  float* T_out;
+  const float* T_in;
+};
+
+static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* idx,
+                         const float* ln, int64_t E_r, int64_t k, TcGate gate, void* y, void* stream, bool dependent,
+                         OutEpilogue ep);
 
 // bound of the kernel's waits on another role, taken at each launch
 static std::atomic<long long> g_wait_ns{kDefaultWaitNs};
@@ -1023,57 +1093,67 @@ extern "C" int64_t moce_tc_wait_limit_ns(int64_t ns) {
   return (int64_t)(ns > 0 ? g_wait_ns.exchange((long long)ns) : g_wait_ns.load());
 }
 
-extern "C" int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* T,
-                           const int32_t* idx, const float* ln, int64_t E_r, int64_t k, void* y, void* stream) {
-  return mix_tc_launch(xstage, dtype, B, C, HW, T, idx, ln, E_r, k, y, stream, false, OutEpilogue{nullptr, nullptr, 0});
+extern "C" int moce_mix_tc(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* z,
+                           const int32_t* idx, const float* ln, int64_t E_r, int64_t k, const float* gate_w,
+                           const float* gate_b, float tmin_tau, float trange_tau, void* y, float* T_out,
+                           void* stream) {
+  MOCE_REQUIRE(B == 0 || (z && gate_w && gate_b), MOCE_ERR_INVALID, "moce_mix_tc: null pointer argument");
+  return mix_tc_launch(xstage, dtype, B, C, HW, idx, ln, E_r, k,
+                       TcGate{z, gate_w, gate_b, tmin_tau, trange_tau, T_out, nullptr}, y, stream, false,
+                       OutEpilogue{nullptr, nullptr, 0});
+}
+
+extern "C" int moce_mix_tc_t(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* T,
+                             const int32_t* idx, const float* ln, int64_t E_r, int64_t k, void* y, void* stream) {
+  MOCE_REQUIRE(B == 0 || T, MOCE_ERR_INVALID, "moce_mix_tc_t: null T");
+  return mix_tc_launch(xstage, dtype, B, C, HW, idx, ln, E_r, k, TcGate{nullptr, nullptr, nullptr, 0.f, 0.f, nullptr, T},
+                       y, stream, false, OutEpilogue{nullptr, nullptr, 0});
 }
 
 namespace moce {
 int pool_stage_run(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
                    const int32_t* meta, float* z, void* y, int64_t E_r, void* xstage, OutEpilogue ep, void* stream);
-int temperature_run(const float* z, int64_t B, int64_t C, const int32_t* idx, int64_t E_r, int64_t k,
-                    const float* gate_w, const float* gate_b, float tmin_tau, float trange_tau, float* T,
-                    void* stream, bool dependent);                                            // gate.cu
 int temperature_mlp_run(const float* z, int64_t B, int64_t C, int64_t Hd, int64_t E_r, const float* w1,
                         const float* b1, const float* w2, const float* b2, float tmin_tau, float trange_tau,
                         float* h, float* T, void* stream, bool dependent);                    // gate.cu
 }
 
-// The three launches of the tensor-core forward, each a programmatic
-// dependent of the one before (its prologue overlaps the previous kernel's
-// tail; griddepcontrol.wait orders its reads after that kernel's writes):
-// pass 1 (pool, residual, operand staging) -> temperatures -> pass 2 (mix).
+// Pass 1 (pool, residual, operand staging), then pass 2 as a programmatic
+// dependent of it: the mix's prologue (A zeroing, tensor-memory allocation,
+// route loads) overlaps pass 1's tail, and its reads of z and the staged X
+// wait for pass 1's results.
 static int forward_tc_run(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
                           const int32_t* meta, const int32_t* idx, const float* ln, int64_t E_r, int64_t k,
                           const float* gate_w, const float* gate_b, float tmin_tau, float trange_tau, float* z,
-                          void* xstage, void* y, float* T, OutEpilogue ep, void* stream) {
+                          void* xstage, void* y, float* T_out, OutEpilogue ep, void* stream) {
   if (B == 0) return MOCE_OK;
-  MOCE_REQUIRE(T, MOCE_ERR_INVALID, "moce_forward_tc: T (fp32 [B, E_r]) is required");
+  MOCE_REQUIRE(gate_w && gate_b, MOCE_ERR_INVALID, "moce_forward_tc: null gate");
   int rc = pool_stage_run(x, dtype, B, C, HW, mask, meta, z, y, E_r, xstage, ep, stream);
   if (rc) return rc;
-  rc = temperature_run(z, B, C, idx, E_r, k, gate_w, gate_b, tmin_tau, trange_tau, T, stream, true);
-  if (rc) return rc;
-  return mix_tc_launch(xstage, dtype, B, C, HW, T, idx, ln, E_r, k, y, stream, true, ep);
+  return mix_tc_launch(xstage, dtype, B, C, HW, idx, ln, E_r, k,
+                       TcGate{z, gate_w, gate_b, tmin_tau, trange_tau, T_out, nullptr}, y, stream, true, ep);
 }
 
 extern "C" int moce_forward_tc(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
                                const int32_t* meta, const int32_t* idx, const float* ln, int64_t E_r, int64_t k,
                                const float* gate_w, const float* gate_b, float tmin_tau, float trange_tau, float* z,
-                               void* xstage, void* y, float* T, void* stream) {
+                               void* xstage, void* y, float* T_out, void* stream) {
   return forward_tc_run(x, dtype, B, C, HW, mask, meta, idx, ln, E_r, k, gate_w, gate_b, tmin_tau, trange_tau, z,
-                        xstage, y, T, OutEpilogue{nullptr, nullptr, 0}, stream);
+                        xstage, y, T_out, OutEpilogue{nullptr, nullptr, 0}, stream);
 }
 
 extern "C" int moce_forward_tc_ep(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
                                   const int32_t* meta, const int32_t* idx, const float* ln, int64_t E_r, int64_t k,
                                   const float* gate_w, const float* gate_b, float tmin_tau, float trange_tau,
                                   const float* out_scale, const float* out_shift, int out_relu, float* z,
-                                  void* xstage, void* y, float* T, void* stream) {
+                                  void* xstage, void* y, float* T_out, void* stream) {
   MOCE_REQUIRE(out_scale && out_shift, MOCE_ERR_INVALID, "moce_forward_tc_ep: null scale or shift");
   return forward_tc_run(x, dtype, B, C, HW, mask, meta, idx, ln, E_r, k, gate_w, gate_b, tmin_tau, trange_tau, z,
-                        xstage, y, T, OutEpilogue{out_scale, out_shift, out_relu ? 1 : 0}, stream);
+                        xstage, y, T_out, OutEpilogue{out_scale, out_shift, out_relu ? 1 : 0}, stream);
 }
 
+// pass 1 -> the two-layer gate's temperatures -> pass 2 from given T, each a
+// programmatic dependent of the launch before
 extern "C" int moce_forward_tc_mlp(const void* x, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* mask,
                                    const int32_t* meta, const int32_t* idx, const float* ln, int64_t E_r, int64_t k,
                                    int64_t Hd, const float* w1, const float* b1, const float* w2, const float* b2,
@@ -1086,20 +1166,23 @@ extern "C" int moce_forward_tc_mlp(const void* x, int dtype, int64_t B, int64_t 
   if (rc) return rc;
   rc = temperature_mlp_run(z, B, C, Hd, E_r, w1, b1, w2, b2, tmin_tau, trange_tau, h, T, stream, true);
   if (rc) return rc;
-  return mix_tc_launch(xstage, dtype, B, C, HW, T, idx, ln, E_r, k, y, stream, true, OutEpilogue{nullptr, nullptr, 0});
+  return mix_tc_launch(xstage, dtype, B, C, HW, idx, ln, E_r, k, TcGate{nullptr, nullptr, nullptr, 0.f, 0.f, nullptr, T},
+                       y, stream, true, OutEpilogue{nullptr, nullptr, 0});
 }
 
-static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const float* T,
-                         const int32_t* idx, const float* ln, int64_t E_r, int64_t k, void* y, void* stream,
-                         bool dependent, OutEpilogue ep) {
+static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, int64_t HW, const int32_t* idx,
+                         const float* ln, int64_t E_r, int64_t k, TcGate gate, void* y, void* stream, bool dependent,
+                         OutEpilogue ep) {
   if (B == 0) return MOCE_OK;
-  MOCE_REQUIRE(xstage && T && idx && ln && y, MOCE_ERR_INVALID, "moce_mix_tc: null pointer argument");
+  MOCE_REQUIRE(xstage && idx && ln && y, MOCE_ERR_INVALID, "moce_mix_tc: null pointer argument");
   MOCE_REQUIRE(B > 0 && C >= 1 && HW >= 1 && E_r >= 1 && k >= 1 && k <= C, MOCE_ERR_INVALID,
                "moce_mix_tc: invalid shape");
   MOCE_REQUIRE(tc_supported(dtype, C, HW, k), MOCE_ERR_UNSUPPORTED,
                "moce_mix_tc: needs bf16/fp16, C <= 512, k <= 64 within shared memory");
   MOCE_REQUIRE(((uintptr_t)xstage & 15) == 0, MOCE_ERR_INVALID, "moce_mix_tc: xstage must be 16-byte aligned");
   MOCE_REQUIRE(B < 65536 && (E_r + 1) * HW < (int64_t)1 << 31, MOCE_ERR_UNSUPPORTED, "moce_mix_tc: shape too large");
+  const bool tin = gate.T_in != nullptr;
+  MOCE_REQUIRE(!tin || ep.scale == nullptr, MOCE_ERR_UNSUPPORTED, "moce_mix_tc: given temperatures take no epilogue");
   const TcShape sh = tc_shape_for(C, HW, k, (((uintptr_t)y) & 15) == 0);
   const int Kp = sh.Kp, KMAX = sh.KMAX;
   const size_t qbytes = sh.qbytes, fixed = sh.fixed;
@@ -1110,7 +1193,7 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
   int n_bsplit = num_sms() / n_tiles;
   if (n_bsplit < 1) n_bsplit = 1;
   if (n_bsplit > B) n_bsplit = (int)B;
-  TcArgs a{xstage, y, T, idx, ln,
+  TcArgs a{xstage, y, gate.z, idx, ln, gate.gate_w, gate.gate_b, gate.T_out, gate.tmin_tau, gate.trange_tau, gate.T_in,
            (int)B, (int)C, (int)HW, (int)E_r, (int)k, Kp, n_tiles, n_bsplit, ns, sh.NP, sh.NA, sh.P, sh.NT,
            sh.tmem_cols, (unsigned long long)g_wait_ns.load(), sh.drain, sh.stg_pitch, sh.nsb, sh.stage_bytes, ep};
   return dispatch_dtype(dtype, [&](auto tag) {
@@ -1120,17 +1203,23 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
     } else {
       const bool gen = !(sh.NP == 64 && sh.NA == 1 && sh.P == 2 && sh.NT == 1 && sh.drain == kDrainOneTile);
       const bool epi = ep.scale != nullptr;
-#define MOCE_TC_KMAX(G, EP)                                                                         \
-  (KMAX == 16 ? mix_tc_kernel<T, 16, G, EP, false>                                                 \
-              : KMAX == 32 ? mix_tc_kernel<T, 32, G, EP, false> : mix_tc_kernel<T, 64, G, EP, false>)
+#define MOCE_TC_KMAX(G, EP, TI)                                                                         \
+  (KMAX == 16 ? mix_tc_kernel<T, 16, G, EP, false, TI>                                                 \
+              : KMAX == 32 ? mix_tc_kernel<T, 32, G, EP, false, TI> : mix_tc_kernel<T, 64, G, EP, false, TI>)
       // pixel-tiled maps with padded staging rows and k <= 16: one weight
       // thread per row and eight drain warps (with one tile per sample the
       // weights are rewritten every unit and the split measured slower:
       // 74.7 against 68.6 us at 14x14)
       const bool w1 = gen && sh.drain == kDrainRows && KMAX == 16;
-      void (*kern)(TcArgs) = w1 ? (epi ? mix_tc_kernel<T, 16, true, true, true> : mix_tc_kernel<T, 16, true, false, true>)
-                             : gen ? (epi ? MOCE_TC_KMAX(true, true) : MOCE_TC_KMAX(true, false))
-                                   : (epi ? MOCE_TC_KMAX(false, true) : MOCE_TC_KMAX(false, false));
+      void (*kern)(TcArgs) = nullptr;
+      if (tin) {
+        kern = w1 ? mix_tc_kernel<T, 16, true, false, true, true>
+                  : gen ? MOCE_TC_KMAX(true, false, true) : MOCE_TC_KMAX(false, false, true);
+      } else {
+        kern = w1 ? (epi ? mix_tc_kernel<T, 16, true, true, true, false> : mix_tc_kernel<T, 16, true, false, true, false>)
+                  : gen ? (epi ? MOCE_TC_KMAX(true, true, false) : MOCE_TC_KMAX(true, false, false))
+                        : (epi ? MOCE_TC_KMAX(false, true, false) : MOCE_TC_KMAX(false, false, false));
+      }
 #undef MOCE_TC_KMAX
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return set_error(MOCE_ERR_CUDA, "moce_mix_tc: cannot reserve %zu B shared memory", smem);

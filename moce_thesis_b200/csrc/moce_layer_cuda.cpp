@@ -460,13 +460,13 @@ std::vector<torch::Tensor> forward_tc(torch::Tensor x, torch::Tensor idx, torch:
     y = torch::empty({d.B, d.E_r + 1, d.H, d.W}, x.options());
   }
   auto z = f32_opts_like(x, {d.B, d.C});
-  auto T = f32_opts_like(x, {d.B, d.E_r});      // the mix reads it (returned when wanted)
+  auto T = want_T ? f32_opts_like(x, {d.B, d.E_r}) : f32_opts_like(x, {0});
   auto xstage = torch::empty({(int64_t)moce_tc_stage_bytes(d.B, d.C, d.HW)}, x.options().dtype(torch::kUInt8));
   ok(moce_forward_tc(x.data_ptr(), dtype_of(x), d.B, d.C, d.HW, mask.data_ptr<int32_t>(), meta.data_ptr<int32_t>(),
                      idx.data_ptr<int32_t>(), ln.data_ptr<float>(), d.E_r, d.K, gate_w.data_ptr<float>(),
                      gate_b.data_ptr<float>(), (float)tmin_tau, (float)trange_tau, z.data_ptr<float>(),
-                     xstage.data_ptr(), y.data_ptr(), T.data_ptr<float>(), cur_stream()));
-  return {y, z, want_T ? T : f32_opts_like(x, {0})};
+                     xstage.data_ptr(), y.data_ptr(), want_T ? T.data_ptr<float>() : nullptr, cur_stream()));
+  return {y, z, T};
 }
 
 // the tensor-core forward with the caller's eval BatchNorm (folded to a
@@ -496,13 +496,12 @@ torch::Tensor forward_tc_ep(torch::Tensor x, torch::Tensor idx, torch::Tensor ln
     y = torch::empty({d.B, d.E_r + 1, d.H, d.W}, x.options());
   }
   auto z = f32_opts_like(x, {d.B, d.C});
-  auto T = f32_opts_like(x, {d.B, d.E_r});
   auto xstage = torch::empty({(int64_t)moce_tc_stage_bytes(d.B, d.C, d.HW)}, x.options().dtype(torch::kUInt8));
   ok(moce_forward_tc_ep(x.data_ptr(), dtype_of(x), d.B, d.C, d.HW, mask.data_ptr<int32_t>(),
                         meta.data_ptr<int32_t>(), idx.data_ptr<int32_t>(), ln.data_ptr<float>(), d.E_r, d.K,
                         gate_w.data_ptr<float>(), gate_b.data_ptr<float>(), (float)tmin_tau, (float)trange_tau,
                         out_scale.data_ptr<float>(), out_shift.data_ptr<float>(), relu ? 1 : 0, z.data_ptr<float>(),
-                        xstage.data_ptr(), y.data_ptr(), T.data_ptr<float>(), cur_stream()));
+                        xstage.data_ptr(), y.data_ptr(), nullptr, cur_stream()));
   return y;
 }
 
@@ -742,8 +741,8 @@ torch::Tensor forward_given_t(torch::Tensor x, torch::Tensor idx, torch::Tensor 
     auto xstage = torch::empty({(int64_t)moce_tc_stage_bytes(d.B, d.C, d.HW)}, x.options().dtype(torch::kUInt8));
     ok(moce_pool_stage(x.data_ptr(), dt, d.B, d.C, d.HW, mask.data_ptr<int32_t>(), meta.data_ptr<int32_t>(),
                        z.data_ptr<float>(), y.data_ptr(), d.E_r, xstage.data_ptr(), cur_stream()));
-    ok(moce_mix_tc(xstage.data_ptr(), dt, d.B, d.C, d.HW, T.data_ptr<float>(), idx.data_ptr<int32_t>(),
-                   ln.data_ptr<float>(), d.E_r, d.K, y.data_ptr(), cur_stream()));
+    ok(moce_mix_tc_t(xstage.data_ptr(), dt, d.B, d.C, d.HW, T.data_ptr<float>(), idx.data_ptr<int32_t>(),
+                     ln.data_ptr<float>(), d.E_r, d.K, y.data_ptr(), cur_stream()));
   } else {
     ok(moce_pool_residual(x.data_ptr(), dt, d.B, d.C, d.HW, mask.data_ptr<int32_t>(), meta.data_ptr<int32_t>(),
                           z.data_ptr<float>(), y.data_ptr(), d.E_r, cur_stream()));

@@ -83,20 +83,32 @@ def tc_supported(x, k):
 
 def forward_tc(x, r, gate_w, gate_b, tmin_tau, trange_tau, want_T=True):
     """Tensor-core path through the C ABI: pass 1 (pool + residual + operand
-    staging), the temperatures, then the tcgen05 mix, as three calls."""
+    staging), then the tcgen05 mix with the gate computed from z."""
     B, C, H, W = x.shape
     E_r, k = r["idx"].shape
     y = torch.empty(B, E_r + 1, H, W, dtype=x.dtype, device=x.device)
     z = torch.empty(B, C, dtype=torch.float32, device=x.device)
-    T = torch.empty(B, E_r, dtype=torch.float32, device=x.device)
+    T = torch.empty(B, E_r, dtype=torch.float32, device=x.device) if want_T else None
     xs = torch.empty(capi.lib().moce_tc_stage_bytes(B, C, H * W), dtype=torch.uint8, device=x.device)
     call("moce_pool_stage", ptr(x), dtype_code(x), B, C, H * W, ptr(r["mask"]), ptr(r["meta"]), ptr(z), ptr(y),
          E_r, ptr(xs), stream_handle())
-    call("moce_temperature", ptr(z), B, C, ptr(r["idx"]), E_r, k, ptr(gate_w), ptr(gate_b), tmin_tau, trange_tau,
-         ptr(T), stream_handle())
-    call("moce_mix_tc", ptr(xs), dtype_code(x), B, C, H * W, ptr(T), ptr(r["idx"]), ptr(r["ln"]), E_r, k, ptr(y),
-         stream_handle())
+    call("moce_mix_tc", ptr(xs), dtype_code(x), B, C, H * W, ptr(z), ptr(r["idx"]), ptr(r["ln"]), E_r, k,
+         ptr(gate_w), ptr(gate_b), tmin_tau, trange_tau, ptr(y), ptr(T), stream_handle())
     return y, z, T
+
+
+def forward_tc_t(x, r, T):
+    """Tensor-core path with given temperatures: pass 1, then moce_mix_tc_t."""
+    B, C, H, W = x.shape
+    E_r, k = r["idx"].shape
+    y = torch.empty(B, E_r + 1, H, W, dtype=x.dtype, device=x.device)
+    z = torch.empty(B, C, dtype=torch.float32, device=x.device)
+    xs = torch.empty(capi.lib().moce_tc_stage_bytes(B, C, H * W), dtype=torch.uint8, device=x.device)
+    call("moce_pool_stage", ptr(x), dtype_code(x), B, C, H * W, ptr(r["mask"]), ptr(r["meta"]), ptr(z), ptr(y),
+         E_r, ptr(xs), stream_handle())
+    call("moce_mix_tc_t", ptr(xs), dtype_code(x), B, C, H * W, ptr(T), ptr(r["idx"]), ptr(r["ln"]), E_r, k, ptr(y),
+         stream_handle())
+    return y
 
 
 def temperature(z, idx, gate_w, gate_b, tmin_tau, trange_tau):

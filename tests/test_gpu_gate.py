@@ -181,3 +181,21 @@ def test_backward_t_dT_matches_oracle():
     dz = ((dg @ w2) * (h > 0)) @ w1
     dX_mix = d["dX"] - dz[:, :, None, None] / HW
     assert maxrel(dx.cpu().numpy(), dX_mix) < 1e-5
+
+
+@pytest.mark.parametrize("B,C,Hh,E,k", [(9, 512, 7, 300, 32), (3, 128, 28, 90, 16), (2, 64, 56, 40, 8)])
+def test_mix_tc_given_T_matches_in_kernel_gate(B, C, Hh, E, k):
+    """moce_mix_tc_t fed the temperatures moce_mix_tc computed from z gives
+    the same bits (the same weights reach the same MMAs)."""
+    g = torch.Generator().manual_seed(B + C + E)
+    x = torch.randn(B, C, Hh, Hh, generator=g).abs().to(DEV, torch.bfloat16)
+    L = torch.randn(E - 1, C, generator=g).to(DEV)
+    gw = (torch.rand(k, generator=g) - 0.5).to(DEV)
+    gb = (torch.randn(1, generator=g) * 0.1).to(DEV)
+    r = H.route_build(L, k, transposed=False)
+    H.tc_fault(clear=True)
+    y, z, T = H.forward_tc(x, r, gw, gb, TMIN * TAU, (TMAX - TMIN) * TAU, want_T=True)
+    y2 = H.forward_tc_t(x, r, T)
+    torch.cuda.synchronize()
+    assert H.tc_fault() == 0
+    assert torch.equal(y, y2)
