@@ -173,11 +173,20 @@ enum TcDrain {
 
 constexpr int kMaxSlots = 8;
 
+// A is written and released in kAPieces pieces along K (2: halves, 4:
+// quarters), each with a full and a free barrier.
+#ifndef MOCE_TC_A_PIECES
+#define MOCE_TC_A_PIECES 2
+#endif
+constexpr int kAPieces = MOCE_TC_A_PIECES;
+static_assert(kAPieces == 2 || kAPieces == 4, "A pieces: halves or quarters");
+constexpr int kAShift = kAPieces == 2 ? 1 : 0;                // K-quarter >> kAShift: its piece
+
 struct TcBars {
   uint64_t full_b[kMaxSlots];     // X quarter landed in the slot (bulk copy, tx bytes)
   uint64_t slot_free[kMaxSlots];  // MMAs reading the slot done
-  uint64_t a_full[2];             // weight rows wrote the A half (128 arrivals)
-  uint64_t a_free[2];             // MMAs reading the A half done
+  uint64_t a_full[kAPieces];      // weight rows wrote the A piece (one arrival per weight warp)
+  uint64_t a_free[kAPieces];      // MMAs reading the A piece done
   uint64_t d_full[2];             // accumulator buffer complete (one commit per issuer)
   uint64_t d_empty[2];            // accumulator buffer drained (128 arrivals)
   uint64_t fin[2];                // per issuer: every MMA it issued has completed
@@ -205,10 +214,10 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
 enum TcWaitSite {
   kSiteSlotFree = 1,      // producer: a ring slot's MMAs done
   kSiteDEmptySample = 2,  // issuer: accumulator buffer drained (one tile per sample)
-  kSiteAFull = 3,         // issuer: weights of a K-half written
+  kSiteAFull = 3,         // issuer: weights of a K-quarter written
   kSiteDEmptyTile = 4,    // issuer: accumulator buffer drained (pixel tiles)
   kSiteFullB = 5,         // issuer: staged X quarter landed
-  kSiteAFree = 6,         // weight rows: a K-half's MMAs of the previous sample done
+  kSiteAFree = 6,         // weight rows: a K-quarter's MMAs of the previous sample done
   kSiteDFull = 7,         // drain: accumulator complete
 };
 
@@ -420,32 +429,46 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       use = n / NS;
     }
   };
-  int n_pre = 0;                                              // copies issued in the prologue
-  if (tid == kWarpProducer * 32) {
+  // the producer warp feeds each ring from a lane of its own (lane r, ring r),
+  // so a ring waiting for a slot never holds back the other ring's copies;
+  // copy m of ring r is X quarter n = ring_copy(r, m)
+  const int n_rings = (P == 2) ? 2 : 1;
+  auto ring_copy = [&](int r, int m) -> int { return (P == 2) ? 4 * (m >> 1) + 2 * r + (m & 1) : m; };
+  const int ring_len = (P == 2) ? 2 * nu : 4 * nu;             // copies per ring
+  int m_pre = 0;                                              // copies this lane issued in the prologue
+  if (warp == kWarpProducer && lane == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&bars->full_b[s], 1);
       mbar_init(&bars->slot_free[s], 1);
     }
+    for (int q = 0; q < kAPieces; ++q) {
+      mbar_init(&bars->a_full[q], WT / 32);                    // one arrival per weight warp
+      mbar_init(&bars->a_free[q], 1);
+    }
     for (int h = 0; h < 2; ++h) {
-      mbar_init(&bars->a_full[h], WT / 32);                    // one arrival per weight warp
-      mbar_init(&bars->a_free[h], 1);
       mbar_init(&bars->d_full[h], P);
       mbar_init(&bars->d_empty[h], DT / 32);                   // one arrival per drain warp
       mbar_init(&bars->fin[h], 1);
     }
     bars->abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    // staged X comes from pass 1, which may still run when this grid is a
-    // programmatic dependent of it (moce_forward_tc); a no-op otherwise
-    grid_dep_wait();
-    // the leading copies that take a slot's first use need no wait
-    for (; n_pre < 4 * nu; ++n_pre) {
-      int slot, use;
-      ring_slot(n_pre, slot, use);
-      if (use > 0) break;
-      mbar_expect_tx(&bars->full_b[slot], qbytes);
-      bulk_g2s(smem_u32(sB) + (uint32_t)slot * qbytes,
-               xs + (size_t)(n_pre >> 2) * sbytes + (size_t)(n_pre & 3) * qbytes, qbytes, &bars->full_b[slot]);
+  }
+  if (warp == kWarpProducer) {
+    __syncwarp();                                             // the barriers are initialized
+    if (lane < n_rings) {
+      // staged X comes from pass 1, which may still run when this grid is a
+      // programmatic dependent of it (moce_forward_tc); a no-op otherwise
+      grid_dep_wait();
+      // the leading copies that take a slot's first use need no wait
+      for (; m_pre < ring_len; ++m_pre) {
+        const int n = ring_copy(lane, m_pre);
+        int slot, use;
+        ring_slot(n, slot, use);
+        if (use > 0) break;
+        mbar_expect_tx(&bars->full_b[slot], qbytes);
+        bulk_g2s(smem_u32(sB) + (uint32_t)slot * qbytes, xs + (size_t)(n >> 2) * sbytes + (size_t)(n & 3) * qbytes,
+                 qbytes, &bars->full_b[slot]);
+      }
     }
   }
   // weight rows: threads 2r and 2r+1 share expert row e0 + r, each with KH
@@ -453,7 +476,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   constexpr int KH = kW1 ? KMAX : KMAX / 2;
   const int row = kW1 ? tid : tid >> 1, part = kW1 ? 0 : tid & 1;
   const bool w_row = tid < WT && row < rows;
-  uint32_t chp[KH];                                           // channel << 17 | byte offset in A
+  uint32_t chp[KH];                                           // K-quarter << 30 | channel << 17 | byte offset in A
   float ln2[KH];
   float mx2 = -INFINITY;
   float t_next = 1.0f;                                        // kTin: this row's temperature, one sample ahead
@@ -472,7 +495,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       if (j < k && w_row) {
         const size_t o = (size_t)(e0 + row) * k + j;
         const int c = a.idx[o];
-        chp[jj] = ((uint32_t)c << 17) | a_off(row, c);
+        chp[jj] = ((uint32_t)(4 * c / Kp) << 30) | ((uint32_t)c << 17) | a_off(row, c);
         ln2[jj] = a.ln[o] * 1.4426950408889634f;            // log2(e)
         mx2 = nan_max(mx2, ln2[jj]);
       }
@@ -504,12 +527,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   const uint32_t tmem = bars->tmem;
 
   if (warp == kWarpProducer) {
-    // ===================== producer
-    if (lane == 0) {
+    // ===================== producer: lane r feeds ring r
+    if (lane < n_rings) {
       const uint32_t aB = smem_u32(sB);
-      const int total = 4 * nu;
-      int n = n_pre;
-      for (; n < total; ++n) {
+      int m = m_pre;
+      for (; m < ring_len; ++m) {
+        const int n = ring_copy(lane, m);
         int slot, use;
         ring_slot(n, slot, use);
         if (use >= 1 && !wait_peer(&bars->slot_free[slot], (use - 1) & 1, kSiteSlotFree, n)) break;
@@ -519,13 +542,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       }
       // copies still in flight land before the block can exit (no-op on the
       // normal path: the issuers consumed every slot): the most recent use
-      // of every slot of each ring
-      for (int h = 0; h < (P == 2 ? 2 : 1); ++h) {
-        const int nsh = (P == 2 && h) ? NS1 : NS0, base = h ? NS0 : 0;
-        const int issued = (P == 2) ? 2 * (n >> 2) + min(2, max(0, (n & 3) - 2 * h)) : n;
-        for (int j = max(0, issued - nsh); j < issued; ++j)
-          if (!mbar_wait(&bars->full_b[base + j % nsh], (j / nsh) & 1)) atomicExch(&g_tc_fault, 1);
-      }
+      // of every slot of this ring
+      const int nsh = (P == 2 && lane) ? NS1 : NS0, base = lane ? NS0 : 0;
+      for (int j = max(0, m - nsh); j < m; ++j)
+        if (!mbar_wait(&bars->full_b[base + j % nsh], (j / nsh) & 1)) atomicExch(&g_tc_fault, 1);
     }
   } else if (warp == kWarpIssuer0 || warp == kWarpIssuer0 + 1) {
     // ===================== MMA issuers.  P == 2: issuer h takes K-half h
@@ -547,11 +567,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         // one tile per sample: the accumulator buffer first, as it frees
         // earlier than the next weights
         if (NT == 1 && i >= 2 && !wait_peer(&bars->d_empty[i & 1], ((i - 2) >> 1) & 1, kSiteDEmptySample, i)) break;
-        // this sample's weights (A), both halves of this issuer
-        for (int h = h0; h < h1 && run; ++h)
-          if (!wait_peer(&bars->a_full[h], i & 1, kSiteAFull, i)) run = false;
-        if (!run) break;
-        tc_fence_after();
         for (int t = 0; t < NT && run; ++t) {
           const int u = i * NT + t, s = u & 1;
           if (NT > 1 && u >= 2) {
@@ -565,6 +580,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
             const uint32_t d = tmem + (uint32_t)(s * P * NP + (P == 2 ? h : 0) * NP);
             for (int qq = 0; qq < 2; ++qq) {
               const int q = 2 * h + qq, n = 4 * u + q;
+              // the sample's weights of this piece of K (first tile), then its X
+              const int pc = q >> kAShift;
+              const bool pfirst = kAPieces == 4 || qq == 0, plast = kAPieces == 4 || qq == 1;
+              if (t == 0 && pfirst && !wait_peer(&bars->a_full[pc], i & 1, kSiteAFull, i)) {
+                run = false;
+                break;
+              }
               int slot, use;
               ring_slot(n, slot, use);
               if (!wait_peer(&bars->full_b[slot], use & 1, kSiteFullB, n)) {
@@ -583,13 +605,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
                 umma_f16(d, da, db, idesc, first ? 0u : 1u);
               }
               umma_commit(&bars->slot_free[slot]);
+              // the last tile of the sample releases the piece's weights
+              if (t == NT - 1 && plast) umma_commit(&bars->a_free[pc]);
             }
           }
           if (!run) break;
-          // the last tile of the sample releases its weights (first, for the
-          // weight rows wait on it) and every tile its accumulator buffer
-          if (t == NT - 1)
-            for (int h = h0; h < h1; ++h) umma_commit(&bars->a_free[h]);
+          // every tile releases its accumulator buffer
           umma_commit(&bars->d_full[s]);
         }
         if (!run) break;
@@ -602,16 +623,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     // ===================== weight rows (pairs of threads per row)
     const int e = e0 + row;
     const bool has_row = w_row;
-    const int Kh = Kp / 2;                                    // first channel of K-half 1
     const uint32_t sAu = smem_u32(sA);
     // the unnormalized weights of the sample stay in registers between the
-    // softmax sum and the two half writes (k <= 32); for k <= 64 they are
-    // recomputed per half to stay within the register budget
+    // softmax sum and the four quarter writes (k <= 32); for k <= 64 they are
+    // recomputed per quarter to stay within the register budget
     constexpr bool kKeepW = KMAX <= 32;
     if constexpr (!kW1) mx2 = nan_max(mx2, __shfl_xor_sync(kFull, mx2, 1));
     const float bias = kTin ? 0.0f : a.gate_b[0];
     bool ok = true;
-    for (int i = 0; i < nb && ok; ++i) {
+    for (int i = 0; i < nb; ++i) {
       const int b = b0 + i;
       float t;
       if constexpr (kTin) {
@@ -626,7 +646,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
 #pragma unroll
         for (int u = 0; u < ZPT; ++u)
           if (tid + u * WT < C) szb[tid + u * WT] = zr[u];
-        role_sync(kBarWeights, WT);
+        // the weight warps agree here, once per sample, on whether to go on
+        // (a warp whose wait ran out below comes here with ok false)
+        ok = role_sync_and(kBarWeights, WT, ok);
+        if (!ok) break;
         if (i + 1 < nb) {
 #pragma unroll
           for (int u = 0; u < ZPT; ++u) {
@@ -637,7 +660,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         float gp = 0.0f;
 #pragma unroll
         for (int jj = 0; jj < KH; ++jj)
-          if (part * KH + jj < k && has_row) gp += (kGwReg ? gwr[jj] : s_gw[part * KH + jj]) * szb[chp[jj] >> 17];
+          if (part * KH + jj < k && has_row) gp += (kGwReg ? gwr[jj] : s_gw[part * KH + jj]) * szb[(chp[jj] >> 17) & 0x1FFu];
         const float g = bias + gp + (kW1 ? 0.0f : __shfl_xor_sync(kFull, gp, 1));
         t = temperature(g, a.tmin_tau, a.trange_tau, nullptr);
         if (a.T_out && has_row && part == 0) a.T_out[(size_t)b * E_r + e] = t;
@@ -653,21 +676,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         zp += ev;
       }
       const float iz = 1.0f / (zp + (kW1 ? 0.0f : __shfl_xor_sync(kFull, zp, 1)));
+      // the pieces in the order the MMAs consume them (quarters: 0, 2, 1, 3
+      // with two issuers, issuer h taking quarters 2h and 2h+1).  Each warp
+      // waits for the previous sample's MMAs of a piece by itself and writes
+      // it, while the MMAs of the later pieces run.
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        // the previous sample's MMAs have released this half of A
-        bool w_ok = true;
-        if (i >= 1 && tid == 0) w_ok = wait_peer(&bars->a_free[h], (i - 1) & 1, kSiteAFree, i);
-        if (i >= 1) w_ok = role_sync_and(kBarWeights, WT, w_ok);
-        if (!w_ok) {
+      for (int qi = 0; qi < kAPieces; ++qi) {
+        const int q = (kAPieces == 4 && P == 2) ? ((qi & 1) << 1) | (qi >> 1) : qi;
+        const bool w_ok = i < 1 || wait_peer(&bars->a_free[q], (i - 1) & 1, kSiteAFree, i);
+        if (!__all_sync(kFull, w_ok)) {
           ok = false;
           break;
         }
         if (has_row) {
 #pragma unroll
           for (int jj = 0; jj < KH; ++jj) {
-            const int c = (int)(chp[jj] >> 17);
-            if (part * KH + jj < k && (c >= Kh) == (h == 1)) {
+            if (part * KH + jj < k && (int)(chp[jj] >> (30 + kAShift)) == q) {
               float ev;
               if constexpr (kKeepW) ev = wv[jj];
               else ev = ex2_approx(ln2[jj] * it - m2);
@@ -676,8 +700,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
           }
         }
         proxy_fence_smem();
-        mbar_arrive_warp(&bars->a_full[h]);
+        mbar_arrive_warp(&bars->a_full[q]);
       }
+      if (kTin && !ok) break;                                 // (!kTin: the warps agree above)
     }
   } else if (tid < WT + DT) {
     // ===================== drain (warps 8-11; kW1: 4-11): TMEM lane quarter = warp % 4

@@ -79,3 +79,26 @@ def test_layer_matches_reference_kernels(B, C, Hh, E, k, dtype):
     a, b = y.float().cpu().numpy(), want.float().cpu().numpy()
     rtol = 1e-5 if dtype == torch.float32 else 1e-2
     assert close(a, b, rtol, 1e-3), worst(a, b)
+
+
+@pytest.mark.parametrize("B,C,Hh,E,k", [(8, 256, 14, 1024, 16), (64, 512, 7, 2048, 32), (16, 128, 4, 200, 40)])
+def test_drop_in_binding_under_reference_eval(B, C, Hh, E, k):
+    """The reference's eval forward (MoCE.py:204-230: ATen pool, gate,
+    softmax, then moce_fixed.moce_cuda.fused_moce_forward_dynamic_temp) run
+    once on the reference's own extension and once on this repository's
+    moce_fixed.moce_cuda, with the same cache and inputs: the drop-in gives
+    the reference's output (fp32, 1e-5)."""
+    import moce_fixed.moce_cuda as ours
+    from oracle import ref_gpu
+    mod = _ref_mod()
+    gen = torch.Generator().manual_seed(B * 3 + C + k)
+    x = torch.randn(B, C, Hh, Hh, generator=gen).abs().to(DEV)
+    L = torch.randn(E - 1, C, generator=gen).to(DEV)
+    gw = ((torch.rand(1, k, generator=gen) * 2 - 1) * (6.0 / (k + 1)) ** 0.5).to(DEV)
+    gb = torch.zeros(1, device=DEV)
+    idx, ln, mask = ref_gpu.cache(L, k)
+    want = ref_gpu.forward_eval(mod, x, idx, ln, gw, gb, mask, TMIN, TMAX, TAU)
+    got = ref_gpu.forward_eval(ours, x, idx, ln, gw, gb, mask, TMIN, TMAX, TAU)
+    torch.cuda.synchronize()
+    a, b = got.cpu().numpy(), want.cpu().numpy()
+    assert close(a, b, 1e-5, 1e-6), worst(a, b)
