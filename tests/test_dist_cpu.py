@@ -37,7 +37,9 @@ def _worker(rank, world, port, q):
         p.grad = torch.full_like(p, float(rank + 1) * (i + 1))
     net[1].gate.bias.grad = None if rank == 0 else net[1].gate.bias.grad
     n = allreduce_moce_grads(net)
-    out = {name: p.grad.clone() for name, p in net.named_parameters()}
+    # numpy arrays travel by value: a torch tensor in the queue is shared
+    # through a file descriptor that dies with this process
+    out = {name: p.grad.detach().numpy().copy() for name, p in net.named_parameters()}
     q.put((rank, n, out))
     dist.destroy_process_group()
 
@@ -58,6 +60,8 @@ def test_allreduce_averages_across_two_ranks():
         assert p.exitcode == 0
     n0, g0 = res[0]
     n1, g1 = res[1]
+    g0 = {name: torch.from_numpy(v) for name, v in g0.items()}
+    g1 = {name: torch.from_numpy(v) for name, v in g1.items()}
     assert n0 == n1 == (7 * 16 + 4 + 1) + (3 * 8 + 2 + 1)
     names = list(g0)
     for i, name in enumerate(names):
