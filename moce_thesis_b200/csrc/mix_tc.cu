@@ -173,14 +173,16 @@ enum TcDrain {
 
 constexpr int kMaxSlots = 8;
 
-// A is written and released in kAPieces pieces along K (2: halves, 4:
-// quarters), each with a full and a free barrier.
-#ifndef MOCE_TC_A_PIECES
-#define MOCE_TC_A_PIECES 2
+// A is written and released in two halves along K, each with a full and a
+// free barrier.  With two MMA issuers, kSplitK: issuer h takes K-quarters h
+// and h + 2 (one of each half), so that both finish half 0 before half 1 and
+// the next sample's half 0 is written while half 1's MMAs run; otherwise
+// issuer h takes both quarters of half h.
+#ifndef MOCE_TC_SPLITK
+#define MOCE_TC_SPLITK 1
 #endif
-constexpr int kAPieces = MOCE_TC_A_PIECES;
-static_assert(kAPieces == 2 || kAPieces == 4, "A pieces: halves or quarters");
-constexpr int kAShift = kAPieces == 2 ? 1 : 0;                // K-quarter >> kAShift: its piece
+constexpr bool kSplitK = MOCE_TC_SPLITK != 0;
+constexpr int kAPieces = 2;
 
 struct TcBars {
   uint64_t full_b[kMaxSlots];     // X quarter landed in the slot (bulk copy, tx bytes)
@@ -410,17 +412,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   const unsigned char* xs = static_cast<const unsigned char*>(a.xstage) + (size_t)b0 * NT * sbytes;
   const int nu = nb * NT;                                     // units (sample, pixel tile) of this CTA
   // X quarter n = 4u + q of unit u goes to a slot of the ring.  With two
-  // issuers (P == 2) issuer h consumes quarters 2h and 2h+1 of every unit
-  // from a ring of its own (slots [0, NS0) for K-half 0, [NS0, NS) for K-half
-  // 1), so that every slot's full barrier has one consumer, which has waited
-  // for each earlier phase of it.  (A slot shared by the two issuers lets one
-  // of them wait for a copy while the slot's previous copy, consumed by the
-  // other, is still landing; a parity wait for a phase two ahead of the
-  // barrier then passes at once, and the ring's accounting breaks.)
+  // issuers (P == 2) issuer h consumes its two quarters of every unit (q = h
+  // and h + 2, or 2h and 2h + 1; see kSplitK) from a ring of its own (slots
+  // [0, NS0) for issuer 0, [NS0, NS) for issuer 1), so that every slot's full
+  // barrier has one consumer, which has waited for each earlier phase of it.
+  // (A slot shared by the two issuers lets one of them wait for a copy while
+  // the slot's previous copy, consumed by the other, is still landing; a
+  // parity wait for a phase two ahead of the barrier then passes at once,
+  // and the ring's accounting breaks.)
   const int NS0 = (P == 2) ? (NS + 1) / 2 : NS, NS1 = (P == 2) ? NS / 2 : 0;
   auto ring_slot = [&](int n, int& slot, int& use) {
     if (P == 2) {
-      const int h = (n >> 1) & 1, m = 2 * (n >> 2) + (n & 1);
+      const int q = n & 3;
+      const int h = kSplitK ? (q & 1) : (q >> 1);             // ring (issuer)
+      const int m = 2 * (n >> 2) + (kSplitK ? (q >> 1) : (q & 1));  // copy of that ring
       const int nsh = h ? NS1 : NS0;
       slot = (h ? NS0 : 0) + m % nsh;
       use = m / nsh;
@@ -433,7 +438,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   // so a ring waiting for a slot never holds back the other ring's copies;
   // copy m of ring r is X quarter n = ring_copy(r, m)
   const int n_rings = (P == 2) ? 2 : 1;
-  auto ring_copy = [&](int r, int m) -> int { return (P == 2) ? 4 * (m >> 1) + 2 * r + (m & 1) : m; };
+  auto ring_copy = [&](int r, int m) -> int {
+    if (P != 2) return m;
+    return 4 * (m >> 1) + (kSplitK ? r + 2 * (m & 1) : 2 * r + (m & 1));
+  };
   const int ring_len = (P == 2) ? 2 * nu : 4 * nu;             // copies per ring
   int m_pre = 0;                                              // copies this lane issued in the prologue
   if (warp == kWarpProducer && lane == 0) {
@@ -443,7 +451,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
     }
     for (int q = 0; q < kAPieces; ++q) {
       mbar_init(&bars->a_full[q], WT / 32);                    // one arrival per weight warp
-      mbar_init(&bars->a_free[q], 1);
+      mbar_init(&bars->a_free[q], (P == 2 && kSplitK) ? 2 : 1); // one commit per issuer reading the half
     }
     for (int h = 0; h < 2; ++h) {
       mbar_init(&bars->d_full[h], P);
@@ -561,7 +569,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       // B slot: NA atoms of Kq channel rows x 128 B; atoms Kq * 128 B apart
       // (leading byte offset), 8-row groups 1024 B apart (stride byte offset)
       const uint32_t atom_stride = (uint32_t)(Kp / 4) * 128;
-      const int h0 = (P == 2) ? hi : 0, h1 = (P == 2) ? hi + 1 : 2;
+      const int nq = (P == 2) ? 2 : 4;                        // K-quarters of a unit this issuer takes
       bool run = true;
       for (int i = 0; i < nb && run; ++i) {
         // one tile per sample: the accumulator buffer first, as it frees
@@ -576,13 +584,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
             }
             tc_fence_after();
           }
-          for (int h = h0; h < h1 && run; ++h) {
-            const uint32_t d = tmem + (uint32_t)(s * P * NP + (P == 2 ? h : 0) * NP);
-            for (int qq = 0; qq < 2; ++qq) {
-              const int q = 2 * h + qq, n = 4 * u + q;
-              // the sample's weights of this piece of K (first tile), then its X
-              const int pc = q >> kAShift;
-              const bool pfirst = kAPieces == 4 || qq == 0, plast = kAPieces == 4 || qq == 1;
+          {
+            const uint32_t d = tmem + (uint32_t)(s * P * NP + (P == 2 ? hi : 0) * NP);
+            for (int qi = 0; qi < nq; ++qi) {
+              const int q = (P == 2) ? (kSplitK ? hi + 2 * qi : 2 * hi + qi) : qi, n = 4 * u + q;
+              // the sample's weights of this half of K (before this issuer's
+              // first quarter of it, first tile), then the quarter's X
+              const int pc = q >> 1;
+              const bool pfirst = (P == 2) ? (kSplitK || qi == 0) : (q & 1) == 0;
+              const bool plast = (P == 2) ? (kSplitK || qi == 1) : (q & 1) == 1;
               if (t == 0 && pfirst && !wait_peer(&bars->a_full[pc], i & 1, kSiteAFull, i)) {
                 run = false;
                 break;
@@ -601,11 +611,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
                 // shared addresses are below 2^18)
                 const uint64_t da = da0 + (uint64_t)(((j >> 2) * 16384 + (j & 3) * 32) >> 4);
                 const uint64_t db = db0 + (uint64_t)(jj * 128);
-                const bool first = (P == 2 || h == 0) && qq == 0 && jj == 0;
+                const bool first = qi == 0 && jj == 0;
                 umma_f16(d, da, db, idesc, first ? 0u : 1u);
               }
               umma_commit(&bars->slot_free[slot]);
-              // the last tile of the sample releases the piece's weights
+              // the last tile of the sample releases the half's weights
               if (t == NT - 1 && plast) umma_commit(&bars->a_free[pc]);
             }
           }
@@ -676,13 +686,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         zp += ev;
       }
       const float iz = 1.0f / (zp + (kW1 ? 0.0f : __shfl_xor_sync(kFull, zp, 1)));
-      // the pieces in the order the MMAs consume them (quarters: 0, 2, 1, 3
-      // with two issuers, issuer h taking quarters 2h and 2h+1).  Each warp
-      // waits for the previous sample's MMAs of a piece by itself and writes
-      // it, while the MMAs of the later pieces run.
+      // the halves in order; each warp waits for the previous sample's MMAs
+      // of a half by itself and writes it, while the MMAs of the other half
+      // run
 #pragma unroll
-      for (int qi = 0; qi < kAPieces; ++qi) {
-        const int q = (kAPieces == 4 && P == 2) ? ((qi & 1) << 1) | (qi >> 1) : qi;
+      for (int q = 0; q < kAPieces; ++q) {
         const bool w_ok = i < 1 || wait_peer(&bars->a_free[q], (i - 1) & 1, kSiteAFree, i);
         if (!__all_sync(kFull, w_ok)) {
           ok = false;
@@ -691,7 +699,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         if (has_row) {
 #pragma unroll
           for (int jj = 0; jj < KH; ++jj) {
-            if (part * KH + jj < k && (int)(chp[jj] >> (30 + kAShift)) == q) {
+            if (part * KH + jj < k && (int)(chp[jj] >> 31) == q) {
               float ev;
               if constexpr (kKeepW) ev = wv[jj];
               else ev = ex2_approx(ln2[jj] * it - m2);

@@ -63,10 +63,51 @@ __device__ __forceinline__ void st4<__half>(__half* p, const float* f) {
 }
 
 // X_b [C, HW] into shared rows of HWp elements (HWp % 4 == 0); padding
-// columns are zeroed.  A flat 16-byte copy when the rows are unpadded.
+// columns are zeroed.  A flat 16-byte copy when the rows are unpadded; padded
+// rows of an aligned sample take the same 16-byte loads, each element then
+// stored to its row and column.
 template <typename T>
 __device__ __forceinline__ void px_stage_rows(T* s_x, const T* xb, int C, int HW, int HWp) {
   const size_t n = (size_t)C * HW;
+  if (HWp != HW && ((((uintptr_t)xb) | (n * sizeof(T))) & 15) == 0) {
+    constexpr int V = 16 / sizeof(T);
+    const int4* s4 = reinterpret_cast<const int4*>(xb);
+    const int n16 = (int)(n * sizeof(T) / 16);
+    for (int q0 = threadIdx.x; q0 < n16; q0 += 8 * blockDim.x) {
+      int4 r[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int q = q0 + u * blockDim.x;
+        if (q < n16) r[u] = __ldg(s4 + q);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int q = q0 + u * blockDim.x;
+        if (q < n16) {
+          union {
+            int4 v;
+            T e[V];
+          } w;
+          w.v = r[u];
+          int c = (q * V) / HW, p = q * V - c * HW;
+#pragma unroll
+          for (int t = 0; t < V; ++t) {
+            s_x[(size_t)c * HWp + p] = w.e[t];
+            if (++p == HW) {
+              p = 0;
+              ++c;
+            }
+          }
+        }
+      }
+    }
+    const int padw = HWp - HW;
+    for (int i = threadIdx.x; i < C * padw; i += blockDim.x) {
+      const int c = i / padw;
+      s_x[(size_t)c * HWp + HW + (i - c * padw)] = from_f<T>(0.0f);
+    }
+    return;
+  }
   if (HWp == HW && ((((uintptr_t)xb) | (n * sizeof(T))) & 15) == 0) {
     const int4* s4 = reinterpret_cast<const int4*>(xb);
     int4* d4 = reinterpret_cast<int4*>(s_x);

@@ -555,13 +555,22 @@ static int mix_px_run(const void* x, int dtype, int64_t B, int64_t C, int64_t HW
   const size_t smem = px_smem_split(C, Ch, HW, k, esize);
   const int nslab = (int)((HW + 127) / 128);
   const int nthr = px_threads(nslab), kPxWarps = nthr / 32;
-  // CTAs per sample so that the grid covers the SMs several times over
-  const int per_sm = smem <= 110 * 1024 && nthr <= 512 ? 2 : 1;
-  int64_t nch = (4LL * per_sm * num_sms() + B - 1) / B;
+  // CTAs per sample: the count whose rounds over the SMs waste least.  A
+  // CTA costs its share of the sample's experts plus a fixed part (staging
+  // X_b, the prologue), taken as 1/16 of a whole sample; the busiest SM runs
+  // ceil(B * nch / SMs) CTAs.  (Small batches used to take enough CTAs per
+  // sample to cover the SMs four times, each restaging X_b.)
   const int64_t max_ch = (E_r + kPxWarps - 1) / kPxWarps;
-  if (nch > max_ch) nch = max_ch;
-  if (nch < 1) nch = 1;
-  if (CL == 2) nch = (nch + 1) / 2 * 2;                   // whole CTA pairs
+  const int64_t n_sm = num_sms();
+  int64_t nch = CL;
+  double best = 1e30;
+  for (int64_t c = CL; c <= max_ch && c <= 64; c += CL) {
+    const double cost = (double)((B * c + n_sm - 1) / n_sm) * (1.0 / (double)c + 1.0 / 16.0);
+    if (cost < best - 1e-9) {
+      best = cost;
+      nch = c;
+    }
+  }
   // grouped weights (k <= 16) pay off with at least 8 experts per warp; a
   // group holds at most 32
   const int64_t per = (E_r + nch - 1) / nch;

@@ -245,6 +245,7 @@ class MoCE(nn.Module):
         self.cached_gate_weight = None
         self.cached_gate_bias = None
         self._route = None        # native eval cache (int32 supports etc.)
+        self._f32_cache = {}      # fp32 gate parameters / folded BatchNorm, keyed by tensor versions
         if gate_type == "mlp":
             self.reset_gate_mlp()
 
@@ -293,6 +294,7 @@ class MoCE(nn.Module):
         self.cached_selected_logits_norm = None
         self.cached_mask_int = None
         self._route = None
+        self._f32_cache = {}
 
     # ------------------------------------------------------------------
     def _compute_aux_losses(self, x, E_routed, tau):
@@ -354,10 +356,29 @@ class MoCE(nn.Module):
             if _CHECK_FAULTS:
                 check_faults()
             return y
-        gw = self.cached_gate_weight.detach().reshape(-1).float().contiguous()
-        gb = self.cached_gate_bias.detach().reshape(-1).float().contiguous()
+        gw, gb = self._gate_f32()
         y, _, _ = route.forward(x, gw, gb, self.cached_temp_min_tau, self.cached_temp_range_tau, False, out)
         return y
+
+    def _cached_f32(self, name, tensors, make, extra=()):
+        """make() once per version of `tensors` (and value of `extra`): an
+        eval forward otherwise launches a conversion kernel per parameter per
+        call."""
+        key = tuple((t.data_ptr(), t._version, t.dtype, t.device) if t is not None else None
+                    for t in tensors) + tuple(extra)
+        hit = self._f32_cache.get(name)
+        if hit is not None and hit[0] == key:
+            return hit[1]
+        with torch.no_grad():
+            val = make()
+        self._f32_cache[name] = (key, val)
+        return val
+
+    def _gate_f32(self):
+        """The shared gate's weight [k] and bias [1] in fp32, contiguous."""
+        w, b = self.cached_gate_weight, self.cached_gate_bias
+        return self._cached_f32("gate", (w, b), lambda: (w.detach().reshape(-1).float().contiguous(),
+                                                          b.detach().reshape(-1).float().contiguous()))
 
     # ------------------------------------------------------------------
     def forward_eval_bn_relu(self, x, bn, relu=True):
@@ -381,17 +402,19 @@ class MoCE(nn.Module):
         if route is None or route.idx.device != x.device:
             route = _Route(self.routing_logits, self.k, transposed=False)
             self._route = route
-        with torch.no_grad():
+        def fold():
             inv = torch.rsqrt(bn.running_var.float() + float(bn.eps))
             scale = inv if bn.weight is None else bn.weight.float() * inv
             shift = -bn.running_mean.float() * scale
             if bn.bias is not None:
                 shift = shift + bn.bias.float()
-        gw = self.cached_gate_weight.detach().reshape(-1).float().contiguous()
-        gb = self.cached_gate_bias.detach().reshape(-1).float().contiguous()
+            return scale.contiguous(), shift.contiguous()
+        scale, shift = self._cached_f32("bn", (bn.running_mean, bn.running_var, bn.weight, bn.bias), fold,
+                                        (float(bn.eps),))
+        gw, gb = self._gate_f32()
         y = m.forward_tc_ep(x.contiguous(), route.idx, route.ln, route.mask, route.meta, gw, gb,
                             float(self.cached_temp_min_tau), float(self.cached_temp_range_tau),
-                            scale.contiguous(), shift.contiguous(), bool(relu))
+                            scale, shift, bool(relu))
         if _CHECK_FAULTS:
             check_faults()
         return y
