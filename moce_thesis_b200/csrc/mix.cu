@@ -13,6 +13,8 @@
 // pixels) per support per step from a bank that no other lane uses in that
 // step (see schedule.cu).  Results are staged per warp in shared memory and
 // written as contiguous expert rows.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 extern "C" int moce_schedule_steps(int64_t k);
@@ -101,12 +103,16 @@ __device__ __forceinline__ void load_pitched(T* dst, const T* src, int C, int HW
 }
 
 // ------------------------------------------------------------------ pass 1
-// grid (B), 256 threads.  Channel chunks [c0, c0 + cc) of one sample are
-// contiguous in X and are copied flat; z per channel (one thread per channel
-// row when rows are short, one warp per row otherwise), the residual per
-// pixel by a thread loop over the chunk's uncovered channels.
+// grid (ncl, B), 256 threads, clusters of ncl CTAs along x: CTA r of a
+// sample's cluster takes channels [r per, (r + 1) per), in chunks [c0, c0 +
+// cc) that are contiguous in X and are copied flat; z per channel (one
+// thread per channel row when rows are short, one warp per row otherwise),
+// the residual per pixel by a thread loop over the chunk's uncovered
+// channels, the CTAs' partial sums added up by rank 0 through distributed
+// shared memory.  (Several CTAs per sample keep the SMs busy at small
+// batches.)
 template <typename T>
-__global__ void __launch_bounds__(256) pool_residual_kernel(const T* __restrict__ x, int C, int HW, int cc,
+__global__ void __launch_bounds__(256) pool_residual_kernel(const T* __restrict__ x, int C, int HW, int cc, int per,
                                                             const int32_t* __restrict__ mask,
                                                             const int32_t* __restrict__ meta, float* __restrict__ z,
                                                             T* __restrict__ y, int E) {
@@ -115,15 +121,17 @@ __global__ void __launch_bounds__(256) pool_residual_kernel(const T* __restrict_
   float* s_res = reinterpret_cast<float*>(s_raw + (((size_t)cc * HW * sizeof(T) + 15) & ~size_t(15)));  // HW
   int* s_ulist = reinterpret_cast<int*>(s_res + HW);                    // cc
   __shared__ int s_nu;
-  const int b = blockIdx.x;
+  cooperative_groups::cluster_group cluster = cooperative_groups::this_cluster();
+  const int b = blockIdx.y, rank = (int)cluster.block_rank(), ncl = (int)cluster.num_blocks();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const int n_u = (mask && meta) ? meta[0] : 0;
   const T* xb = x + (size_t)b * C * HW;
   if (n_u > 0)
     for (int p = threadIdx.x; p < HW; p += blockDim.x) s_res[p] = 0.0f;
   const float inv_hw = 1.0f / (float)HW;
-  for (int c0 = 0; c0 < C; c0 += cc) {
-    const int cn = min(cc, C - c0);
+  const int c_end = min(C, (rank + 1) * per);
+  for (int c0 = rank * per; c0 < c_end; c0 += cc) {
+    const int cn = min(cc, c_end - c0);
     const T* src = xb + (size_t)c0 * HW;
     const size_t n = (size_t)cn * HW;
     __syncthreads();
@@ -172,11 +180,17 @@ __global__ void __launch_bounds__(256) pool_residual_kernel(const T* __restrict_
     }
   }
   __syncthreads();
-  if (y) {
+  if (ncl > 1 && n_u > 0) cluster.sync();                 // every CTA's partial sums are complete
+  if (y && rank == 0) {
     T* yr = y + ((size_t)b * E + (E - 1)) * HW;
-    for (int p = threadIdx.x; p < HW; p += blockDim.x)
-      yr[p] = from_f<T>(n_u > 0 ? s_res[p] / (float)n_u : 0.0f);
+    for (int p = threadIdx.x; p < HW; p += blockDim.x) {
+      float r = 0.0f;
+      if (n_u > 0)
+        for (int q = 0; q < ncl; ++q) r += q == 0 ? s_res[p] : cluster.map_shared_rank(s_res, q)[p];
+      yr[p] = from_f<T>(n_u > 0 ? r / (float)n_u : 0.0f);
+    }
   }
+  if (ncl > 1 && n_u > 0) cluster.sync();                 // peers' shared memory stays until rank 0 has read it
 }
 
 // ------------------------------------------------------------------ pass 2
@@ -506,10 +520,16 @@ extern "C" int moce_pool_residual(const void* x, int dtype, int64_t B, int64_t C
   // channel chunk: a multiple of m channels so chunk starts stay 16-byte aligned
   int64_t m = 1;
   while ((m * HW * (int64_t)es) % 16 != 0 && m < 16) m *= 2;
+  // CTAs per sample (a cluster): enough for about four CTAs per SM, at most 8
+  int64_t ncl = (4LL * num_sms() + B - 1) / B;
+  if (ncl > 8) ncl = 8;
+  if (ncl < 1) ncl = 1;
+  const int64_t per = ((C + ncl - 1) / ncl + m - 1) / m * m;    // channels per CTA
+  ncl = (C + per - 1) / per;
   int64_t cc = (int64_t)(96 * 1024 / ((size_t)HW * es));
   cc = (cc / m) * m;
   if (cc < 1) cc = 1;
-  if (cc > C) cc = C;
+  if (cc > per) cc = per;
   const size_t smem = (((size_t)cc * HW * es + 15) & ~size_t(15)) + (size_t)HW * 4 + (size_t)cc * 4;
   return dispatch_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
@@ -517,8 +537,21 @@ extern "C" int moce_pool_residual(const void* x, int dtype, int64_t B, int64_t C
         cudaFuncSetAttribute(pool_residual_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
             cudaSuccess)
       return set_error(MOCE_ERR_CUDA, "moce_pool_residual: smem %zu", smem);
-    pool_residual_kernel<T><<<(unsigned)B, 256, smem, (cudaStream_t)stream>>>(
-        static_cast<const T*>(x), (int)C, (int)HW, (int)cc, mask, meta, z, static_cast<T*>(y), (int)(E_r + 1));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ncl, (unsigned)B);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)ncl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, pool_residual_kernel<T>, static_cast<const T*>(x), (int)C, (int)HW, (int)cc,
+                           (int)per, mask, meta, z, static_cast<T*>(y), (int)(E_r + 1)) != cudaSuccess)
+      return check_launch("pool_residual_kernel");
     return check_launch("pool_residual_kernel");
   });
 }
