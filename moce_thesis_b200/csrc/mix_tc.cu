@@ -401,16 +401,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
   const int tile = blockIdx.x % a.n_tiles, bsplit = blockIdx.x / a.n_tiles;
   const int e0 = tile * 128;
   const int rows = min(128, E_r - e0);
-  const int b0 = (int)((long long)bsplit * a.B / a.n_bsplit);
-  const int b1 = (int)((long long)(bsplit + 1) * a.B / a.n_bsplit);
-  const int nb = b1 - b0;
+  // this CTA's units: [u0, u1) of the B * NT (sample, pixel tile) units of
+  // its expert tile, in sample-major order; it touches samples b0 .. b0+nb-1
+  // (the first from tile t0 on, the last up to unit u1 - 1), and writes the
+  // weights of each sample it touches
+  const long long n_units = (long long)a.B * NT;
+  const int u0 = (int)(bsplit * n_units / a.n_bsplit), u1 = (int)((bsplit + 1) * n_units / a.n_bsplit);
+  const int b0 = u0 / NT, t0 = u0 - (u0 / NT) * NT;
+  const int nb = u1 > u0 ? (u1 - 1) / NT - b0 + 1 : 0;
   const int E = E_r + 1;
 
   // ---- prologue.  The producer initializes the barriers and starts the
   // first X copies, and the weight rows start their register loads, before
   // all threads zero A, so that those latencies overlap the zeroing.
-  const unsigned char* xs = static_cast<const unsigned char*>(a.xstage) + (size_t)b0 * NT * sbytes;
-  const int nu = nb * NT;                                     // units (sample, pixel tile) of this CTA
+  const unsigned char* xs = static_cast<const unsigned char*>(a.xstage) + (size_t)u0 * sbytes;
+  const int nu = u1 - u0;                                     // units (sample, pixel tile) of this CTA
   // X quarter n = 4u + q of unit u goes to a slot of the ring.  With two
   // issuers (P == 2) issuer h consumes its two quarters of every unit (q = h
   // and h + 2, or 2h and 2h + 1; see kSplitK) from a ring of its own (slots
@@ -575,8 +580,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
         // one tile per sample: the accumulator buffer first, as it frees
         // earlier than the next weights
         if (NT == 1 && i >= 2 && !wait_peer(&bars->d_empty[i & 1], ((i - 2) >> 1) & 1, kSiteDEmptySample, i)) break;
-        for (int t = 0; t < NT && run; ++t) {
-          const int u = i * NT + t, s = u & 1;
+        // this sample's tiles in the CTA's range (one tile per sample: the
+        // tile, and unit i)
+        const int t_beg = (NT == 1 || i > 0) ? 0 : t0;
+        const int t_end = (NT == 1 || i < nb - 1) ? NT : u1 - (b0 + i) * NT;
+        for (int t = t_beg; t < t_end && run; ++t) {
+          const int u = NT == 1 ? i : (b0 + i) * NT + t - u0, s = u & 1;   // unit of this CTA
           if (NT > 1 && u >= 2) {
             if (!wait_peer(&bars->d_empty[s], ((u - 2) >> 1) & 1, kSiteDEmptyTile, u)) {
               run = false;
@@ -593,7 +602,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
               const int pc = q >> 1;
               const bool pfirst = (P == 2) ? (kSplitK || qi == 0) : (q & 1) == 0;
               const bool plast = (P == 2) ? (kSplitK || qi == 1) : (q & 1) == 1;
-              if (t == 0 && pfirst && !wait_peer(&bars->a_full[pc], i & 1, kSiteAFull, i)) {
+              if (t == t_beg && pfirst && !wait_peer(&bars->a_full[pc], i & 1, kSiteAFull, i)) {
                 run = false;
                 break;
               }
@@ -616,7 +625,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
               }
               umma_commit(&bars->slot_free[slot]);
               // the last tile of the sample releases the half's weights
-              if (t == NT - 1 && plast) umma_commit(&bars->a_free[pc]);
+              if (t == t_end - 1 && plast) umma_commit(&bars->a_free[pc]);
             }
           }
           if (!run) break;
@@ -793,7 +802,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       const uint32_t pitch = (uint32_t)a.stg_pitch;
       unsigned char* row0 = reinterpret_cast<unsigned char*>(stg) + (size_t)dt * pitch;
       for (int u = 0; u < nu; ++u) {
-        const int s = u & 1, i = u / NT, t = u - (u / NT) * NT;
+        const int s = u & 1, ug = u0 + u, i = ug / NT - b0, t = ug - (ug / NT) * NT;
         const int p0 = t * NP, tp = min(NP, HW - p0);       // a multiple of 8
         unsigned char* row = row0 + (size_t)(u % a.nsb) * 128u * pitch;
         bool ok = true;
@@ -883,7 +892,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       // pixel tiles of 16-byte aligned rows when no staging buffer fits:
       // 16-byte stores from registers straight to Y
       for (int u = 0; u < nu; ++u) {
-        const int s = u & 1, i = u / NT, t = u - (u / NT) * NT;
+        const int s = u & 1, ug = u0 + u, i = ug / NT - b0, t = ug - (ug / NT) * NT;
         const int p0 = t * NP, tp = min(NP, HW - p0);
         bool ok = true;
         if (dlead) ok = wait_peer(&bars->d_full[s], (u >> 1) & 1, kSiteDFull, u);
@@ -931,7 +940,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
       // other pixel tiles: 16-bit stores into rows of the tile's width, one
       // bulk copy (or element copy) per row
       for (int u = 0; u < nu; ++u) {
-        const int s = u & 1, i = u / NT, t = u - (u / NT) * NT;
+        const int s = u & 1, ug = u0 + u, i = ug / NT - b0, t = ug - (ug / NT) * NT;
         const int p0 = t * NP, tp = min(NP, HW - p0);         // this tile's pixels
         bool ok = true;
         if (dlead) ok = wait_peer(&bars->d_full[s], (u >> 1) & 1, kSiteDFull, u);
@@ -1223,9 +1232,11 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
   MOCE_REQUIRE(ns >= 2, MOCE_ERR_UNSUPPORTED, "moce_mix_tc: not enough shared memory (%d B)", smem_optin_tc());
   const size_t smem = fixed + (size_t)ns * qbytes;
   const int n_tiles = (int)((E_r + 127) / 128);
+  // CTAs per expert tile: one per SM over all tiles, each with a range of
+  // (sample, pixel tile) units (a range may start and end inside a sample)
   int n_bsplit = num_sms() / n_tiles;
   if (n_bsplit < 1) n_bsplit = 1;
-  if (n_bsplit > B) n_bsplit = (int)B;
+  if (n_bsplit > B * sh.NT) n_bsplit = (int)(B * sh.NT);
   TcArgs a{xstage, y, gate.z, idx, ln, gate.gate_w, gate.gate_b, gate.T_out, gate.tmin_tau, gate.trange_tau, gate.T_in,
            (int)B, (int)C, (int)HW, (int)E_r, (int)k, Kp, n_tiles, n_bsplit, ns, sh.NP, sh.NA, sh.P, sh.NT,
            sh.tmem_cols, (unsigned long long)g_wait_ns.load(), sh.drain, sh.stg_pitch, sh.nsb, sh.stage_bytes, ep};

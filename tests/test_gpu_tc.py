@@ -50,6 +50,9 @@ def relerr(a, b):
     (3, 72, 4, 4, 100, 8, torch.float16),       # HW == 16, 16-byte staging stores of one tile
     (59, 512, 7, 7, 601, 32, torch.bfloat16),   # 5 expert tiles (the last of 88 rows), samples split 29 ways
     (59, 192, 6, 6, 601, 16, torch.float16),    # the same through the general one-tile kernel (N = 48)
+    (11, 64, 56, 56, 64, 4, torch.bfloat16),    # 143 (sample, tile) units over 143 CTAs: ranges inside samples
+    (13, 128, 28, 28, 300, 16, torch.bfloat16), # 3 expert tiles x 49 CTAs over 52 units: ranges cross samples
+    (7, 256, 14, 14, 130, 16, torch.float16),   # two expert tiles (the second of one row), one-tile samples
 ])
 def test_tc_mix_matches_oracle(B, C, H_, W_, E, k, dtype):
     gen = torch.Generator().manual_seed(B * 100 + C + k)
