@@ -810,20 +810,22 @@ def resnet_measure(args, world, rank, local, dev, steps, global_batch=1024, eage
             with Clocks(local) as clk:
                 if world > 1:
                     dist.barrier()
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(st)
-                for _ in range(steps):
+                evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+                evs[0].record(st)
+                for i in range(steps):
                     fwd()
-                e1.record(st)
+                    evs[i + 1].record(st)
                 torch.cuda.synchronize()
             del g
-        return _max_over_ranks(e0.elapsed_time(e1), world, dev) / steps, clk.summary()
+        # per-forward device times (this rank), to show a slow phase if one occurs
+        per_step = [round(evs[i].elapsed_time(evs[i + 1]), 3) for i in range(steps)]
+        return _max_over_ranks(evs[0].elapsed_time(evs[-1]), world, dev) / steps, clk.summary(), per_step
 
     # MoCE -> bn1 -> relu1 fused in the MoCE kernels (the product path, the
     # headline value), then the reference's eval sequence (MoCE, then
     # BatchNorm and ReLU as torch ops) on the same weights
     resnet.set_fused_epilogue(model, True)
-    ms, clocks = timed(graph=True)
+    ms, clocks, per_step = timed(graph=True)
     out = {"metric": "ResNet-50-MoCE inference img/s", "value": round(gb / (ms * 1e-3), 1), "unit": "img/s",
            "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
@@ -833,14 +835,14 @@ def resnet_measure(args, world, rank, local, dev, steps, global_batch=1024, eage
                       "parallelism": f"data-parallel x{world}, no collective in inference",
                       "inference": "MoCE -> bn1 -> relu1 in the MoCE kernels; other layers torch / cuDNN, NCHW; "
                                    "the forward replayed as one CUDA graph"},
-           "clocks": clocks}
+           "clocks": clocks, "step_ms_rank0": per_step}
     if eager:
-        ms_eager, _ = timed()
+        ms_eager, _, _ = timed()
         out["eager"] = {"value": round(gb / (ms_eager * 1e-3), 1), "ms_per_step": round(ms_eager, 3),
                         "note": "same path, launched op by op instead of one CUDA graph"}
     if unfused:
         resnet.set_fused_epilogue(model, False)
-        ms_plain, _ = timed()
+        ms_plain, _, _ = timed()
         resnet.set_fused_epilogue(model, True)
         out["unfused"] = {"value": round(gb / (ms_plain * 1e-3), 1), "ms_per_step": round(ms_plain, 3),
                           "note": "reference eval order, eager"}

@@ -451,6 +451,24 @@ int moce_aux_loss_backward(const float* logits, int64_t E_r, int64_t C,
                            void* workspace, size_t workspace_bytes,
                            void* stream);
 
+/*
+ * The bottleneck's other eval-mode BatchNorms, fused with what follows them
+ * (models_unified.py:155-169: relu2(bn2(conv2)), relu3(bn3(conv3) +
+ * shortcut)), in one pass over NCHW tensors [N, C, HW] of x's dtype:
+ *   y = act(x * scale[c] + shift[c] + (residual ? residual * rs[c] + rt[c] : 0))
+ * with rs = 1, rt = 0 when r_scale / r_shift are null (an identity shortcut)
+ * and act the ReLU when relu != 0 (a NaN stays NaN).  scale / shift (and
+ * r_scale / r_shift, for a shortcut convolution's BatchNorm) are the
+ * BatchNorms folded to fp32 per-channel affines: scale = weight /
+ * sqrt(running_var + eps), shift = bias - running_mean * scale.  y may be x.
+ * No reference counterpart (the reference runs the BatchNorm, add and ReLU
+ * as torch ops).
+ */
+int moce_bn_act(const void* x, int dtype, int64_t N, int64_t C, int64_t HW,
+                const float* scale, const float* shift, const void* residual,
+                const float* r_scale, const float* r_shift, int relu, void* y,
+                void* stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

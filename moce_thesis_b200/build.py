@@ -34,7 +34,7 @@ NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-
                      "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]
 
 CU_SOURCES = ["status.cu", "route.cu", "schedule.cu", "forward.cu", "mix.cu", "stage.cu", "gate.cu", "mix_tc.cu", "simt.cu",
-              "backward.cu", "aux.cu", "noalloc.cu"]
+              "backward.cu", "aux.cu", "noalloc.cu", "epilogue.cu"]
 
 
 def _run(cmd, verbose):

@@ -71,6 +71,7 @@ SIGNATURES = {
     "moce_aux_workspace_bytes": (_sz, [_i64, _i64]),
     "moce_aux_loss": (_i32, [_p, _i64, _i64, _f32, _f32, _f32, _f32, _f32, _p, _p, _sz, _p]),
     "moce_aux_loss_backward": (_i32, [_p, _i64, _i64, _f32, _f32, _f32, _f32, _f32, _p, _p, _p, _sz, _p]),
+    "moce_bn_act": (_i32, [_p, _i32, _i64, _i64, _i64, _p, _p, _p, _p, _p, _i32, _p, _p]),
     "moce_backward_t": (_i32, [_p, _p, _i32, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _p, _p, _p,
                                _p, _p, _sz, _p]),
 }

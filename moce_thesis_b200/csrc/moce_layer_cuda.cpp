@@ -505,6 +505,58 @@ torch::Tensor forward_tc_ep(torch::Tensor x, torch::Tensor idx, torch::Tensor ln
   return y;
 }
 
+// a bottleneck's eval BatchNorm (folded to scale / shift per channel), an
+// optional residual with its own optional affine, and an optional ReLU in one
+// pass; in place when out is x
+torch::Tensor bn_act(torch::Tensor x, torch::Tensor scale, torch::Tensor shift, c10::optional<torch::Tensor> r_opt,
+                     c10::optional<torch::Tensor> rs_opt, c10::optional<torch::Tensor> rt_opt, bool relu,
+                     c10::optional<torch::Tensor> out_opt) {
+  CHECK_INPUT(x);
+  CHECK_INPUT(scale);
+  CHECK_INPUT(shift);
+  const c10::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(x.dim() == 4, "x must be [N, C, H, W]");
+  const int64_t N = x.size(0), C = x.size(1), HW = x.size(2) * x.size(3);
+  auto f32c = [&](const torch::Tensor& t, const char* name) {
+    TORCH_CHECK(t.scalar_type() == torch::kFloat32 && t.numel() == C, name, " must be float32 [C]");
+    TORCH_CHECK(t.device() == x.device(), name, " must be on the device of x");
+  };
+  f32c(scale, "scale");
+  f32c(shift, "shift");
+  const void* r = nullptr;
+  const float* rs = nullptr;
+  const float* rt = nullptr;
+  if (r_opt.has_value()) {
+    CHECK_INPUT(*r_opt);
+    TORCH_CHECK(r_opt->sizes() == x.sizes() && r_opt->scalar_type() == x.scalar_type() &&
+                    r_opt->device() == x.device(),
+                "residual must match x");
+    r = r_opt->data_ptr();
+  }
+  TORCH_CHECK(rs_opt.has_value() == rt_opt.has_value(), "r_scale and r_shift go together");
+  if (rs_opt.has_value()) {
+    TORCH_CHECK(r != nullptr, "r_scale without a residual");
+    CHECK_INPUT(*rs_opt);
+    CHECK_INPUT(*rt_opt);
+    f32c(*rs_opt, "r_scale");
+    f32c(*rt_opt, "r_shift");
+    rs = rs_opt->data_ptr<float>();
+    rt = rt_opt->data_ptr<float>();
+  }
+  torch::Tensor y;
+  if (out_opt.has_value()) {
+    y = *out_opt;
+    CHECK_INPUT(y);
+    TORCH_CHECK(y.sizes() == x.sizes() && y.scalar_type() == x.scalar_type() && y.device() == x.device(),
+                "out must match x");
+  } else {
+    y = torch::empty_like(x);
+  }
+  ok(moce_bn_act(x.data_ptr(), dtype_of(x), N, C, HW, scale.data_ptr<float>(), shift.data_ptr<float>(), r, rs, rt,
+                 relu ? 1 : 0, y.data_ptr(), cur_stream()));
+  return y;
+}
+
 bool px_supported(torch::Tensor x, int64_t k) {
   if (x.dim() != 4) return false;
   return moce_px_supported(dtype_of(x), x.size(1), x.size(2) * x.size(3), k) != 0;
@@ -853,6 +905,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("meta"), py::arg("group_expert"), py::arg("sched"), py::arg("gate_w"), py::arg("gate_b"),
         py::arg("tmin_tau"), py::arg("trange_tau"), py::arg("want_T") = false, py::arg("out") = py::none());
   m.def("tc_supported", &tc_supported, "Whether the tensor-core mix takes this input");
+  m.def("bn_act", &bn_act,
+        "y = act(x * scale + shift + residual * r_scale + r_shift): a folded eval BatchNorm with an optional "
+        "residual (its own optional affine) and ReLU, one pass over NCHW",
+        py::arg("x"), py::arg("scale"), py::arg("shift"), py::arg("residual") = py::none(),
+        py::arg("r_scale") = py::none(), py::arg("r_shift") = py::none(), py::arg("relu") = true,
+        py::arg("out") = py::none());
   m.def("forward_tc_ep", &forward_tc_ep,
         "Tensor-core forward with a folded BatchNorm (scale, shift per output channel) and ReLU on the outputs",
         py::arg("x"), py::arg("idx"), py::arg("ln"), py::arg("mask"), py::arg("meta"), py::arg("gate_w"),

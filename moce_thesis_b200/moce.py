@@ -388,20 +388,19 @@ class MoCE(nn.Module):
 
         On the tensor-core path the BatchNorm, folded to a per-channel
         scale / shift, and the ReLU are applied to each output in the mix's
-        store (one pass over Y instead of three).  Other inputs, or a
-        BatchNorm in training mode, run forward_eval and then the torch ops.
+        store (one pass over Y instead of three).  The CUDA-core paths run
+        forward_eval and then the folded BatchNorm and ReLU as one native
+        pass over Y (``moce_bn_act``); a BatchNorm in training mode, or a CPU
+        tensor, runs the torch ops.
         """
         if self.cached_indices is None:
             raise RuntimeError("MoCE eval cache not built. Call build_moce_cache(model) before eval.")
         m = native()
         use_bn_stats = (not bn.training) and bn.running_mean is not None and bn.running_var is not None
-        if not (use_bn_stats and m.tc_supported(x, self.k)) or self.gate_type == "mlp":
+        if not use_bn_stats or not x.is_cuda:
             y = bn(self.forward_eval(x))
             return F.relu(y) if relu else y
-        route = self._route
-        if route is None or route.idx.device != x.device:
-            route = _Route(self.routing_logits, self.k, transposed=False)
-            self._route = route
+
         def fold():
             inv = torch.rsqrt(bn.running_var.float() + float(bn.eps))
             scale = inv if bn.weight is None else bn.weight.float() * inv
@@ -411,6 +410,15 @@ class MoCE(nn.Module):
             return scale.contiguous(), shift.contiguous()
         scale, shift = self._cached_f32("bn", (bn.running_mean, bn.running_var, bn.weight, bn.bias), fold,
                                         (float(bn.eps),))
+        if not m.tc_supported(x, self.k) or self.gate_type == "mlp":
+            # the CUDA-core paths: the layer, then the folded BatchNorm and the
+            # ReLU as one native pass in place
+            y = self.forward_eval(x)
+            return m.bn_act(y, scale, shift, relu=bool(relu), out=y)
+        route = self._route
+        if route is None or route.idx.device != x.device:
+            route = _Route(self.routing_logits, self.k, transposed=False)
+            self._route = route
         gw, gb = self._gate_f32()
         y = m.forward_tc_ep(x.contiguous(), route.idx, route.ln, route.mask, route.meta, gw, gb,
                             float(self.cached_temp_min_tau), float(self.cached_temp_range_tau),

@@ -13,18 +13,47 @@ torch / cuDNN.
 What differs: in eval mode a block without projection runs MoCE -> bn1 ->
 relu1 as one native call (``MoCE.forward_eval_bn_relu``: on the tensor-core
 path the BatchNorm, folded to a per-channel scale and shift, and the ReLU are
-applied in the mix's output store).  ``fuse_epilogue=False`` on a block, or
-``set_fused_epilogue(model, False)``, restores the three separate ops.
+applied in the mix's output store), and the block's other BatchNorms run as
+one native pass each with what follows them (``moce_bn_act``: relu2(bn2(.)),
+and relu3(bn3(.) + shortcut) with the shortcut's own BatchNorm folded in),
+as does the stem's BatchNorm and ReLU.  ``fuse_epilogue=False`` on a block,
+or ``set_fused_epilogue(model, False)``, restores the separate torch ops.
 """
 from __future__ import annotations
 
 import torch
 import torch.nn as nn
 
-from .moce import MoCE
+from .moce import MoCE, native
 
 # per-block k (one list per stage), models_unified.py:25-30
 DEFAULT_MOCE_K_50 = [[8, 8, 8], [12, 12, 12, 12], [24] * 6, [48, 48, 48]]
+
+
+def _bn_eval(bn) -> bool:
+    """An eval-mode BatchNorm2d with running statistics (foldable)."""
+    return (isinstance(bn, nn.BatchNorm2d) and not bn.training and bn.running_mean is not None
+            and bn.running_var is not None)
+
+
+def bn_affine(bn):
+    """The eval BatchNorm as fp32 (scale, shift) per channel: scale = weight /
+    sqrt(running_var + eps), shift = bias - running_mean * scale.  Cached on
+    the module per version of its buffers and parameters."""
+    ts = (bn.running_mean, bn.running_var, bn.weight, bn.bias)
+    key = tuple((t.data_ptr(), t._version, t.device) if t is not None else None for t in ts) + (float(bn.eps),)
+    hit = bn.__dict__.get("_moce_affine")
+    if hit is not None and hit[0] == key:
+        return hit[1]
+    with torch.no_grad():
+        inv = torch.rsqrt(bn.running_var.float() + float(bn.eps))
+        scale = inv if bn.weight is None else bn.weight.float() * inv
+        shift = -bn.running_mean.float() * scale
+        if bn.bias is not None:
+            shift = shift + bn.bias.float()
+    val = (scale.contiguous(), shift.contiguous())
+    bn.__dict__["_moce_affine"] = (key, val)
+    return val
 
 
 def normalize_k_config(k, layers_config):
@@ -75,10 +104,28 @@ class BottleneckWithMoCEProjection(nn.Module):
     def forward(self, x):
         if self.projection is None and not self.training and self.fuse_epilogue:
             out = self.moce.forward_eval_bn_relu(x, self.bn1, relu=True)
+        elif (self.projection is not None and not self.training and self.fuse_epilogue and x.is_cuda
+              and _bn_eval(self.bn_proj)):
+            # MoCE, the projection, then relu1(bn_proj(.)) as one native pass
+            out = self.projection(self.moce(x)).contiguous()
+            out = native().bn_act(out, *bn_affine(self.bn_proj), relu=True, out=out)
         else:
             out = self.moce(x)
             out = self.bn_proj(self.projection(out)) if self.projection is not None else self.bn1(out)
             out = self.relu1(out)
+        sc_bn = self.shortcut[1] if len(self.shortcut) == 2 else None
+        if (not self.training and self.fuse_epilogue and out.is_cuda and _bn_eval(self.bn2) and _bn_eval(self.bn3)
+                and (sc_bn is None or _bn_eval(sc_bn))):
+            # relu2(bn2(conv2)) and relu3(bn3(conv3) + shortcut) as one
+            # native pass each, in place on the convolution outputs
+            m = native()
+            out = self.conv2(out).contiguous()
+            out = m.bn_act(out, *bn_affine(self.bn2), relu=True, out=out)
+            out = self.conv3(out).contiguous()
+            if sc_bn is None:
+                return m.bn_act(out, *bn_affine(self.bn3), x.contiguous(), relu=True, out=out)
+            r = self.shortcut[0](x).contiguous()
+            return m.bn_act(out, *bn_affine(self.bn3), r, *bn_affine(sc_bn), relu=True, out=out)
         out = self.relu2(self.bn2(self.conv2(out)))
         out = self.bn3(self.conv3(out))
         out = out + self.shortcut(x)
@@ -111,6 +158,7 @@ class ResNet50(nn.Module):
             self.maxpool = nn.Identity()
         self.bn1 = nn.BatchNorm2d(64)
         self.relu = nn.ReLU(inplace=True)
+        self.fuse_epilogue = True
         widths, strides = (64, 128, 256, 512), (1, 2, 2, 2)
         for i in range(4):
             setattr(self, f"layer{i + 1}", self._make_layer(widths[i], self.layers_config[i], strides[i], i))
@@ -145,7 +193,11 @@ class ResNet50(nn.Module):
                     nn.init.constant_(m.bias, 0)
 
     def forward(self, x):
-        x = self.maxpool(self.relu(self.bn1(self.conv1(x))))
+        if not self.training and self.fuse_epilogue and x.is_cuda and _bn_eval(self.bn1):
+            y = self.conv1(x).contiguous()
+            x = self.maxpool(native().bn_act(y, *bn_affine(self.bn1), relu=True, out=y))
+        else:
+            x = self.maxpool(self.relu(self.bn1(self.conv1(x))))
         x = self.layer4(self.layer3(self.layer2(self.layer1(x))))
         return self.fc(torch.flatten(self.avgpool(x), 1))
 
@@ -167,6 +219,6 @@ def build_moce_cache(model):
 def set_fused_epilogue(model, on=True):
     """Switch the eval-mode MoCE -> bn1 -> relu1 fusion of every block."""
     for module in model.modules():
-        if isinstance(module, BottleneckWithMoCEProjection):
+        if isinstance(module, (BottleneckWithMoCEProjection, ResNet50)):
             module.fuse_epilogue = bool(on)
 
