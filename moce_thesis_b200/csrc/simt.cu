@@ -186,14 +186,24 @@ __global__ void __launch_bounds__(px_threads(NSLAB), 1) mix_px_kernel(PxArgs a) 
 // them, k <= 16 KL16); the gate, temperature and softmax reduce over the 16
 // lanes of the half, and each support's channel and weight reach the half by
 // a width-16 shuffle.  X_b in one CTA's shared memory, as mix_px_kernel.
-template <typename T, int KL16>
+//
+// kCw: each half writes its expert's supports as (row offset, weight) pairs
+// into a buffer of the warp in shared memory, and the pixel loop reads two
+// supports per 16-byte load (a broadcast within each half; the halves'
+// buffers 16 bytes out of bank step) instead of two width-16 shuffles per
+// support.  Taken when the buffers fit beside X_b.
+template <typename T, int KL16, bool kCw>
 __global__ void __launch_bounds__(px_threads(1), 1) mix_px_half_kernel(PxArgs a) {
   constexpr int kPxThreads = px_threads(1), kPxWarps = kPxThreads / 32;
+  constexpr int kCwStride = KL16 * 8 + 1;                                              // float4 per half
   extern __shared__ __align__(16) unsigned char s_raw[];
   const int C = a.C, HW = a.HW, HWp = a.HWp, k = a.k, E_r = a.E_r;
   T* s_x = reinterpret_cast<T*>(s_raw);                                                // C x HWp
   float* s_z = reinterpret_cast<float*>(s_raw + (((size_t)C * HWp * sizeof(T) + 15) & ~size_t(15)));  // C
   float* s_gw = s_z + C;                                                               // k
+  // kCw: [warp][half][kCwStride] float4, after z and the gate weights
+  float4* s_cw = reinterpret_cast<float4*>(
+      s_raw + ((reinterpret_cast<unsigned char*>(s_gw + k) - s_raw + 15) & ~(ptrdiff_t)15));
   const int b = blockIdx.y, ch = blockIdx.x, nch = gridDim.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hl = lane & 15, hsel = lane >> 4;
@@ -251,18 +261,43 @@ __global__ void __launch_bounds__(px_threads(1), 1) mix_px_half_kernel(PxArgs a)
     for (int q = 0; q < KL16; ++q) a_l[q] /= sum;
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     const int p = 4 * hl;
+    if constexpr (kCw) {
+      float4* cw = s_cw + (size_t)(2 * warp + hsel) * kCwStride;
+      float2* cw2 = reinterpret_cast<float2*>(cw);
 #pragma unroll
-    for (int q = 0; q < KL16; ++q) {
-      const int nq = min(16, k - 16 * q);
+      for (int q = 0; q < KL16; ++q)
+        cw2[hl + 16 * q] = make_float2(__int_as_float(c_l[q] * HWp), a_l[q]);
+      __syncwarp();
 #pragma unroll 4
-      for (int j = 0; j < nq; ++j) {
-        const int c = __shfl_sync(kFull, c_l[q], j, 16);
-        const float w = __shfl_sync(kFull, a_l[q], j, 16);
+      for (int j2 = 0; 2 * j2 < k; ++j2) {
+        const float4 v = cw[j2];                              // supports 2 j2 and 2 j2 + 1
         if (p < HW) {
           float f[4];
-          ld4<T>(s_x + (size_t)c * HWp + p, f);
+          ld4<T>(s_x + __float_as_int(v.x) + p, f);
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj) acc[jj] = fmaf(w, f[jj], acc[jj]);
+          for (int jj = 0; jj < 4; ++jj) acc[jj] = fmaf(v.y, f[jj], acc[jj]);
+          if (2 * j2 + 1 < k) {
+            ld4<T>(s_x + __float_as_int(v.z) + p, f);
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) acc[jj] = fmaf(v.w, f[jj], acc[jj]);
+          }
+        }
+      }
+      __syncwarp();                                           // read before the next pair's writes
+    } else {
+#pragma unroll
+      for (int q = 0; q < KL16; ++q) {
+        const int nq = min(16, k - 16 * q);
+#pragma unroll 4
+        for (int j = 0; j < nq; ++j) {
+          const int c = __shfl_sync(kFull, c_l[q], j, 16);
+          const float w = __shfl_sync(kFull, a_l[q], j, 16);
+          if (p < HW) {
+            float f[4];
+            ld4<T>(s_x + (size_t)c * HWp + p, f);
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) acc[jj] = fmaf(w, f[jj], acc[jj]);
+          }
         }
       }
     }
@@ -552,7 +587,7 @@ static int mix_px_run(const void* x, int dtype, int64_t B, int64_t C, int64_t HW
   const int HWp = (int)((HW + 3) / 4 * 4);
   const int CL = px_cluster(dtype, C, HW, k);
   const int64_t Ch = CL == 1 ? C : (C + 1) / 2;
-  const size_t smem = px_smem_split(C, Ch, HW, k, esize);
+  size_t smem = px_smem_split(C, Ch, HW, k, esize);
   const int nslab = (int)((HW + 127) / 128);
   const int nthr = px_threads(nslab), kPxWarps = nthr / 32;
   // CTAs per sample: the count whose rounds over the SMs waste least.  A
@@ -588,12 +623,19 @@ static int mix_px_run(const void* x, int dtype, int64_t B, int64_t C, int64_t HW
   case NS:                                                                                        \
     kern = grouped ? mix_px_grouped_kernel<T, NS, 16> : CL == 2 ? MOCE_PX_KL(NS, 2) : MOCE_PX_KL(NS, 1); \
     break;
-    // maps of at most 64 pixels: two experts per warp (half-warps)
+    // maps of at most 64 pixels: two experts per warp (half-warps), with the
+    // supports staged per warp in shared memory when that fits
     const bool half = CL == 1 && HW <= 64 && !grouped;
-    if (half)
-      kern = k <= 16 ? mix_px_half_kernel<T, 1> : k <= 32 ? mix_px_half_kernel<T, 2>
-             : k <= 64 ? mix_px_half_kernel<T, 4> : mix_px_half_kernel<T, 8>;
-    else switch (nslab) {
+    if (half) {
+      const int kl16 = k <= 16 ? 1 : k <= 32 ? 2 : k <= 64 ? 4 : 8;
+      const size_t cw_end = ((smem + 15) & ~size_t(15)) + (size_t)kPxWarps * 2 * (kl16 * 8 + 1) * 16;
+      const bool cw = cw_end <= (size_t)px_smem_max();
+      if (cw) smem = cw_end;
+      kern = k <= 16 ? (cw ? mix_px_half_kernel<T, 1, true> : mix_px_half_kernel<T, 1, false>)
+             : k <= 32 ? (cw ? mix_px_half_kernel<T, 2, true> : mix_px_half_kernel<T, 2, false>)
+             : k <= 64 ? (cw ? mix_px_half_kernel<T, 4, true> : mix_px_half_kernel<T, 4, false>)
+                       : (cw ? mix_px_half_kernel<T, 8, true> : mix_px_half_kernel<T, 8, false>);
+    } else switch (nslab) {
       MOCE_PX_PICK(1)
       MOCE_PX_PICK(2)
       MOCE_PX_PICK(3)
