@@ -49,6 +49,9 @@ def test_workspace_queries_are_host_only():
     lambda l: l.moce_pool(1, 7, 1, 4, 4, 1, None),                                     # bad dtype
     lambda l: l.moce_forward_dynamic_temp(1, 0, 1, 16, 1, 1, 1, 1, 4, 4, 3, 2, None),  # bad index width
     lambda l: l.moce_gate_temperature(1, 0, None, -1, 4, 4, 1, 3, 2, 1, 1, 0.1, 1.0, None, 1, None),
+    lambda l: l.moce_bn_act(1, 0, 2, 4, 9, None, 1, None, None, None, 1, 1, None),        # no scale
+    lambda l: l.moce_bn_act(1, 0, 2, 4, 9, 1, 1, None, 1, 1, 1, 1, None),                 # affine without residual
+    lambda l: l.moce_bn_act(1, 0, 2, 4, 9, 1, 1, 1, 1, None, 1, 1, None),                 # r_scale without r_shift
 ])
 def test_invalid_arguments_rejected_on_host(call):
     lib = capi.lib()
