@@ -49,9 +49,13 @@ struct PxArgs {
 // half of X_b's channels, and a support row of the other half is read from
 // the peer's shared memory (distributed shared memory), so samples of up to
 // twice the shared memory of one CTA (C = 1024 at 14x14) stay on chip.
-template <typename T, int NSLAB, int KL, int CL>
+// kCw: the expert's supports are staged as (channel, weight) pairs in a
+// buffer of the warp in shared memory and read two per 16-byte broadcast
+// load, in place of two shuffles per support (when the buffers fit).
+template <typename T, int NSLAB, int KL, int CL, bool kCw>
 __global__ void __launch_bounds__(px_threads(NSLAB), 1) mix_px_kernel(PxArgs a) {
   constexpr int kPxThreads = px_threads(NSLAB), kPxWarps = kPxThreads / 32;
+  constexpr int kCwStride = KL * 16 + 1;                                               // float4 per warp
   extern __shared__ __align__(16) unsigned char s_raw[];
   const int C = a.C, HW = a.HW, HWp = a.HWp, k = a.k, E_r = a.E_r;
   const int Ch = (CL == 1) ? C : a.csplit;                                             // channels per CTA
@@ -61,6 +65,9 @@ __global__ void __launch_bounds__(px_threads(NSLAB), 1) mix_px_kernel(PxArgs a) 
   T* s_x = reinterpret_cast<T*>(s_raw);                                                // Ch x HWp
   float* s_z = reinterpret_cast<float*>(s_raw + (((size_t)Ch * HWp * sizeof(T) + 15) & ~size_t(15)));  // C
   float* s_gw = s_z + C;                                                               // k
+  // kCw: [warp][kCwStride] float4, after z and the gate weights
+  float4* s_cw = reinterpret_cast<float4*>(
+      s_raw + ((reinterpret_cast<unsigned char*>(s_gw + k) - s_raw + 15) & ~(ptrdiff_t)15));
   const int b = blockIdx.y, ch = blockIdx.x, nch = gridDim.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const T* xg = static_cast<const T*>(a.x);
@@ -136,31 +143,46 @@ __global__ void __launch_bounds__(px_threads(NSLAB), 1) mix_px_kernel(PxArgs a) 
     for (int sl = 0; sl < NSLAB; ++sl)
 #pragma unroll
       for (int j = 0; j < 4; ++j) acc[sl][j] = 0.0f;
+    // one support's row into the accumulators (the row's owner is uniform
+    // across the warp: one support at a time)
+    auto mix_support = [&](int c, float w) {
+      auto mix_row = [&](const T* row) {
 #pragma unroll
-    for (int q = 0; q < KL; ++q) {
-      const int nq = min(32, k - 32 * q);
-#pragma unroll 4
-      for (int j = 0; j < nq; ++j) {
-        const int c = __shfl_sync(kFull, c_l[q], j);
-        const float w = __shfl_sync(kFull, a_l[q], j);
-        auto mix_row = [&](const T* row) {
+        for (int sl = 0; sl < NSLAB; ++sl) {
+          if (128 * sl + 4 * lane < HW) {
+            float f[4];
+            ld4<T>(row + 128 * sl, f);
 #pragma unroll
-          for (int sl = 0; sl < NSLAB; ++sl) {
-            if (128 * sl + 4 * lane < HW) {
-              float f[4];
-              ld4<T>(row + 128 * sl, f);
-#pragma unroll
-              for (int jj = 0; jj < 4; ++jj) acc[sl][jj] = fmaf(w, f[jj], acc[sl][jj]);
-            }
+            for (int jj = 0; jj < 4; ++jj) acc[sl][jj] = fmaf(w, f[jj], acc[sl][jj]);
           }
-        };
-        if constexpr (CL == 1) {
-          mix_row(s_x + (size_t)c * HWp + 4 * lane);
-        } else {
-          // the row's owner is uniform across the warp (one support at a time)
-          if (c >= cs0 && c < cs0 + chn) mix_row(s_x + (size_t)(c - cs0) * HWp + 4 * lane);
-          else mix_row(s_peer + (size_t)(c - (rank ^ 1) * Ch) * HWp + 4 * lane);
         }
+      };
+      if constexpr (CL == 1) {
+        mix_row(s_x + (size_t)c * HWp + 4 * lane);
+      } else {
+        if (c >= cs0 && c < cs0 + chn) mix_row(s_x + (size_t)(c - cs0) * HWp + 4 * lane);
+        else mix_row(s_peer + (size_t)(c - (rank ^ 1) * Ch) * HWp + 4 * lane);
+      }
+    };
+    if constexpr (kCw) {
+      float4* cw = s_cw + (size_t)warp * kCwStride;
+      float2* cw2 = reinterpret_cast<float2*>(cw);
+#pragma unroll
+      for (int q = 0; q < KL; ++q) cw2[lane + 32 * q] = make_float2(__int_as_float(c_l[q]), a_l[q]);
+      __syncwarp();
+#pragma unroll 2
+      for (int j2 = 0; 2 * j2 < k; ++j2) {
+        const float4 v = cw[j2];                              // supports 2 j2 and 2 j2 + 1
+        mix_support(__float_as_int(v.x), v.y);
+        if (2 * j2 + 1 < k) mix_support(__float_as_int(v.z), v.w);
+      }
+      __syncwarp();                                           // read before the next expert's writes
+    } else {
+#pragma unroll
+      for (int q = 0; q < KL; ++q) {
+        const int nq = min(32, k - 32 * q);
+#pragma unroll 4
+        for (int j = 0; j < nq; ++j) mix_support(__shfl_sync(kFull, c_l[q], j), __shfl_sync(kFull, a_l[q], j));
       }
     }
     T* yr = yg + ((size_t)b * E + e) * HW;
@@ -614,14 +636,23 @@ static int mix_px_run(const void* x, int dtype, int64_t B, int64_t C, int64_t HW
   const int vec = (HW % 4 == 0) && (((uintptr_t)y) % 16 == 0);
   PxArgs a{x, y, z, idx, ln, gate_w, gate_b, T_in ? nullptr : T_out, tmin_tau, trange_tau, T_in,
            (int)B, (int)C, (int)HW, HWp, (int)E_r, (int)k, vec, 0, (int)Ch};
+  // warp buffers of (channel, weight) pairs for the warp-per-expert kernel
+  const int kl32 = k <= 32 ? 1 : k <= 64 ? 2 : 4;
+  const size_t cw_end = ((smem + 15) & ~size_t(15)) + (size_t)kPxWarps * (kl32 * 16 + 1) * 16;
+  const bool cw_fits = cw_end <= (size_t)px_smem_max();
   return dispatch_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
     void (*kern)(PxArgs) = nullptr;
-#define MOCE_PX_KL(NS, CLN) (k <= 32 ? mix_px_kernel<T, NS, 1, CLN> : k <= 64 ? mix_px_kernel<T, NS, 2, CLN> \
-                                                                          : mix_px_kernel<T, NS, 4, CLN>)
+#define MOCE_PX_KL(NS, CLN) (k <= 32 ? mix_px_kernel<T, NS, 1, CLN, false> : k <= 64 ? mix_px_kernel<T, NS, 2, CLN, false> \
+                                                                          : mix_px_kernel<T, NS, 4, CLN, false>)
+#define MOCE_PX_KLC(NS, CLN) (k <= 32 ? mix_px_kernel<T, NS, 1, CLN, true> : k <= 64 ? mix_px_kernel<T, NS, 2, CLN, true> \
+                                                                           : mix_px_kernel<T, NS, 4, CLN, true>)
 #define MOCE_PX_PICK(NS)                                                                          \
   case NS:                                                                                        \
-    kern = grouped ? mix_px_grouped_kernel<T, NS, 16> : CL == 2 ? MOCE_PX_KL(NS, 2) : MOCE_PX_KL(NS, 1); \
+    kern = grouped ? mix_px_grouped_kernel<T, NS, 16>                                             \
+           : cw_fits ? (CL == 2 ? MOCE_PX_KLC(NS, 2) : MOCE_PX_KLC(NS, 1))                        \
+                     : (CL == 2 ? MOCE_PX_KL(NS, 2) : MOCE_PX_KL(NS, 1));                          \
+    if (!grouped && cw_fits) smem = cw_end;                                                       \
     break;
     // maps of at most 64 pixels: two experts per warp (half-warps), with the
     // supports staged per warp in shared memory when that fits
@@ -644,6 +675,7 @@ static int mix_px_run(const void* x, int dtype, int64_t B, int64_t C, int64_t HW
     }
 #undef MOCE_PX_PICK
 #undef MOCE_PX_KL
+#undef MOCE_PX_KLC
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return set_error(MOCE_ERR_CUDA, "moce_mix_px: cannot reserve %zu B shared memory", smem);
     cudaLaunchConfig_t cfg = {};
