@@ -376,8 +376,12 @@ __global__ void __launch_bounds__(kPxThreadsB, 1) bwd_px_route_kernel(
 // grid (ceil(HW / 32), B): a 32-pixel tile of dY for all E experts, as fp32,
 // in shared memory (dY read from HBM once); warp per input channel, lane per
 // pixel, the channel's transposed list gathered in list order as in
-// bwd_dx_kernel.
+// bwd_dx_kernel.  Each chunk of 32 list entries is staged as (row offset,
+// weight) pairs in a buffer of the warp after dY, and read two entries per
+// 16-byte broadcast load (one shared load per entry for the dY value, where
+// two shuffles per entry were needed before).
 constexpr int kDxThreads = 1024;          // 32 warps (56 registers a thread): more channel rows in flight
+constexpr int kDxCwStride = 17;           // float4 per warp: 32 entries and a 16-byte skew
 template <typename T>
 __global__ void __launch_bounds__(kDxThreads, 1) bwd_px_dx_kernel(
     const T* __restrict__ dy, int C, int HW, int E_r, int k, const int32_t* __restrict__ mask,
@@ -388,6 +392,7 @@ __global__ void __launch_bounds__(kDxThreads, 1) bwd_px_dx_kernel(
   const int b = blockIdx.y, p0 = blockIdx.x * 32;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = E_r + 1;
+  float4* cw = reinterpret_cast<float4*>(s_raw + (size_t)E * 32 * 4) + (size_t)warp * kDxCwStride;
   const T* dyb = dy + (size_t)b * E * HW;
   for (int q = threadIdx.x; q < E * 32; q += kDxThreads) {
     const int p = p0 + (q & 31);
@@ -431,11 +436,14 @@ __global__ void __launch_bounds__(kDxThreads, 1) bwd_px_dx_kernel(
       sc2 = (c2 < C) ? toff[c2] : 0;
     }
     if (c2 < C) fetch(c2, sc2, e_n, a_n, g_n);
-    for (int j = 0; j < n; ++j) {
-      const int e = __shfl_sync(kFull, e_l, j);
-      const float a = __shfl_sync(kFull, a_l, j);
-      acc = fmaf(a, s_dy[e * 32 + lane], acc);
+    reinterpret_cast<float2*>(cw)[lane] = make_float2(__int_as_float(e_l * 32), a_l);
+    __syncwarp();
+    for (int j2 = 0; 2 * j2 < n; ++j2) {
+      const float4 v = cw[j2];                                // entries 2 j2 and 2 j2 + 1
+      acc = fmaf(v.y, s_dy[__float_as_int(v.x) + lane], acc);
+      if (2 * j2 + 1 < n) acc = fmaf(v.w, s_dy[__float_as_int(v.z) + lane], acc);
     }
+    __syncwarp();                                             // read before the next chunk's writes
     if (c2 == c) {
       sc = sc2;
       continue;
@@ -625,7 +633,7 @@ static int backward_run(const void* x, const void* dy, int dtype, int64_t B, int
     }
     int r = check_launch("moce_backward/route");
     if (r) return r;
-    const size_t smem_dx = (size_t)(E_r + 1) * 32 * 4;
+    const size_t smem_dx = (size_t)(E_r + 1) * 32 * 4 + (size_t)(kDxThreads / 32) * kDxCwStride * 16;
     if (smem_dx <= (size_t)smem_max) {
       if (cudaFuncSetAttribute(bwd_px_dx_kernel<Tt>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_dx) !=
           cudaSuccess)
