@@ -30,8 +30,13 @@
 // moce_tc_wait_limit_ns) sets g_tc_fault, the roles leave their loops
 // together, the copies and MMAs already in flight complete (waits bounded by
 // kOwnWaitNs), and the kernel returns after releasing its tensor memory.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <atomic>
+#include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -169,6 +174,10 @@ enum TcDrain {
                                   // 16 bytes (conflict-free), one bulk copy per row, `nsb` buffers
   kDrainDirect = 2,               // 16-byte stores from registers straight to Y (when staging does not fit)
   kDrainRowsLegacy = 3,           // other pixel tiles: 16-bit stores into rows of NP elements
+  kDrainTma = 4,                  // pixel tiles of a multiple of 64 pixels, 16-byte aligned rows: 64-pixel
+                                  // column blocks staged in the 128-byte swizzled layout, each written by
+                                  // one TMA tensor store of up to 128 rows (Y as [B][E_r][H*W], so the
+                                  // residual row is outside the map)
 };
 
 constexpr int kMaxSlots = 8;
@@ -275,6 +284,16 @@ __device__ __forceinline__ void bulk_wait_read_all_but1() {
 }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// TMA store of one box of the tensor map from shared memory (box start at
+// pixel x, expert y, sample z); the caller commits the bulk group
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
 // Named barrier over the 128 threads of one role that also ANDs a flag, so
 // that every thread of the role takes the same branch after a bounded wait.
 __device__ __forceinline__ bool role_sync_and(int id, int nthreads, bool ok) {
@@ -369,7 +388,7 @@ constexpr int kWarpIssuer0 = 12, kWarpProducer = 14;
 // each taking one half of a tile's 32-column chunks: the drain of a
 // 128 x 256 tile, not the MMAs, sets the pace of these maps.
 template <typename T, int KMAX, bool kGen, bool kEp, bool kW1, bool kTin>
-__global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
+__global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a, const __grid_constant__ CUtensorMap tmap_y) {
   constexpr int WT = kW1 ? 128 : kWeightThreads;              // weight threads
   constexpr int DT = kW1 ? 256 : kDrainThreads;               // drain threads
   extern __shared__ unsigned char s_dyn[];
@@ -792,19 +811,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
           role_sync(kBarDrain, DT);
         }
       }
-    } else if (drain == kDrainRows) {
-      // Pixel tiles of 16-byte aligned rows: each thread stages its row with
-      // 16-byte stores into rows 2 NP + 16 bytes apart (the 16-byte skew puts
-      // the 32 rows of a warp's store in distinct bank quads), then copies it
-      // out with one bulk copy; `nsb` buffers alternate.  (Warp-coalesced row
-      // stores in place of the bulk copies measured 249 against 228 us at
-      // 56x56, C=64.)
+    } else if (drain == kDrainRows || drain == kDrainTma) {
+      // Pixel tiles of 16-byte aligned rows; `nsb` staging buffers alternate.
+      // kDrainRows: each thread stages its row with 16-byte stores into rows
+      // 2 NP + 16 bytes apart (the 16-byte skew puts the 32 rows of a warp's
+      // store in distinct bank quads), then copies it out with one bulk copy.
+      // (Warp-coalesced row stores in place of the bulk copies measured 249
+      // against 228 us at 56x56, C=64.)
+      // kDrainTma: the tile is staged as 64-pixel column blocks of 128 rows x
+      // 128 bytes in the 128-byte swizzled layout (16-byte unit j of row r at
+      // r * 128 + ((j ^ (r & 7)) << 4): a warp's 32 rows fill the banks once
+      // per 8 rows), and one thread writes each block with one TMA tensor
+      // store; 128 row copies per tile took the drain's time at 56x56.
+      const bool tma = drain == kDrainTma;
       const uint32_t pitch = (uint32_t)a.stg_pitch;
       unsigned char* row0 = reinterpret_cast<unsigned char*>(stg) + (size_t)dt * pitch;
       for (int u = 0; u < nu; ++u) {
         const int s = u & 1, ug = u0 + u, i = ug / NT - b0, t = ug - (ug / NT) * NT;
         const int p0 = t * NP, tp = min(NP, HW - p0);       // a multiple of 8
         unsigned char* row = row0 + (size_t)(u % a.nsb) * 128u * pitch;
+        unsigned char* blk = reinterpret_cast<unsigned char*>(stg) + (size_t)(u % a.nsb) * (size_t)NP * 256u;
         bool ok = true;
         if (dlead) ok = wait_peer(&bars->d_full[s], (u >> 1) & 1, kSiteDFull, u);
         // this thread's copy out of this buffer, nsb units ago, has read it
@@ -824,12 +850,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
 #pragma unroll
               for (int p = 0; p < 32; ++p) v[p] = apply_epilogue(v[p], esc, esh, erelu);
             }
+            uint4 q[4];
 #pragma unroll
             for (int g = 0; g < 4; ++g)
-              if (cb + 8 * g < tp)
-                *reinterpret_cast<uint4*>(row + (size_t)(cb + 8 * g) * 2) =
-                    make_uint4(pack2_16<T>(v[8 * g], v[8 * g + 1]), pack2_16<T>(v[8 * g + 2], v[8 * g + 3]),
-                               pack2_16<T>(v[8 * g + 4], v[8 * g + 5]), pack2_16<T>(v[8 * g + 6], v[8 * g + 7]));
+              q[g] = make_uint4(pack2_16<T>(v[8 * g], v[8 * g + 1]), pack2_16<T>(v[8 * g + 2], v[8 * g + 3]),
+                                pack2_16<T>(v[8 * g + 4], v[8 * g + 5]), pack2_16<T>(v[8 * g + 6], v[8 * g + 7]));
+            if (tma) {
+              // the chunk lies in one 64-pixel block (32-column chunks start
+              // on 32-column boundaries)
+              unsigned char* b = blk + (size_t)(cb >> 6) * 16384u + (size_t)dt * 128u;
+              const int j0 = (cb & 63) >> 3;
+#pragma unroll
+              for (int g = 0; g < 4; ++g)
+                if (cb + 8 * g < tp) *reinterpret_cast<uint4*>(b + (size_t)(((j0 + g) ^ (dt & 7)) << 4)) = q[g];
+            } else {
+#pragma unroll
+              for (int g = 0; g < 4; ++g)
+                if (cb + 8 * g < tp) *reinterpret_cast<uint4*>(row + (size_t)(cb + 8 * g) * 2) = q[g];
+            }
           }
         };
         // this thread's columns: the whole tile, or (kW1) one half of its
@@ -882,7 +920,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a) {
             put(r0, r1, cb);
           }
         }
-        if (has_row && c_hi > c_lo) {
+        if (tma) {
+          // every row's blocks written (and visible to the async proxy), then
+          // one store per 64-pixel block; pixels past H*W and experts past
+          // E_r are outside the map and are not written
+          proxy_fence_smem();
+          role_sync(kBarDrain, DT);
+          if (dlead) {
+            for (int at = 0; at * 64 < tp; ++at)
+              tma_store_3d(&tmap_y, smem_u32(blk) + (uint32_t)at * 16384u, p0 + 64 * at, e0, b0 + i);
+            bulk_commit();
+          }
+        } else if (has_row && c_hi > c_lo) {
           proxy_fence_smem();
           bulk_s2g(yg + ((size_t)(b0 + i) * E + e0 + dt) * HW + p0 + c_lo, smem_u32(row + (size_t)c_lo * 2),
                    (uint32_t)(c_hi - c_lo) * (uint32_t)sizeof(T));
@@ -1009,6 +1058,23 @@ void tc_tiling(int64_t HW, int np_max, int* NP, int* NT, int* NA) {
 
 int smem_optin_tc();
 
+// The driver's tensor-map encoder, looked up once through the runtime (no
+// link against the driver library); null when the driver does not offer it.
+PFN_cuTensorMapEncodeTiled_v12000 tma_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
 // The kernel's shape for (C, H*W, k) and a Y that is (or is not) 16-byte
 // aligned: tiling, accumulators, output path and shared-memory plan.
 // ns == 0 when the shape does not fit shared memory.
@@ -1043,11 +1109,16 @@ TcShape tc_shape(int64_t C, int64_t HW, int64_t k, bool y_aligned, int np_max) {
     // one tile: the block is the tile's rows, H*W apart
     pick(kDrainOneTile, (int)HW, 1, (size_t)128 * HW * 2);
   } else if (HW % 8 == 0 && y_aligned) {
-    // rows of 16-byte aligned segments: padded staging rows, two buffers if
-    // three ring slots still fit, else one with two slots, else no staging
+    // rows of 16-byte aligned segments: 64-pixel column blocks for TMA stores
+    // when the tile is a multiple of 64 pixels, else padded staging rows; two
+    // buffers if three ring slots still fit, else one with two slots, else
+    // no staging
     const int pitch = 2 * t.NP + 16;
-    const size_t one = (size_t)128 * pitch;
-    if (slots(2 * one) >= 3) pick(kDrainRows, pitch, 2, 2 * one);
+    const size_t one = (size_t)128 * pitch, blocks = (size_t)t.NP * 256;
+    const bool tma = t.NP % 64 == 0 && tma_encode_fn() != nullptr;
+    if (tma && slots(2 * blocks) >= 3) pick(kDrainTma, pitch, 2, 2 * blocks);
+    else if (tma && slots(blocks) >= 2) pick(kDrainTma, pitch, 1, blocks);
+    else if (slots(2 * one) >= 3) pick(kDrainRows, pitch, 2, 2 * one);
     else if (slots(one) >= 2) pick(kDrainRows, pitch, 1, one);
     else pick(kDrainDirect, 0, 0, 0);
   } else {
@@ -1240,6 +1311,21 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
   TcArgs a{xstage, y, gate.z, idx, ln, gate.gate_w, gate.gate_b, gate.T_out, gate.tmin_tau, gate.trange_tau, gate.T_in,
            (int)B, (int)C, (int)HW, (int)E_r, (int)k, Kp, n_tiles, n_bsplit, ns, sh.NP, sh.NA, sh.P, sh.NT,
            sh.tmem_cols, (unsigned long long)g_wait_ns.load(), sh.drain, sh.stg_pitch, sh.nsb, sh.stage_bytes, ep};
+  // kDrainTma: Y as [B][E_r][H*W] (the residual row E_r lies outside), boxes
+  // of 64 pixels x 128 experts x 1 sample in the 128-byte swizzled layout
+  CUtensorMap tmap;
+  memset(&tmap, 0, sizeof(tmap));
+  if (sh.drain == kDrainTma) {
+    const cuuint64_t dims[3] = {(cuuint64_t)HW, (cuuint64_t)E_r, (cuuint64_t)B};
+    const cuuint64_t strides[2] = {(cuuint64_t)HW * 2, (cuuint64_t)(E_r + 1) * (cuuint64_t)HW * 2};
+    const cuuint32_t box[3] = {64, (cuuint32_t)std::min<int64_t>(128, E_r), 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = tma_encode_fn()(
+        &tmap, dtype == MOCE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, y, dims,
+        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    MOCE_REQUIRE(r == CUDA_SUCCESS, MOCE_ERR_CUDA, "moce_mix_tc: cannot encode the output tensor map (%d)", (int)r);
+  }
   return dispatch_dtype(dtype, [&](auto tag) {
     using T = decltype(tag);
     if constexpr (sizeof(T) != 2) {
@@ -1254,8 +1340,8 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
       // thread per row and eight drain warps (with one tile per sample the
       // weights are rewritten every unit and the split measured slower:
       // 74.7 against 68.6 us at 14x14)
-      const bool w1 = gen && sh.drain == kDrainRows && KMAX == 16;
-      void (*kern)(TcArgs) = nullptr;
+      const bool w1 = gen && (sh.drain == kDrainRows || sh.drain == kDrainTma) && KMAX == 16;
+      void (*kern)(TcArgs, CUtensorMap) = nullptr;
       if (tin) {
         kern = w1 ? mix_tc_kernel<T, 16, true, false, true, true>
                   : gen ? MOCE_TC_KMAX(true, false, true) : MOCE_TC_KMAX(false, false, true);
@@ -1277,7 +1363,7 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
       attr[0].val.programmaticStreamSerializationAllowed = 1;
       cfg.attrs = attr;
       cfg.numAttrs = dependent ? 1 : 0;
-      if (cudaLaunchKernelEx(&cfg, kern, a) != cudaSuccess) return check_launch("mix_tc_kernel");
+      if (cudaLaunchKernelEx(&cfg, kern, a, tmap) != cudaSuccess) return check_launch("mix_tc_kernel");
       return check_launch("mix_tc_kernel");
     }
   });
