@@ -388,7 +388,8 @@ constexpr int kWarpIssuer0 = 12, kWarpProducer = 14;
 // each taking one half of a tile's 32-column chunks: the drain of a
 // 128 x 256 tile, not the MMAs, sets the pace of these maps.
 template <typename T, int KMAX, bool kGen, bool kEp, bool kW1, bool kTin>
-__global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a, const __grid_constant__ CUtensorMap tmap_y) {
+__global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a, const __grid_constant__ CUtensorMap tmap_y,
+                                                          const __grid_constant__ CUtensorMap tmap_r) {
   constexpr int WT = kW1 ? 128 : kWeightThreads;              // weight threads
   constexpr int DT = kW1 ? 256 : kDrainThreads;               // drain threads
   extern __shared__ unsigned char s_dyn[];
@@ -855,7 +856,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a, const _
             for (int g = 0; g < 4; ++g)
               q[g] = make_uint4(pack2_16<T>(v[8 * g], v[8 * g + 1]), pack2_16<T>(v[8 * g + 2], v[8 * g + 3]),
                                 pack2_16<T>(v[8 * g + 4], v[8 * g + 5]), pack2_16<T>(v[8 * g + 6], v[8 * g + 7]));
-            if (tma) {
+            if (tma && (cb >> 6) < (NP >> 6)) {
               // the chunk lies in one 64-pixel block (32-column chunks start
               // on 32-column boundaries)
               unsigned char* b = blk + (size_t)(cb >> 6) * 16384u + (size_t)dt * 128u;
@@ -863,6 +864,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a, const _
 #pragma unroll
               for (int g = 0; g < 4; ++g)
                 if (cb + 8 * g < tp) *reinterpret_cast<uint4*>(b + (size_t)(((j0 + g) ^ (dt & 7)) << 4)) = q[g];
+            } else if (tma) {
+              // the tile's last NP % 64 pixels: rows of (NP % 64) * 2 bytes,
+              // unswizzled, after the full blocks
+              const int full = NP >> 6, rb = (NP & 63) * 2;
+              unsigned char* b = blk + (size_t)full * 16384u + (size_t)dt * rb + (size_t)(cb - 64 * full) * 2;
+#pragma unroll
+              for (int g = 0; g < 4; ++g)
+                if (cb + 8 * g < tp) *reinterpret_cast<uint4*>(b + 16 * g) = q[g];
             } else {
 #pragma unroll
               for (int g = 0; g < 4; ++g)
@@ -927,8 +936,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) mix_tc_kernel(TcArgs a, const _
           proxy_fence_smem();
           role_sync(kBarDrain, DT);
           if (dlead) {
-            for (int at = 0; at * 64 < tp; ++at)
+            const int full = NP >> 6;
+            for (int at = 0; at < full && at * 64 < tp; ++at)
               tma_store_3d(&tmap_y, smem_u32(blk) + (uint32_t)at * 16384u, p0 + 64 * at, e0, b0 + i);
+            if ((NP & 63) && 64 * full < tp)
+              tma_store_3d(&tmap_r, smem_u32(blk) + (uint32_t)full * 16384u, p0 + 64 * full, e0, b0 + i);
             bulk_commit();
           }
         } else if (has_row && c_hi > c_lo) {
@@ -1109,13 +1121,14 @@ TcShape tc_shape(int64_t C, int64_t HW, int64_t k, bool y_aligned, int np_max) {
     // one tile: the block is the tile's rows, H*W apart
     pick(kDrainOneTile, (int)HW, 1, (size_t)128 * HW * 2);
   } else if (HW % 8 == 0 && y_aligned) {
-    // rows of 16-byte aligned segments: 64-pixel column blocks for TMA stores
-    // when the tile is a multiple of 64 pixels, else padded staging rows; two
+    // rows of 16-byte aligned segments: 64-pixel column blocks (and the
+    // tile's remaining NP % 64 pixels) for TMA stores, else padded staging
+    // rows; two
     // buffers if three ring slots still fit, else one with two slots, else
     // no staging
     const int pitch = 2 * t.NP + 16;
     const size_t one = (size_t)128 * pitch, blocks = (size_t)t.NP * 256;
-    const bool tma = t.NP % 64 == 0 && tma_encode_fn() != nullptr;
+    const bool tma = tma_encode_fn() != nullptr;
     if (tma && slots(2 * blocks) >= 3) pick(kDrainTma, pitch, 2, 2 * blocks);
     else if (tma && slots(blocks) >= 2) pick(kDrainTma, pitch, 1, blocks);
     else if (slots(2 * one) >= 3) pick(kDrainRows, pitch, 2, 2 * one);
@@ -1313,17 +1326,25 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
            sh.tmem_cols, (unsigned long long)g_wait_ns.load(), sh.drain, sh.stg_pitch, sh.nsb, sh.stage_bytes, ep};
   // kDrainTma: Y as [B][E_r][H*W] (the residual row E_r lies outside), boxes
   // of 64 pixels x 128 experts x 1 sample in the 128-byte swizzled layout
-  CUtensorMap tmap;
+  // (tmap_r: the same with boxes of the tile's last NP % 64 pixels, unswizzled)
+  CUtensorMap tmap, tmap_r;
   memset(&tmap, 0, sizeof(tmap));
+  memset(&tmap_r, 0, sizeof(tmap_r));
   if (sh.drain == kDrainTma) {
     const cuuint64_t dims[3] = {(cuuint64_t)HW, (cuuint64_t)E_r, (cuuint64_t)B};
     const cuuint64_t strides[2] = {(cuuint64_t)HW * 2, (cuuint64_t)(E_r + 1) * (cuuint64_t)HW * 2};
-    const cuuint32_t box[3] = {64, (cuuint32_t)std::min<int64_t>(128, E_r), 1};
+    const cuuint32_t rows = (cuuint32_t)std::min<int64_t>(128, E_r);
     const cuuint32_t estr[3] = {1, 1, 1};
-    const CUresult r = tma_encode_fn()(
-        &tmap, dtype == MOCE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, y, dims,
-        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUtensorMapDataType dt = dtype == MOCE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const cuuint32_t box[3] = {64, rows, 1};
+    CUresult r = tma_encode_fn()(&tmap, dt, 3, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r == CUDA_SUCCESS && (sh.NP & 63)) {
+      const cuuint32_t box_r[3] = {(cuuint32_t)(sh.NP & 63), rows, 1};
+      r = tma_encode_fn()(&tmap_r, dt, 3, y, dims, strides, box_r, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
     MOCE_REQUIRE(r == CUDA_SUCCESS, MOCE_ERR_CUDA, "moce_mix_tc: cannot encode the output tensor map (%d)", (int)r);
   }
   return dispatch_dtype(dtype, [&](auto tag) {
@@ -1341,7 +1362,7 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
       // weights are rewritten every unit and the split measured slower:
       // 74.7 against 68.6 us at 14x14)
       const bool w1 = gen && (sh.drain == kDrainRows || sh.drain == kDrainTma) && KMAX == 16;
-      void (*kern)(TcArgs, CUtensorMap) = nullptr;
+      void (*kern)(TcArgs, CUtensorMap, CUtensorMap) = nullptr;
       if (tin) {
         kern = w1 ? mix_tc_kernel<T, 16, true, false, true, true>
                   : gen ? MOCE_TC_KMAX(true, false, true) : MOCE_TC_KMAX(false, false, true);
@@ -1363,7 +1384,7 @@ static int mix_tc_launch(const void* xstage, int dtype, int64_t B, int64_t C, in
       attr[0].val.programmaticStreamSerializationAllowed = 1;
       cfg.attrs = attr;
       cfg.numAttrs = dependent ? 1 : 0;
-      if (cudaLaunchKernelEx(&cfg, kern, a, tmap) != cudaSuccess) return check_launch("mix_tc_kernel");
+      if (cudaLaunchKernelEx(&cfg, kern, a, tmap, tmap_r) != cudaSuccess) return check_launch("mix_tc_kernel");
       return check_launch("mix_tc_kernel");
     }
   });
